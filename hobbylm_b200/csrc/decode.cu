@@ -1,0 +1,800 @@
+// Decode-step kernels (Model::forward, hobby-rs/src/model.rs:152-327) for T tokens of T sequences.
+//
+// Per layer: pre_norm (residual update + RMSNorm + activation quantization) -> QKV Q8 matvec ->
+// paged split-K attention with fused QK-norm/RoPE/append and in-kernel combine (writes the
+// quantized attention output) -> output projection with the residual add fused -> ffn RMSNorm +
+// router + top-k -> gate/up SwiGLU over active experts -> down projection. The MoE combine of a
+// layer is folded into the next layer's pre_norm. Finally output norm + lm_head + greedy argmax.
+//
+// Arithmetic: the Q8 matvec (quant.rs:44-67, 106-136), the activation quantization (quant.rs:
+// 112-123), the router dot (ops.rs:7-36), sigmoid/silu (ops.rs:75-82, exp pinned to
+// (float)exp((double)x)), top-k (model.rs:282-293) and the rank-order combine (model.rs:300-323)
+// reproduce the reference bit for bit given the same inputs. RMSNorm / QK-norm sums and the
+// attention softmax / value sums are parallel reductions (tolerance, not bit-exact).
+#include <cfloat>
+
+#include "hg_model.cuh"
+
+namespace hg {
+
+// ------------------------------------------------------------------------------------------
+// Block reductions
+// ------------------------------------------------------------------------------------------
+__device__ inline float block_sum(float v, float* red) {
+  int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.0f;
+  if (w == 0) {
+    s = lane < nw ? red[lane] : 0.0f;
+    s = warp_sum(s);
+    if (lane == 0) red[0] = s;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+// ------------------------------------------------------------------------------------------
+// pre_norm: residual update, RMSNorm (ops.rs:85-95 with a tree sum), quantization of the result.
+// mode 0: x = token embedding; 1: x += y[t][0] (dense FFN); 2: x += MoE combine (model.rs:300-323,
+// rank order then the shared expert); 3: x unchanged.
+// ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_pre_norm(Dims D, DecodeBufs B, int mode, const float* __restrict__ embd,
+                                                  const float* __restrict__ norm_w, int8_t* q_out, float* s_out,
+                                                  float* h_out, int reset_moe, int reset_amax) {
+  extern __shared__ float xs[];
+  __shared__ float red[32];
+  const int t = blockIdx.x, d = D.d;
+  float* x = B.x + (size_t)t * d;
+  if (mode == 0) {
+    int tok = B.tok[t];
+    if (tok < 0 || tok >= D.vocab) {
+      if (threadIdx.x == 0) atomicExch(B.err, HG_ERR_TOKEN);
+      tok = 0;
+    }
+    const float* e = embd + (size_t)tok * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) xs[i] = e[i];
+  } else if (mode == 1) {
+    const float* y = B.y + (size_t)t * (D.k + 1) * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) xs[i] = fadd(x[i], y[i]);
+  } else if (mode == 2) {
+    const float* y = B.y + (size_t)t * (D.k + 1) * d;
+    float sc[MAX_TOPK];
+    for (int r = 0; r < D.k; r++) sc[r] = fmul(B.selw[t * D.k + r], D.wscale);
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+      float o = 0.0f;
+      for (int r = 0; r < D.k; r++) o = fadd(o, fmul(sc[r], y[r * d + i]));
+      if (D.nsh > 0) o = fadd(o, y[D.k * d + i]);
+      xs[i] = fadd(x[i], o);
+    }
+  } else {
+    for (int i = threadIdx.x; i < d; i += blockDim.x) xs[i] = x[i];
+  }
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    if (mode != 3) x[i] = xs[i];
+    ss += fmul(xs[i], xs[i]);
+  }
+  ss = block_sum(ss, red);
+  float scale = __fdiv_rn(1.0f, __fsqrt_rn(fadd(__fdiv_rn(ss, (float)d), D.eps)));
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    float h = fmul(fmul(xs[i], scale), norm_w[i]);
+    xs[i] = h;
+    if (h_out) h_out[(size_t)t * d + i] = h;
+  }
+  __syncthreads();
+  quant_row_block(xs, d, q_out + (size_t)t * d, s_out + (size_t)t * q8_ss(d >> 5));
+  if (reset_moe && t == 0)
+    for (int i = threadIdx.x; i < D.ne + 2; i += blockDim.x) B.ecount[i] = 0;
+  if (reset_amax && threadIdx.x == 0) B.amax[t] = 0ull;
+}
+
+// ------------------------------------------------------------------------------------------
+// Q8 matvec over the step's tokens. ROWS rows x 8 lanes per CTA; activations of up to TT tokens
+// are staged in shared memory. NB = blocks per row (0: runtime).
+// ------------------------------------------------------------------------------------------
+template <int NB>
+struct Frag {
+  static constexpr int NC = NB / 4, NT = NB % 4;
+  int4 w[NC > 0 ? NC : 1];
+  float4 s[NC > 0 ? NC : 1];
+  int wt[NT > 0 ? NT : 1];
+  float st[NT > 0 ? NT : 1];
+  __device__ __forceinline__ void load(const int8_t* __restrict__ wq, const float* __restrict__ ws, int lane) {
+#pragma unroll
+    for (int c = 0; c < NC; c++) {
+      w[c] = __ldg(reinterpret_cast<const int4*>(wq + c * 128 + lane * 16));
+      s[c] = __ldg(reinterpret_cast<const float4*>(ws + c * 4));
+    }
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+      wt[t] = __ldg(reinterpret_cast<const int*>(wq + NC * 128 + t * 32 + lane * 4));
+      st[t] = __ldg(ws + NC * 4 + t);
+    }
+  }
+  __device__ __forceinline__ float dot(const int8_t* aq, const float* as, int lane) const {
+    float acc = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NC; c++) {
+      int4 a = *reinterpret_cast<const int4*>(aq + c * 128 + lane * 16);
+      float4 d = *reinterpret_cast<const float4*>(as + c * 4);
+      acc = __fmaf_rn(fmul(s[c].x, d.x), (float)__dp4a(w[c].x, a.x, 0), acc);
+      acc = __fmaf_rn(fmul(s[c].y, d.y), (float)__dp4a(w[c].y, a.y, 0), acc);
+      acc = __fmaf_rn(fmul(s[c].z, d.z), (float)__dp4a(w[c].z, a.z, 0), acc);
+      acc = __fmaf_rn(fmul(s[c].w, d.w), (float)__dp4a(w[c].w, a.w, 0), acc);
+    }
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+      int a = *reinterpret_cast<const int*>(aq + NC * 128 + t * 32 + lane * 4);
+      acc = __fmaf_rn(fmul(st[t], as[NC * 4 + t]), (float)__dp4a(wt[t], a, 0), acc);
+    }
+    return acc;
+  }
+};
+
+// Weight row of one (row, lane) thread, dotted with staged activations. Rows with NB <= 24 keep
+// their words in registers across tokens; longer rows re-read them (L1) per token.
+template <int NB>
+struct RowDot {
+  static constexpr bool REG = (NB > 0 && NB <= 24);
+  Frag<REG ? NB : 4> f;
+  const int8_t* wq;
+  const float* ws;
+  int nb;
+  __device__ __forceinline__ void init(const int8_t* q, const float* s, int lane, int nb_) {
+    wq = q;
+    ws = s;
+    nb = nb_;
+    if constexpr (REG) f.load(q, s, lane);
+  }
+  __device__ __forceinline__ float dot(const int8_t* aq, const float* as, int lane) const {
+    if constexpr (REG) return f.dot(aq, as, lane);
+    else if constexpr (NB > 0) return q8_lane_dot<NB>(wq, ws, aq, as, lane);
+    else return q8_lane_dot_rt(wq, ws, aq, as, lane, nb);
+  }
+};
+
+// Copy n activation rows (cols bytes + ss floats each, contiguous per row in global) into smem.
+__device__ inline void stage_rows(int8_t* aq_s, float* as_s, const int8_t* q, const float* s, const int* rows_idx,
+                                  int n, int cols, int ss, long long qstride, long long sstride) {
+  int vq = cols >> 4;  // int4 per row
+  for (int i = threadIdx.x; i < n * vq; i += blockDim.x) {
+    int r = i / vq, c = i - r * vq;
+    long long src = rows_idx ? rows_idx[r] : r;
+    reinterpret_cast<int4*>(aq_s + (size_t)r * cols)[c] = reinterpret_cast<const int4*>(q + src * qstride)[c];
+  }
+  for (int i = threadIdx.x; i < n * ss; i += blockDim.x) {
+    int r = i / ss, c = i - r * ss;
+    long long src = rows_idx ? rows_idx[r] : r;
+    as_s[(size_t)r * ss + c] = s[src * sstride + c];
+  }
+}
+
+enum { EPI_STORE = 0, EPI_RESID = 1, EPI_LMHEAD = 2 };
+
+// Rows of one matrix against all T tokens' activations (aq/as rows t, strides cols / ss).
+template <int NB, int ROWS, int TT, int EPI>
+__global__ void __launch_bounds__(ROWS * 8) k_mv_tokens(Dims D, DecodeBufs B, Q8M W, const int8_t* __restrict__ aq,
+                                                         const float* __restrict__ as, float* out, int ostride) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int cols = W.cols, nb = cols >> 5, ss = W.ss;
+  int8_t* aq_s = reinterpret_cast<int8_t*>(smem);
+  float* as_s = reinterpret_cast<float*>(smem + (size_t)TT * cols);
+  const int lane = threadIdx.x & 7, rl = threadIdx.x >> 3;
+  const int row = blockIdx.x * ROWS + rl;
+  const bool valid_row = row < W.rows;
+  RowDot<NB> rd;
+  rd.init(W.row_q(0, valid_row ? row : 0), W.row_s(0, valid_row ? row : 0), lane, nb);
+  __shared__ unsigned long long best_s[TT > 0 ? TT : 1];
+  for (int t0 = 0; t0 < B.T; t0 += TT) {
+    int n = min(TT, B.T - t0);
+    __syncthreads();
+    stage_rows(aq_s, as_s, aq + (size_t)t0 * cols, as + (size_t)t0 * ss, nullptr, n, cols, ss, cols, ss);
+    if (EPI == EPI_LMHEAD && threadIdx.x < TT) best_s[threadIdx.x] = 0ull;
+    __syncthreads();
+#pragma unroll 1
+    for (int i = 0; i < n; i++) {
+      float v = hsum8_group(rd.dot(aq_s + (size_t)i * cols, as_s + (size_t)i * ss, lane));
+      int t = t0 + i;
+      if (EPI == EPI_STORE) {
+        if (lane == 0 && valid_row) out[(size_t)t * ostride + row] = v;
+      } else if (EPI == EPI_RESID) {
+        if (lane == 0 && valid_row) {
+          float* xp = B.x + (size_t)t * D.d + row;
+          *xp = fadd(*xp, v);
+        }
+      } else {
+        if (lane == 0 && valid_row && out) out[(size_t)t * ostride + row] = v;
+        unsigned long long key = (valid_row && row < D.valid) ? argmax_key(v, (uint32_t)row) : 0ull;
+        key = max(key, __shfl_xor_sync(0xffffffffu, key, 8));
+        key = max(key, __shfl_xor_sync(0xffffffffu, key, 16));
+        if ((threadIdx.x & 31) == 0) atomicMax(&best_s[i], key);
+      }
+    }
+    if (EPI == EPI_LMHEAD) {
+      __syncthreads();
+      if (threadIdx.x < n) atomicMax(&B.amax[t0 + threadIdx.x], best_s[threadIdx.x]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Router (model.rs:270-293): ffn RMSNorm, quantized copy for the experts, f32 router logits in
+// the ops::dot order, sigmoid, selection score + bias, top-k by descending score (ties by lower
+// id), gate weights = raw scores (optionally renormalized), expert token lists.
+// ------------------------------------------------------------------------------------------
+// prenormed != 0: B.h2 already holds the normed hidden state (op-level MoE entry point).
+__global__ void __launch_bounds__(256) k_route(Dims D, DecodeBufs B, LayerDev Ld, int layer, int prenormed) {
+  extern __shared__ float hs[];  // d floats
+  __shared__ float red[32];
+  __shared__ float logit_s[128], score_s[128], selsc_s[128];
+  __shared__ int rank_e[MAX_TOPK];
+  const int t = blockIdx.x, d = D.d;
+  if (prenormed) {
+    for (int i = threadIdx.x; i < d; i += blockDim.x) hs[i] = B.h2[(size_t)t * d + i];
+  } else {
+    const float* x = B.x + (size_t)t * d;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+      float v = x[i];
+      hs[i] = v;
+      ss += fmul(v, v);
+    }
+    ss = block_sum(ss, red);
+    float scale = __fdiv_rn(1.0f, __fsqrt_rn(fadd(__fdiv_rn(ss, (float)d), D.eps)));
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+      float h = fmul(fmul(hs[i], scale), Ld.ffn_norm[i]);
+      hs[i] = h;
+      B.h2[(size_t)t * d + i] = h;
+    }
+  }
+  __syncthreads();
+  quant_row_block(hs, d, B.qh + (size_t)t * d, B.sh + (size_t)t * q8_ss(d >> 5));
+  if (!Ld.moe) return;
+  const int ne = D.ne, k = D.k, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int e = warp; e < ne; e += nw) {
+    float lg = dot_ref_warp(Ld.router + (size_t)e * d, hs, d);
+    if ((threadIdx.x & 31) == 0) logit_s[e] = lg;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !D.gsig) {  // softmax gating (ops.rs:112-128), sequential
+    float m = -INFINITY;
+    for (int e = 0; e < ne; e++) m = logit_s[e] > m ? logit_s[e] : m;
+    float sum = 0.0f;
+    for (int e = 0; e < ne; e++) {
+      score_s[e] = exp_cr(logit_s[e] - m);
+      sum = fadd(sum, score_s[e]);
+    }
+    float inv = __fdiv_rn(1.0f, sum);
+    for (int e = 0; e < ne; e++) score_s[e] = fmul(score_s[e], inv);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < ne; e += blockDim.x) {
+    float sc = D.gsig ? sigmoid_ref(logit_s[e]) : score_s[e];
+    score_s[e] = sc;
+    selsc_s[e] = fadd(sc, Ld.bias[e]);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < ne; e += blockDim.x) {
+    float v = selsc_s[e];
+    int r = 0;
+    for (int j = 0; j < ne; j++) {
+      float u = selsc_s[j];
+      r += (u > v) || (u == v && j < e);
+    }
+    if (r < k) rank_e[r] = e;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float w[MAX_TOPK];
+    for (int r = 0; r < k; r++) w[r] = score_s[rank_e[r]];
+    if (D.wnorm) {
+      float s = -0.0f;
+      for (int r = 0; r < k; r++) s = fadd(s, w[r]);
+      s = fadd(s, 1e-9f);
+      for (int r = 0; r < k; r++) w[r] = __fdiv_rn(w[r], s);
+    }
+    for (int r = 0; r < k; r++) {
+      int e = rank_e[r];
+      B.sel[t * k + r] = e;
+      B.selw[t * k + r] = w[r];
+      if (B.dbg_sel) B.dbg_sel[((size_t)layer * B.T + t) * k + r] = e;
+      int slot = atomicAdd(&B.ecount[e], 1);
+      if (slot == 0) B.active[atomicAdd(&B.ecount[ne], 1)] = e;
+      B.elist[(size_t)e * B.T + slot] = t * 32 + r;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// SwiGLU gate/up (model.rs:243-255, 300-305, 313-318): blockIdx.y = slot group (0: shared expert
+// or the dense FFN; 1 + i: i-th active routed expert). Each CTA covers PAIRS rows of gate and the
+// same rows of up (16 lanes per pair) and writes act = silu(g) * u for every token of the group.
+// ------------------------------------------------------------------------------------------
+template <int NB, int PAIRS, int TT>
+__global__ void __launch_bounds__(PAIRS * 16) k_ffn_up(Dims D, DecodeBufs B, LayerDev Ld) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ int ent_s[TT];
+  const int cols = D.d, nb = cols >> 5, ss = q8_ss(nb);
+  const int grp = blockIdx.y;
+  int expert = 0, nent, fdim;
+  if (grp == 0) {
+    if (Ld.moe && D.nsh == 0) return;
+    nent = B.T;
+    fdim = Ld.moe ? D.f : D.df;
+  } else {
+    if (!Ld.moe || grp - 1 >= B.ecount[D.ne]) return;
+    expert = B.active[grp - 1];
+    nent = B.ecount[expert];
+    fdim = D.f;
+  }
+  const int pair0 = blockIdx.x * PAIRS;
+  if (pair0 >= fdim) return;
+  int8_t* aq_s = reinterpret_cast<int8_t*>(smem);
+  float* as_s = reinterpret_cast<float*>(smem + (size_t)TT * cols);
+  const int lane = threadIdx.x & 7, rg = threadIdx.x >> 3, pr = rg >> 1, is_up = rg & 1;
+  const int row = pair0 + pr;
+  const bool valid_row = row < fdim;
+  const Q8M M = grp == 0 ? (Ld.moe ? (is_up ? Ld.sup : Ld.sgate) : (is_up ? Ld.up : Ld.gate))
+                         : (is_up ? Ld.up : Ld.gate);
+  const int mi = grp == 0 ? 0 : expert;
+  RowDot<NB> rd;
+  rd.init(M.row_q(mi, valid_row ? row : 0), M.row_s(mi, valid_row ? row : 0), lane, nb);
+  for (int e0 = 0; e0 < nent; e0 += TT) {
+    int n = min(TT, nent - e0);
+    __syncthreads();
+    if (threadIdx.x < n) {
+      int code = grp == 0 ? (e0 + threadIdx.x) * 32 : B.elist[(size_t)expert * B.T + e0 + threadIdx.x];
+      ent_s[threadIdx.x] = code;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n * (cols >> 4); i += blockDim.x) {
+      int r = i / (cols >> 4), c = i - r * (cols >> 4);
+      int t = ent_s[r] >> 5;
+      reinterpret_cast<int4*>(aq_s + (size_t)r * cols)[c] = reinterpret_cast<const int4*>(B.qh + (size_t)t * cols)[c];
+    }
+    for (int i = threadIdx.x; i < n * ss; i += blockDim.x) {
+      int r = i / ss, c = i - r * ss;
+      int t = ent_s[r] >> 5;
+      as_s[(size_t)r * ss + c] = B.sh[(size_t)t * ss + c];
+    }
+    __syncthreads();
+#pragma unroll 1
+    for (int i = 0; i < n; i++) {
+      float v = hsum8_group(rd.dot(aq_s + (size_t)i * cols, as_s + (size_t)i * ss, lane));
+      float u = __shfl_down_sync(0xffffffffu, v, 8);  // up row value from the neighbouring group
+      if (!is_up && lane == 0 && valid_row) {
+        int code = ent_s[i], t = code >> 5, r = code & 31;
+        int slot = grp == 0 ? (Ld.moe ? D.k : 0) : r;
+        B.act[(size_t)t * B.act_stride + (size_t)slot * fdim + row] = fmul(silu_ref(v), u);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Down projection: blockIdx.y = slot group as in k_ffn_up; the activation row of each (token,
+// slot) is quantized in shared memory (quant.rs:112-123) and dotted with ROWS rows of the down
+// matrix; y[t][slot][row] = result.
+// ------------------------------------------------------------------------------------------
+template <int NB, int ROWS, int TT>
+__global__ void __launch_bounds__(ROWS * 8) k_ffn_down(Dims D, DecodeBufs B, LayerDev Ld) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ int ent_s[TT];
+  const int grp = blockIdx.y;
+  int expert = 0, nent, fdim;
+  if (grp == 0) {
+    if (Ld.moe && D.nsh == 0) return;
+    nent = B.T;
+    fdim = Ld.moe ? D.f : D.df;
+  } else {
+    if (!Ld.moe || grp - 1 >= B.ecount[D.ne]) return;
+    expert = B.active[grp - 1];
+    nent = B.ecount[expert];
+    fdim = D.f;
+  }
+  const Q8M W = (grp == 0 && Ld.moe) ? Ld.sdown : Ld.down;
+  const int cols = fdim, nb = cols >> 5, ss = q8_ss(nb);
+  int8_t* aq_s = reinterpret_cast<int8_t*>(smem);
+  float* as_s = reinterpret_cast<float*>(smem + (size_t)TT * cols);
+  const int lane = threadIdx.x & 7, rl = threadIdx.x >> 3;
+  const int row = blockIdx.x * ROWS + rl;
+  const bool valid_row = row < D.d;
+  const int mi = grp == 0 ? 0 : expert;
+  RowDot<NB> rd;
+  rd.init(W.row_q(mi, valid_row ? row : 0), W.row_s(mi, valid_row ? row : 0), lane, nb);
+  for (int e0 = 0; e0 < nent; e0 += TT) {
+    int n = min(TT, nent - e0);
+    __syncthreads();
+    if (threadIdx.x < n) {
+      int code = grp == 0 ? (e0 + threadIdx.x) * 32 : B.elist[(size_t)expert * B.T + e0 + threadIdx.x];
+      ent_s[threadIdx.x] = code;
+    }
+    __syncthreads();
+    // quantize each entry's activation row: warps take 32-blocks
+    {
+      int warp = threadIdx.x >> 5, wl = threadIdx.x & 31, nw = blockDim.x >> 5;
+      for (int j = warp; j < n * nb; j += nw) {
+        int r = j / nb, b = j - r * nb;
+        int code = ent_s[r], t = code >> 5, rk = code & 31;
+        int slot = grp == 0 ? (Ld.moe ? D.k : 0) : rk;
+        const float* a = B.act + (size_t)t * B.act_stride + (size_t)slot * fdim;
+        float dq;
+        int8_t q = quant_lane(a[b * 32 + wl], &dq);
+        aq_s[(size_t)r * cols + q8_pos(b * 32 + wl, nb)] = q;
+        if (wl == 0) as_s[(size_t)r * ss + b] = dq;
+      }
+    }
+    __syncthreads();
+#pragma unroll 1
+    for (int i = 0; i < n; i++) {
+      float v = hsum8_group(rd.dot(aq_s + (size_t)i * cols, as_s + (size_t)i * ss, lane));
+      if (lane == 0 && valid_row) {
+        int code = ent_s[i], t = code >> 5, rk = code & 31;
+        int slot = grp == 0 ? (Ld.moe ? D.k : 0) : rk;
+        B.y[((size_t)t * (D.k + 1) + slot) * D.d + row] = v;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Attention (model.rs:199-233) over a paged f32 KV pool. Work item = (token, kv head, chunk of
+// ATT_CHUNK positions); 8 warps x 8 positions per item. The item holding the new position
+// QK-norms + ropes k and appends k, v to its page slot. Each item writes an online-softmax
+// partial (max, sum, o[hd]) per q head; the last item of a (token, kv head) to arrive combines
+// the partials, writes o (f32, optional) and its quantized form (optional).
+// ------------------------------------------------------------------------------------------
+
+// per-head RMSNorm (model.rs:753-763, tree sum) + rotate-half RoPE (ops.rs:157-166) of one head
+// vector held by one warp; E = hd/32 elements per lane, lane owns elements lane + 32 j.
+template <int HD>
+__device__ __forceinline__ void norm_rope_warp(const float* src, const float* w, float eps, const float* cs,
+                                               const float* sn, float* dst) {
+  constexpr int E = HD / 32, HALF = HD / 2;
+  int lane = threadIdx.x & 31;
+  float v[E];
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < E; j++) {
+    v[j] = src[lane + 32 * j];
+    ss += fmul(v[j], v[j]);
+  }
+  ss = warp_sum(ss);
+  float scale = __fdiv_rn(1.0f, __fsqrt_rn(fadd(__fdiv_rn(ss, (float)HD), eps)));
+#pragma unroll
+  for (int j = 0; j < E; j++) dst[lane + 32 * j] = fmul(fmul(v[j], scale), w[lane + 32 * j]);
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < E / 2; j++) {
+    int i = lane + 32 * j;  // i < HALF
+    float x1 = dst[i], x2 = dst[i + HALF];
+    float c = cs[i], s = sn[i];
+    __syncwarp();
+    dst[i] = __fsub_rn(fmul(x1, c), fmul(x2, s));
+    dst[i + HALF] = fadd(fmul(x2, c), fmul(x1, s));
+  }
+  __syncwarp();
+}
+
+template <int HD, int REP>
+__global__ void __launch_bounds__(256) k_attn(AttnArgs A) {
+  constexpr int E = HD / 32;  // floats per lane per row
+  __shared__ __align__(16) float q_s[REP][HD];
+  __shared__ __align__(16) float knew_s[HD], vnew_s[HD];
+  __shared__ float wm_s[8][REP], wl_s[8][REP];
+  __shared__ __align__(16) float wo_s[8][REP][HD];
+  __shared__ int prefix_s[257];
+  __shared__ int last_s;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // item prefix over tokens: items(t) = nchunks(t) * nkv
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    prefix_s[0] = 0;
+    for (int t = 0; t < A.T; t++) {
+      int p = A.pos[t];
+      int nch = (p + 1 + ATT_CHUNK - 1) / ATT_CHUNK;
+      if (p < 0 || p >= A.max_pos || nch > A.max_chunks) {
+        nch = 0;
+        if (A.err) atomicExch(A.err, HG_ERR_CONTEXT);
+      }
+      acc += nch * A.nkv;
+      prefix_s[t + 1] = acc;
+    }
+  }
+  __syncthreads();
+  const int total = prefix_s[A.T];
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+  for (int item = blockIdx.x; item < total; item += gridDim.x) {
+    int lo = 0, hi = A.T - 1;
+    while (lo < hi) {
+      int mid = (lo + hi + 1) >> 1;
+      if (prefix_s[mid] <= item) lo = mid;
+      else hi = mid - 1;
+    }
+    const int t = lo, rem = item - prefix_s[t];
+    const int kvh = rem % A.nkv, c = rem / A.nkv;
+    const int pos = A.pos[t], n = pos + 1, nch = (n + ATT_CHUNK - 1) / ATT_CHUNK;
+    const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
+    const float* qkv = A.qkv + (size_t)t * A.qkv_stride;
+    const int qd = A.nh * HD, kvd = A.nkv * HD;
+    const float* cs = A.rope_cos + (size_t)pos * (HD / 2);
+    const float* sn = A.rope_sin + (size_t)pos * (HD / 2);
+    const int c0 = c * ATT_CHUNK;
+    const bool has_new = pos >= c0 && pos < c0 + ATT_CHUNK;
+    __syncthreads();
+    if (warp < REP) norm_rope_warp<HD>(qkv + (kvh * REP + warp) * HD, A.q_norm, A.eps, cs, sn, q_s[warp]);
+    if (has_new) {
+      const int pg = bt[pos / PAGE], slot = pos % PAGE;
+      long long off = (long long)pg * A.page_stride + ((long long)kvh * PAGE + slot) * HD;
+      if (warp == REP) {
+        norm_rope_warp<HD>(qkv + qd + kvh * HD, A.k_norm, A.eps, cs, sn, knew_s);
+        for (int j = lane; j < HD; j += 32) A.k_pool[off + j] = knew_s[j];
+      } else if (warp == REP + 1) {
+        for (int j = lane; j < HD; j += 32) {
+          float v = qkv[qd + kvd + kvh * HD + j];
+          vnew_s[j] = v;
+          A.v_pool[off + j] = v;
+        }
+      }
+    }
+    __syncthreads();
+    // scores for this warp's positions
+    float qreg[REP][E];
+#pragma unroll
+    for (int h = 0; h < REP; h++)
+#pragma unroll
+      for (int j = 0; j < E; j++) qreg[h][j] = q_s[h][lane * E + j];
+    float sc[8][REP];
+    float vr[8][E];
+    float m[REP];
+#pragma unroll
+    for (int h = 0; h < REP; h++) m[h] = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const int p = c0 + warp * 8 + i;
+      float kr[E];
+      if (p < n) {
+        const float *kp, *vp;
+        if (p == pos) {
+          kp = knew_s + lane * E;
+          vp = vnew_s + lane * E;
+        } else {
+          long long off = (long long)bt[p / PAGE] * A.page_stride + ((long long)kvh * PAGE + (p % PAGE)) * HD + lane * E;
+          kp = A.k_pool + off;
+          vp = A.v_pool + off;
+        }
+#pragma unroll
+        for (int j = 0; j < E; j++) {
+          kr[j] = kp[j];
+          vr[i][j] = vp[j];
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < E; j++) {
+          kr[j] = 0.0f;
+          vr[i][j] = 0.0f;
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < REP; h++) {
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < E; j++) s += qreg[h][j] * kr[j];
+        s = warp_sum(s) * scale;
+        sc[i][h] = p < n ? s : -INFINITY;
+        m[h] = fmaxf(m[h], sc[i][h]);
+      }
+    }
+    float o[REP][E], l[REP];
+#pragma unroll
+    for (int h = 0; h < REP; h++) {
+      l[h] = 0.0f;
+#pragma unroll
+      for (int j = 0; j < E; j++) o[h][j] = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        float pr = sc[i][h] == -INFINITY ? 0.0f : expf(sc[i][h] - m[h]);
+        l[h] += pr;
+#pragma unroll
+        for (int j = 0; j < E; j++) o[h][j] += pr * vr[i][j];
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < REP; h++) {
+      if (lane == 0) {
+        wm_s[warp][h] = m[h];
+        wl_s[warp][h] = l[h];
+      }
+#pragma unroll
+      for (int j = 0; j < E; j++) wo_s[warp][h][lane * E + j] = o[h][j];
+    }
+    __syncthreads();
+    // combine the 8 warps: threads over (head, dim)
+    for (int idx = threadIdx.x; idx < REP * HD; idx += blockDim.x) {
+      int h = idx / HD, dd = idx - h * HD;
+      float M = -INFINITY;
+      for (int w = 0; w < 8; w++) M = fmaxf(M, wm_s[w][h]);
+      float L = 0.0f, O = 0.0f;
+      for (int w = 0; w < 8; w++) {
+        float f = wm_s[w][h] == -INFINITY ? 0.0f : expf(wm_s[w][h] - M);
+        L += wl_s[w][h] * f;
+        O += wo_s[w][h][dd] * f;
+      }
+      float* pp = A.part + (((size_t)t * A.nh + kvh * REP + h) * A.max_chunks + c) * (HD + 2);
+      pp[2 + dd] = O;
+      if (dd == 0) {
+        pp[0] = M;
+        pp[1] = L;
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int old = atomicAdd(&A.cnt[t * A.nkv + kvh], 1);
+      last_s = (old == nch - 1);
+    }
+    __syncthreads();
+    if (!last_s) continue;
+    __threadfence();
+    // final combine over chunks for the REP heads of this kv head
+    for (int idx = threadIdx.x; idx < REP * HD; idx += blockDim.x) {
+      int h = idx / HD, dd = idx - h * HD;
+      const float* pb = A.part + (((size_t)t * A.nh + kvh * REP + h) * A.max_chunks) * (HD + 2);
+      float M = -INFINITY;
+      for (int cc = 0; cc < nch; cc++) M = fmaxf(M, __ldcg(pb + (size_t)cc * (HD + 2)));
+      float L = 0.0f, O = 0.0f;
+      for (int cc = 0; cc < nch; cc++) {
+        const float* p2 = pb + (size_t)cc * (HD + 2);
+        float f = expf(__ldcg(p2) - M);
+        L += __ldcg(p2 + 1) * f;
+        O += __ldcg(p2 + 2 + dd) * f;
+      }
+      float ov = O / L;
+      wo_s[0][h][dd] = ov;
+      if (A.out) A.out[(size_t)t * qd + (kvh * REP + h) * HD + dd] = ov;
+    }
+    __syncthreads();
+    if (A.qo) {
+      const int nbq = qd >> 5, nblk = REP * HD / 32, b0 = kvh * nblk;
+      for (int b = warp; b < nblk; b += 8) {
+        float dq;
+        int8_t q = quant_lane((&wo_s[0][0][0])[b * 32 + lane], &dq);
+        A.qo[(size_t)t * qd + q8_pos((b0 + b) * 32 + lane, nbq)] = q;
+        if (lane == 0) A.so[(size_t)t * q8_ss(nbq) + b0 + b] = dq;
+      }
+    }
+    if (threadIdx.x == 0) A.cnt[t * A.nkv + kvh] = 0;
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Row quantization of f32 activations (op-level entry points).
+// ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_quant_rows(const float* x, int cols, int8_t* q, float* s) {
+  const int t = blockIdx.x;
+  quant_row_block(x + (size_t)t * cols, cols, q + (size_t)t * cols, s + (size_t)t * q8_ss(cols >> 5));
+}
+
+// ------------------------------------------------------------------------------------------
+// Launchers
+// ------------------------------------------------------------------------------------------
+#define HG_NB_SWITCH(nb, ...)            \
+  switch (nb) {                          \
+    case 6: { constexpr int NB = 6; __VA_ARGS__; } break;   \
+    case 10: { constexpr int NB = 10; __VA_ARGS__; } break; \
+    case 16: { constexpr int NB = 16; __VA_ARGS__; } break; \
+    case 24: { constexpr int NB = 24; __VA_ARGS__; } break; \
+    case 48: { constexpr int NB = 48; __VA_ARGS__; } break; \
+    case 72: { constexpr int NB = 72; __VA_ARGS__; } break; \
+    default: { constexpr int NB = 0; __VA_ARGS__; } break;  \
+  }
+
+static inline size_t act_smem(int tt, int cols) { return (size_t)tt * cols + (size_t)tt * q8_ss(cols >> 5) * 4; }
+
+template <int EPI>
+static void launch_mv_tokens_t(const Dims& D, const DecodeBufs& B, const Q8M& W, const int8_t* aq, const float* as,
+                               float* out, int ostride, cudaStream_t st) {
+  int nb = W.cols >> 5;
+  if (B.T == 1) {
+    constexpr int ROWS = 8, TT = 1;
+    dim3 grid((W.rows + ROWS - 1) / ROWS);
+    HG_NB_SWITCH(nb, k_mv_tokens<NB, ROWS, TT, EPI><<<grid, ROWS * 8, act_smem(TT, W.cols), st>>>(D, B, W, aq, as, out, ostride));
+  } else {
+    constexpr int ROWS = 32, TT = 8;
+    dim3 grid((W.rows + ROWS - 1) / ROWS);
+    HG_NB_SWITCH(nb, k_mv_tokens<NB, ROWS, TT, EPI><<<grid, ROWS * 8, act_smem(TT, W.cols), st>>>(D, B, W, aq, as, out, ostride));
+  }
+}
+
+void launch_mv_store(const Dims& D, const DecodeBufs& B, const Q8M& W, const int8_t* aq, const float* as, float* out,
+                     int ostride, cudaStream_t st) {
+  launch_mv_tokens_t<EPI_STORE>(D, B, W, aq, as, out, ostride, st);
+}
+void launch_mv_resid(const Dims& D, const DecodeBufs& B, const Q8M& W, const int8_t* aq, const float* as,
+                     cudaStream_t st) {
+  launch_mv_tokens_t<EPI_RESID>(D, B, W, aq, as, nullptr, 0, st);
+}
+void launch_lmhead(const Dims& D, const DecodeBufs& B, const Q8M& W, const int8_t* aq, const float* as, float* logits,
+                   cudaStream_t st) {
+  launch_mv_tokens_t<EPI_LMHEAD>(D, B, W, aq, as, logits, D.vocab, st);
+}
+
+void launch_pre_norm(const Dims& D, const DecodeBufs& B, int mode, const float* embd, const float* norm_w,
+                     int8_t* q_out, float* s_out, float* h_out, int reset_moe, int reset_amax, cudaStream_t st) {
+  k_pre_norm<<<B.T, 256, D.d * sizeof(float), st>>>(D, B, mode, embd, norm_w, q_out, s_out, h_out, reset_moe,
+                                                    reset_amax);
+}
+
+void launch_route(const Dims& D, const DecodeBufs& B, const LayerDev& L, int layer, int prenormed, cudaStream_t st) {
+  k_route<<<B.T, 256, D.d * sizeof(float), st>>>(D, B, L, layer, prenormed);
+}
+
+// MoE combine without a residual (op-level entry point): y_out[t] = rank-order combine.
+__global__ void k_moe_combine(Dims D, DecodeBufs B, float* y_out) {
+  const int t = blockIdx.x, d = D.d;
+  const float* y = B.y + (size_t)t * (D.k + 1) * d;
+  float sc[MAX_TOPK];
+  for (int r = 0; r < D.k; r++) sc[r] = fmul(B.selw[t * D.k + r], D.wscale);
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    float o = 0.0f;
+    for (int r = 0; r < D.k; r++) o = fadd(o, fmul(sc[r], y[r * d + i]));
+    if (D.nsh > 0) o = fadd(o, y[D.k * d + i]);
+    y_out[(size_t)t * d + i] = o;
+  }
+}
+void launch_moe_combine(const Dims& D, const DecodeBufs& B, float* y_out, cudaStream_t st) {
+  k_moe_combine<<<B.T, 256, 0, st>>>(D, B, y_out);
+}
+
+void launch_ffn(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaStream_t st) {
+  const int groups = L.moe ? 1 + (D.ne < B.T * D.k ? D.ne : B.T * D.k) : 1;
+  const int fdim = L.moe ? D.f : D.df;
+  const int nb_up = D.d >> 5;
+  if (B.T == 1) {
+    constexpr int PAIRS = 16, TT = 1;
+    dim3 grid((fdim + PAIRS - 1) / PAIRS, groups);
+    HG_NB_SWITCH(nb_up, k_ffn_up<NB, PAIRS, TT><<<grid, PAIRS * 16, act_smem(TT, D.d), st>>>(D, B, L));
+  } else {
+    constexpr int PAIRS = 16, TT = 8;
+    dim3 grid((fdim + PAIRS - 1) / PAIRS, groups);
+    HG_NB_SWITCH(nb_up, k_ffn_up<NB, PAIRS, TT><<<grid, PAIRS * 16, act_smem(TT, D.d), st>>>(D, B, L));
+  }
+  // dense layers and the shared expert use the down matrix of their own width
+  const int nb_dn = fdim >> 5;
+  if (B.T == 1) {
+    constexpr int ROWS = 8, TT = 1;
+    dim3 grid((D.d + ROWS - 1) / ROWS, groups);
+    HG_NB_SWITCH(nb_dn, k_ffn_down<NB, ROWS, TT><<<grid, ROWS * 8, act_smem(TT, fdim), st>>>(D, B, L));
+  } else {
+    constexpr int ROWS = 32, TT = 8;
+    dim3 grid((D.d + ROWS - 1) / ROWS, groups);
+    HG_NB_SWITCH(nb_dn, k_ffn_down<NB, ROWS, TT><<<grid, ROWS * 8, act_smem(TT, fdim), st>>>(D, B, L));
+  }
+}
+
+int attn_grid(int T, int nkv, int max_chunks) {
+  long long items = (long long)T * nkv * max_chunks;
+  long long g = items < 4 * 148 ? items : 4 * 148;
+  return (int)(g > 0 ? g : 1);
+}
+
+cudaError_t launch_attn_args(const AttnArgs& A, int grid, cudaStream_t st) {
+  int rep = A.nh / A.nkv;
+  if (A.hd == 128 && rep == 4) k_attn<128, 4><<<grid, 256, 0, st>>>(A);
+  else if (A.hd == 64 && rep == 4) k_attn<64, 4><<<grid, 256, 0, st>>>(A);
+  else if (A.hd == 128 && rep == 2) k_attn<128, 2><<<grid, 256, 0, st>>>(A);
+  else if (A.hd == 64 && rep == 2) k_attn<64, 2><<<grid, 256, 0, st>>>(A);
+  else if (A.hd == 128 && rep == 1) k_attn<128, 1><<<grid, 256, 0, st>>>(A);
+  else if (A.hd == 64 && rep == 1) k_attn<64, 1><<<grid, 256, 0, st>>>(A);
+  else return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+void launch_quant_rows(const float* x, int rows, int cols, int8_t* q, float* s, cudaStream_t st) {
+  k_quant_rows<<<rows, 256, 0, st>>>(x, cols, q, s);
+}
+
+}  // namespace hg

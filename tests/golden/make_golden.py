@@ -1,0 +1,130 @@
+"""Generate the golden fixtures that pin the synthetic-model producer and the oracle's semantics.
+
+Run here (where the reference checkout is readable), never on the GPU box:
+
+    python tests/golden/make_golden.py --reference /path/to/HobbyLM
+
+It imports the reference's own Python code and writes, under tests/golden/:
+
+* synth_digests_{130M,500M}.json — per-tensor sha256 (f32 row-major bytes) of the F32 GGUF written by
+  the reference exporter (export/to_gguf.py:38-133) from ``MoETransformer(get_config(preset))``
+  after ``torch.manual_seed(0)`` (hobbylm/model.py:259-313). The exporter's HF-hub tokenizer download
+  (to_gguf.py:18-35) is replaced by placeholder tokens, and the 130M preset (no shared expert) gets
+  zero shared-expert tensors in its checkpoint so the exporter's unconditional shared-expert export
+  (to_gguf.py:126-129) can run.
+* torch_logits_130M.npz — the reference PyTorch model's f32 logits (hobbylm/model.py:322-356, MoE
+  ``expert_backend="bmm"``, hobbylm/moe.py:121-135) for a 12-token prompt (ids from
+  ``torch.Generator().manual_seed(1)``): the full last-position row plus per-position top-8 ids,
+  values and logsumexp. hobby-rs reads rms_eps from GGUF metadata while the PyTorch RMSNorm uses
+  1e-6, so the oracle is compared on a file written with rms_eps=1e-6.
+"""
+from __future__ import annotations
+
+import argparse
+import dataclasses
+import importlib.util
+import json
+import os
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+
+def reference_gguf_digests(ref: str, preset: str) -> dict:
+    import torch
+    import gguf
+    from hobbylm_b200.synth import tensor_digest
+
+    sys.path.insert(0, ref)
+    from hobbylm.config import get_config
+    from hobbylm.model import MoETransformer
+
+    cfg = get_config(preset)
+    torch.manual_seed(0)
+    model = MoETransformer(cfg)
+    sd = {k: v.detach().clone() for k, v in model.state_dict().items()}
+    if cfg.n_shared == 0:
+        for i in range(cfg.n_dense_layers, cfg.n_layers):
+            sd[f"blocks.{i}.ffn.shared.w13"] = torch.zeros(1, cfg.d_model, 2 * cfg.expert_ffn)
+            sd[f"blocks.{i}.ffn.shared.w2"] = torch.zeros(1, cfg.expert_ffn, cfg.d_model)
+    spec = importlib.util.spec_from_file_location("ref_to_gguf", os.path.join(ref, "export", "to_gguf.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+
+    def placeholder_tokenizer(vocab_size):
+        toks = [f"<|tok_{i}|>" for i in range(vocab_size)]
+        toks[50256] = "<|endoftext|>"
+        return toks, [3 if i == 50256 else 1 for i in range(vocab_size)], ["Ġ t"]
+
+    mod._gpt2_tokenizer = placeholder_tokenizer
+    with tempfile.TemporaryDirectory() as td:
+        ck = os.path.join(td, "ck", "model.pt")
+        os.makedirs(os.path.dirname(ck))
+        torch.save({"model": sd, "config": dataclasses.asdict(cfg)}, ck)
+        out = os.path.join(td, "ref.gguf")
+        argv = sys.argv
+        sys.argv = ["to_gguf.py", "--ckpt", ck, "--out", out]
+        try:
+            mod.main()
+        finally:
+            sys.argv = argv
+        r = gguf.GGUFReader(out)
+        digests = {}
+        for t in r.tensors:
+            arr = np.asarray(t.data, dtype=np.float32).reshape([int(x) for x in reversed(t.shape)])
+            digests[t.name] = tensor_digest(arr)
+        meta = {}
+        for k in ("hobbylm.context_length", "hobbylm.embedding_length", "hobbylm.block_count",
+                  "hobbylm.attention.layer_norm_rms_epsilon", "hobbylm.rope.freq_base",
+                  "hobbylm.expert_used_count", "hobbylm.expert_shared_count"):
+            f = r.fields[k]
+            meta[k] = float(f.parts[f.data[0]][0])
+    return {"preset": preset, "seed": 0, "digests": digests, "meta": meta}
+
+
+def reference_torch_logits(ref: str) -> dict:
+    import torch
+
+    sys.path.insert(0, ref)
+    from hobbylm.config import get_config
+    from hobbylm.model import MoETransformer
+    from hobbylm_b200.synth import prompt_ids
+
+    cfg = get_config("130M")
+    cfg.expert_backend = "bmm"
+    torch.manual_seed(0)
+    model = MoETransformer(cfg).eval()
+    ids = torch.from_numpy(prompt_ids(12, 1).astype(np.int64)).view(1, -1)
+    with torch.no_grad():
+        logits, _ = model(ids)
+    lg = logits[0].float().numpy()
+    top_ids = np.argsort(-lg, axis=1)[:, :8]
+    top_vals = np.take_along_axis(lg, top_ids, axis=1)
+    lse = np.log(np.exp(lg - lg.max(1, keepdims=True)).sum(1)) + lg.max(1)
+    return {"ids": ids[0].numpy().astype(np.uint32), "last": lg[-1].astype(np.float32),
+            "top_ids": top_ids.astype(np.int32), "top_vals": top_vals.astype(np.float32),
+            "lse": lse.astype(np.float32)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("HOBBYLM_REFERENCE", ""))
+    a = ap.parse_args()
+    if not a.reference or not os.path.isdir(a.reference):
+        raise SystemExit("--reference must point at the HobbyLM checkout")
+    for preset in ("130M", "500M"):
+        d = reference_gguf_digests(a.reference, preset)
+        with open(os.path.join(HERE, f"synth_digests_{preset}.json"), "w") as f:
+            json.dump(d, f, indent=1, sort_keys=True)
+        print(preset, len(d["digests"]), "tensors")
+    lg = reference_torch_logits(a.reference)
+    np.savez(os.path.join(HERE, "torch_logits_130M.npz"), **lg)
+    print("logits", lg["last"].shape)
+
+
+if __name__ == "__main__":
+    main()
