@@ -176,6 +176,7 @@ void alloc_work(hg_engine* e) {
   const int rep = c.n_heads / c.n_kv_heads;
   const size_t s_elems = (size_t)c.context_length * e->pf_tq * rep;
   const size_t pf_act = std::max((size_t)PF * c.dense_ffn, (size_t)PF * (k + 1) * f);
+  const size_t pf_act_s = std::max((size_t)PF * host_q8_ss(c.dense_ffn), (size_t)PF * (k + 1) * host_q8_ss(f));
   size_t bytes = 0;
   auto F = [&](size_t n) { bytes += f32_bytes(n); };
   auto I = [&](size_t n) { bytes += (n * 4 + 255) & ~size_t(255); };
@@ -194,7 +195,7 @@ void alloc_work(hg_engine* e) {
   F(pf_act); F(pf_act); F(pf_act); F((size_t)PF * (k + 1) * d); F((size_t)PF * k); F(s_elems);
   F((size_t)e->pf_tq * rep);
   B8((size_t)PF * std::max(d, qd)); B8(pf_act);
-  F((size_t)PF * std::max(ss_d, ss_q)); F((pf_act / 32) + PF * 8);
+  F((size_t)PF * std::max(ss_d, ss_q)); F(pf_act_s);
   I(PF); I((size_t)PF * k); I(ne); I((size_t)ne * PF); I((size_t)(ne + 1) * PF); I((size_t)(ne + 1) * PF);
   I(ne); I(ne); I(ne);
   e->work.init(bytes + (1 << 20));
@@ -247,7 +248,7 @@ void alloc_work(hg_engine* e) {
   P.qa = a.take<int8_t>((size_t)PF * std::max(d, qd));
   P.qact = a.take<int8_t>(pf_act);
   P.sa = a.take<float>((size_t)PF * std::max(ss_d, ss_q));
-  P.sact = a.take<float>((pf_act / 32) + PF * 8);
+  P.sact = a.take<float>(pf_act_s);
   P.ids = a.take<int32_t>(PF);
   P.sel = a.take<int32_t>((size_t)PF * k);
   P.ecount = a.take<int32_t>(ne);
