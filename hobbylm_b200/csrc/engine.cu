@@ -28,16 +28,25 @@ void set_last_error(const std::string& m) { g_last_error = m; }
   } while (0)
 
 // Device memory arena: one cudaMalloc, 256-byte aligned sub-allocations.
+// A measuring arena (measure = true) hands out no memory and only sums the sizes, so a layout
+// routine can run once to size the real allocation and once to carve it.
 struct Arena {
   char* base = nullptr;
   size_t cap = 0, used = 0;
+  bool measure = false;
   void init(size_t bytes) {
     cap = bytes;
+    used = 0;
+    measure = false;
     HG_CUDA(cudaMalloc((void**)&base, bytes));
   }
   template <class T>
   T* take(size_t n) {
     size_t b = (n * sizeof(T) + 255) & ~size_t(255);
+    if (measure) {
+      used += b;
+      return nullptr;
+    }
     if (used + b > cap) throw Error(HG_ERR_CUDA, "arena overflow");
     T* p = reinterpret_cast<T*>(base + used);
     used += b;
@@ -115,6 +124,14 @@ T* dev_alloc(Arena& a, size_t n) {
 
 void upload_q8(hg_engine* e, const Gguf& g, const std::string& name, int64_t count, int64_t rows, int64_t cols, Q8M* m,
                bool ref_counted = true) {
+  int ss0 = host_q8_ss(cols);
+  if (e->weights.measure) {
+    const GgufTensor* t = g.tensor(name);
+    if (!t) throw Error(HG_ERR_MISSING, "tensor `" + name + "` not found");
+    e->weights.take<int8_t>((size_t)(count * rows * cols));
+    e->weights.take<float>((size_t)(count * rows * ss0));
+    return;
+  }
   std::vector<float> w = g.load(name);
   if ((int64_t)w.size() != count * rows * cols)
     throw Error(HG_ERR_FORMAT, "tensor `" + name + "` has " + std::to_string(w.size()) + " elements, expected " +
@@ -139,14 +156,9 @@ void upload_q8(hg_engine* e, const Gguf& g, const std::string& name, int64_t cou
 
 float* upload_f32(hg_engine* e, const std::vector<float>& v) {
   float* d = dev_alloc<float>(e->weights, v.size());
-  HG_CUDA(cudaMemcpy(d, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+  if (!e->weights.measure) HG_CUDA(cudaMemcpy(d, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
   return d;
 }
-
-size_t q8_bytes(int64_t rows, int64_t cols) {
-  return (((size_t)(rows * cols) + 255) & ~size_t(255)) + (((size_t)(rows * host_q8_ss(cols)) * 4 + 255) & ~size_t(255));
-}
-size_t f32_bytes(size_t n) { return (n * 4 + 255) & ~size_t(255); }
 
 void validate_cfg(const hg_config& c) {
   auto bad = [](const std::string& m) { throw Error(HG_ERR_FORMAT, m); };
@@ -177,29 +189,14 @@ void alloc_work(hg_engine* e) {
   const size_t s_elems = (size_t)c.context_length * e->pf_tq * rep;
   const size_t pf_act = std::max((size_t)PF * c.dense_ffn, (size_t)PF * (k + 1) * f);
   const size_t pf_act_s = std::max((size_t)PF * host_q8_ss(c.dense_ffn), (size_t)PF * (k + 1) * host_q8_ss(f));
-  size_t bytes = 0;
-  auto F = [&](size_t n) { bytes += f32_bytes(n); };
-  auto I = [&](size_t n) { bytes += (n * 4 + 255) & ~size_t(255); };
-  auto B8 = [&](size_t n) { bytes += (n + 255) & ~size_t(255); };
-  // decode
-  I(3 * T);
-  F((size_t)T * d); B8((size_t)T * d); F((size_t)T * ss_d); F((size_t)T * qkvd);
-  B8((size_t)T * qd); F((size_t)T * ss_q); F((size_t)T * d); B8((size_t)T * d); F((size_t)T * ss_d);
-  I((size_t)T * k); F((size_t)T * k); I(ne + 2); I(ne); I((size_t)ne * T);
-  F((size_t)T * act_stride); F((size_t)T * (k + 1) * d);
-  F((size_t)T * c.n_heads * max_chunks * (c.head_dim + 2)); I((size_t)T * c.n_kv_heads);
-  F((size_t)T * c.vocab_size); bytes += (T * 8 + 255) & ~size_t(255);
-  I((size_t)c.n_layers * T * k); I(4);
-  // prefill
-  F((size_t)PF * d); F((size_t)PF * d); F((size_t)PF * qkvd); F((size_t)PF * qd); F((size_t)PF * qd);
-  F(pf_act); F(pf_act); F(pf_act); F((size_t)PF * (k + 1) * d); F((size_t)PF * k); F(s_elems);
-  F((size_t)e->pf_tq * rep);
-  B8((size_t)PF * std::max(d, qd)); B8(pf_act);
-  F((size_t)PF * std::max(ss_d, ss_q)); F(pf_act_s);
-  I(PF); I((size_t)PF * k); I(ne); I((size_t)ne * PF); I((size_t)(ne + 1) * PF); I((size_t)(ne + 1) * PF);
-  I(ne); I(ne); I(ne);
-  e->work.init(bytes + (1 << 20));
   Arena& a = e->work;
+  for (int pass = 0; pass < 2; pass++) {
+  if (pass == 0) {
+    a.measure = true;
+    a.used = 0;
+  } else {
+    a.init(a.used + (1 << 20));
+  }
   e->d_meta = a.take<int32_t>(3 * T);
   DecodeBufs& B = e->buf;
   B.T = T;
@@ -258,6 +255,7 @@ void alloc_work(hg_engine* e) {
   P.gm = a.take<int32_t>(ne);
   P.go = a.take<int32_t>(ne);
   P.gc = a.take<int32_t>(ne);
+  }
   HG_CUDA(cudaMemset(a.base, 0, a.cap));
 }
 
@@ -295,19 +293,15 @@ void load_engine(hg_engine* e, const char* path, const hg_engine_opts& o) {
   D.gsig = c.gating_sigmoid;
   D.max_pos = c.context_length;
   const int d = c.d_model, f = c.expert_ffn, df = c.dense_ffn, ne = c.n_experts, L = c.n_layers;
-  // weights arena size
-  size_t wb = f32_bytes((size_t)c.vocab_size * d) + f32_bytes(d) + q8_bytes(c.vocab_size, d);
-  wb += 2 * f32_bytes((size_t)c.context_length * (c.head_dim / 2));
-  for (int i = 0; i < L; i++) {
-    wb += 4 * f32_bytes(std::max(d, c.head_dim)) + q8_bytes(D.qkvd, d) + q8_bytes(d, D.qd);
-    if (i >= c.n_dense) {
-      wb += f32_bytes((size_t)ne * d) + f32_bytes(ne) + 2 * q8_bytes((int64_t)ne * f, d) + q8_bytes((int64_t)ne * d, f);
-      if (c.n_shared > 0) wb += 2 * q8_bytes(f, d) + q8_bytes(d, f);
-    } else {
-      wb += 2 * q8_bytes(df, d) + q8_bytes(d, df);
-    }
+  // weights: one measuring pass sizes the arena, the second uploads
+  for (int pass = 0; pass < 2; pass++) {
+  if (pass == 0) {
+    e->weights.measure = true;
+    e->weights.used = 0;
+  } else {
+    e->weights.init(e->weights.used + (1 << 20));
+    e->ref_weight_bytes = 0;
   }
-  e->weights.init(wb + (1 << 20));
   e->embd = upload_f32(e, g.load("token_embd.weight"));
   if (g.tensor("token_embd.weight")->n_elems() < (uint64_t)c.vocab_size * d)
     throw Error(HG_ERR_FORMAT, "token_embd too small");
@@ -353,6 +347,7 @@ void load_engine(hg_engine* e, const char* path, const hg_engine_opts& o) {
       upload_q8(e, g, p + "ffn_up.weight", 1, df, d, &Ld.up);
       upload_q8(e, g, p + "ffn_down.weight", 1, d, df, &Ld.down);
     }
+  }
   }
   // KV pool
   const long long blk = (long long)c.n_kv_heads * PAGE * c.head_dim;  // floats of one K (or V) page block

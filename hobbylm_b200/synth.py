@@ -23,6 +23,7 @@ from __future__ import annotations
 
 import hashlib
 import os
+import tempfile
 from dataclasses import dataclass
 
 import numpy as np
@@ -261,7 +262,7 @@ def cached_model(preset: str = "130M", seed: int = 0, *, quant: str = "q8_0", co
                  rms_eps: float = 1e-5, cache_dir: str | None = None) -> str:
     """Path of a cached synthetic GGUF (generated on first use)."""
     root = cache_dir or os.environ.get("HOBBYLM_B200_CACHE") or os.path.join(
-        os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "_cache")
+        tempfile.gettempdir(), "hobbylm_b200_cache")
     os.makedirs(root, exist_ok=True)
     eps_tag = f"{rms_eps:g}".replace("-", "m")
     name = f"hobbylm-{preset}-s{seed}-{quant}-ctx{context_length}-eps{eps_tag}.gguf"
