@@ -36,8 +36,22 @@ __device__ inline float block_sum(float v, float* red) {
   return red[0];
 }
 
+// Sequential f32 sum of squares of xs[0..n) (ops.rs:85-95 `ss += v * v`, no FMA) computed by one
+// thread; every thread of the block receives the result.
+__device__ inline float seq_sumsq_block(const float* xs, int n, float* red) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float ss = 0.0f;
+#pragma unroll 8
+    for (int i = 0; i < n; i++) ss = fadd(ss, fmul(xs[i], xs[i]));
+    red[0] = ss;
+  }
+  __syncthreads();
+  return red[0];
+}
+
 // ------------------------------------------------------------------------------------------
-// pre_norm: residual update, RMSNorm (ops.rs:85-95 with a tree sum), quantization of the result.
+// pre_norm: residual update, RMSNorm (ops.rs:85-95, sequential sum), quantization of the result.
 // mode 0: x = token embedding; 1: x += y[t][0] (dense FFN); 2: x += MoE combine (model.rs:300-323,
 // rank order then the shared expert); 3: x unchanged.
 // ------------------------------------------------------------------------------------------
@@ -72,12 +86,9 @@ __global__ void __launch_bounds__(256) k_pre_norm(Dims D, DecodeBufs B, int mode
   } else {
     for (int i = threadIdx.x; i < d; i += blockDim.x) xs[i] = x[i];
   }
-  float ss = 0.0f;
-  for (int i = threadIdx.x; i < d; i += blockDim.x) {
-    if (mode != 3) x[i] = xs[i];
-    ss += fmul(xs[i], xs[i]);
-  }
-  ss = block_sum(ss, red);
+  if (mode != 3)
+    for (int i = threadIdx.x; i < d; i += blockDim.x) x[i] = xs[i];
+  float ss = seq_sumsq_block(xs, d, red);
   float scale = __fdiv_rn(1.0f, __fsqrt_rn(fadd(__fdiv_rn(ss, (float)d), D.eps)));
   for (int i = threadIdx.x; i < d; i += blockDim.x) {
     float h = fmul(fmul(xs[i], scale), norm_w[i]);
@@ -236,13 +247,8 @@ __global__ void __launch_bounds__(256) k_route(Dims D, DecodeBufs B, LayerDev Ld
     for (int i = threadIdx.x; i < d; i += blockDim.x) hs[i] = B.h2[(size_t)t * d + i];
   } else {
     const float* x = B.x + (size_t)t * d;
-    float ss = 0.0f;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) {
-      float v = x[i];
-      hs[i] = v;
-      ss += fmul(v, v);
-    }
-    ss = block_sum(ss, red);
+    for (int i = threadIdx.x; i < d; i += blockDim.x) hs[i] = x[i];
+    float ss = seq_sumsq_block(hs, d, red);
     float scale = __fdiv_rn(1.0f, __fsqrt_rn(fadd(__fdiv_rn(ss, (float)d), D.eps)));
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
       float h = fmul(fmul(hs[i], scale), Ld.ffn_norm[i]);
@@ -441,55 +447,62 @@ __global__ void __launch_bounds__(ROWS * 8) k_ffn_down(Dims D, DecodeBufs B, Lay
 }
 
 // ------------------------------------------------------------------------------------------
-// Attention (model.rs:199-233) over a paged f32 KV pool. Work item = (token, kv head, chunk of
-// ATT_CHUNK positions); 8 warps x 8 positions per item. The item holding the new position
-// QK-norms + ropes k and appends k, v to its page slot. Each item writes an online-softmax
-// partial (max, sum, o[hd]) per q head; the last item of a (token, kv head) to arrive combines
-// the partials, writes o (f32, optional) and its quantized form (optional).
+// Attention (model.rs:199-233) over a paged f32 KV pool, in the reference's arithmetic order.
+//
+// k_attn_scores: work item = (token, kv head, chunk of ATT_CHUNK positions), 8 warps x 8
+//   positions. QK-norm (sequential sum, model.rs:753-763) + RoPE of the item's q heads, and for
+//   the chunk holding the new position the same for k, plus the k/v append to its page slot.
+//   s[t][h][j] = dot(q_h, k_j) * (1/sqrt(hd)) in the ops::dot order; the chunk maximum per head.
+// k_attn_out: one CTA per (token, kv head), REP*HD threads. Softmax (ops.rs:112-128): global max,
+//   e_j = exp(s_j - max) (parallel), sum = sequential f32 sum over j, inv = 1/sum; then every
+//   (head, dim) thread accumulates o += (e_j * inv) * v_j[dim] sequentially over j (model.rs:
+//   227-232). V pages stream through a shared-memory ring filled by TMA bulk copies
+//   (cp.async.bulk, one 16 x hd block per page) completing on mbarriers. The result is quantized
+//   per 32-block for the output projection (quant.rs:112-123).
 // ------------------------------------------------------------------------------------------
 
-// per-head RMSNorm (model.rs:753-763, tree sum) + rotate-half RoPE (ops.rs:157-166) of one head
-// vector held by one warp; E = hd/32 elements per lane, lane owns elements lane + 32 j.
+// per-head RMSNorm with a sequential sum (model.rs:753-763) + rotate-half RoPE (ops.rs:157-166)
+// of one head vector by one warp. buf: this warp's HD-float shared scratch; dst may alias buf.
 template <int HD>
 __device__ __forceinline__ void norm_rope_warp(const float* src, const float* w, float eps, const float* cs,
-                                               const float* sn, float* dst) {
-  constexpr int E = HD / 32, HALF = HD / 2;
-  int lane = threadIdx.x & 31;
-  float v[E];
-  float ss = 0.0f;
-#pragma unroll
-  for (int j = 0; j < E; j++) {
-    v[j] = src[lane + 32 * j];
-    ss += fmul(v[j], v[j]);
+                                               const float* sn, float* buf) {
+  constexpr int HALF = HD / 2;
+  const int lane = threadIdx.x & 31;
+  for (int i = lane; i < HD; i += 32) buf[i] = src[i];
+  __syncwarp();
+  float scale = 0.0f;
+  if (lane == 0) {
+    float ss = 0.0f;
+#pragma unroll 8
+    for (int i = 0; i < HD; i++) ss = fadd(ss, fmul(buf[i], buf[i]));
+    scale = __fdiv_rn(1.0f, __fsqrt_rn(fadd(__fdiv_rn(ss, (float)HD), eps)));
   }
-  ss = warp_sum(ss);
-  float scale = __fdiv_rn(1.0f, __fsqrt_rn(fadd(__fdiv_rn(ss, (float)HD), eps)));
+  scale = __shfl_sync(0xffffffffu, scale, 0);
+  float v[HD / 32];
 #pragma unroll
-  for (int j = 0; j < E; j++) dst[lane + 32 * j] = fmul(fmul(v[j], scale), w[lane + 32 * j]);
+  for (int j = 0; j < HD / 32; j++) v[j] = fmul(fmul(buf[lane + 32 * j], scale), w[lane + 32 * j]);
   __syncwarp();
 #pragma unroll
-  for (int j = 0; j < E / 2; j++) {
-    int i = lane + 32 * j;  // i < HALF
-    float x1 = dst[i], x2 = dst[i + HALF];
-    float c = cs[i], s = sn[i];
-    __syncwarp();
-    dst[i] = __fsub_rn(fmul(x1, c), fmul(x2, s));
-    dst[i + HALF] = fadd(fmul(x2, c), fmul(x1, s));
+  for (int j = 0; j < HD / 32; j++) buf[lane + 32 * j] = v[j];
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < HD / 64; j++) {
+    const int i = lane + 32 * j;  // i < HALF
+    const float x1 = buf[i], x2 = buf[i + HALF], c = cs[i], sv = sn[i];
+    v[j] = __fsub_rn(fmul(x1, c), fmul(x2, sv));
+    v[j + HD / 64] = fadd(fmul(x2, c), fmul(x1, sv));
+  }
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < HD / 64; j++) {
+    buf[lane + 32 * j] = v[j];
+    buf[lane + 32 * j + HALF] = v[j + HD / 64];
   }
   __syncwarp();
 }
 
-template <int HD, int REP>
-__global__ void __launch_bounds__(256) k_attn(AttnArgs A) {
-  constexpr int E = HD / 32;  // floats per lane per row
-  __shared__ __align__(16) float q_s[REP][HD];
-  __shared__ __align__(16) float knew_s[HD], vnew_s[HD];
-  __shared__ float wm_s[8][REP], wl_s[8][REP];
-  __shared__ __align__(16) float wo_s[8][REP][HD];
-  __shared__ int prefix_s[257];
-  __shared__ int last_s;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // item prefix over tokens: items(t) = nchunks(t) * nkv
+// item prefix over tokens: items(t) = nchunks(t) * nkv (positions beyond max_pos raise an error)
+__device__ inline int attn_item_prefix(const AttnArgs& A, int* prefix_s) {
   if (threadIdx.x == 0) {
     int acc = 0;
     prefix_s[0] = 0;
@@ -505,7 +518,18 @@ __global__ void __launch_bounds__(256) k_attn(AttnArgs A) {
     }
   }
   __syncthreads();
-  const int total = prefix_s[A.T];
+  return prefix_s[A.T];
+}
+
+template <int HD, int REP>
+__global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
+  constexpr int E = HD / 32;
+  __shared__ __align__(16) float q_s[REP][HD];
+  __shared__ __align__(16) float knew_s[HD];
+  __shared__ float wmax_s[8][REP];
+  __shared__ int prefix_s[257];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = attn_item_prefix(A, prefix_s);
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
   for (int item = blockIdx.x; item < total; item += gridDim.x) {
     int lo = 0, hi = A.T - 1;
@@ -516,7 +540,7 @@ __global__ void __launch_bounds__(256) k_attn(AttnArgs A) {
     }
     const int t = lo, rem = item - prefix_s[t];
     const int kvh = rem % A.nkv, c = rem / A.nkv;
-    const int pos = A.pos[t], n = pos + 1, nch = (n + ATT_CHUNK - 1) / ATT_CHUNK;
+    const int pos = A.pos[t], n = pos + 1;
     const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
     const float* qkv = A.qkv + (size_t)t * A.qkv_stride;
     const int qd = A.nh * HD, kvd = A.nkv * HD;
@@ -527,147 +551,212 @@ __global__ void __launch_bounds__(256) k_attn(AttnArgs A) {
     __syncthreads();
     if (warp < REP) norm_rope_warp<HD>(qkv + (kvh * REP + warp) * HD, A.q_norm, A.eps, cs, sn, q_s[warp]);
     if (has_new) {
-      const int pg = bt[pos / PAGE], slot = pos % PAGE;
-      long long off = (long long)pg * A.page_stride + ((long long)kvh * PAGE + slot) * HD;
+      const long long off =
+          (long long)bt[pos / PAGE] * A.page_stride + ((long long)kvh * PAGE + pos % PAGE) * HD;
       if (warp == REP) {
         norm_rope_warp<HD>(qkv + qd + kvh * HD, A.k_norm, A.eps, cs, sn, knew_s);
         for (int j = lane; j < HD; j += 32) A.k_pool[off + j] = knew_s[j];
       } else if (warp == REP + 1) {
-        for (int j = lane; j < HD; j += 32) {
-          float v = qkv[qd + kvd + kvh * HD + j];
-          vnew_s[j] = v;
-          A.v_pool[off + j] = v;
-        }
+        for (int j = lane; j < HD; j += 32) A.v_pool[off + j] = qkv[qd + kvd + kvh * HD + j];
       }
+      // the V/K rows are read by bulk copies in k_attn_out: order these generic writes first
+      asm volatile("fence.proxy.async.global;" ::: "memory");
     }
     __syncthreads();
-    // scores for this warp's positions
     float qreg[REP][E];
 #pragma unroll
     for (int h = 0; h < REP; h++)
 #pragma unroll
-      for (int j = 0; j < E; j++) qreg[h][j] = q_s[h][lane * E + j];
-    float sc[8][REP];
-    float vr[8][E];
-    float m[REP];
+      for (int i = 0; i < E; i++) qreg[h][i] = q_s[h][32 * i + lane];
+    float mx[REP];
 #pragma unroll
-    for (int h = 0; h < REP; h++) m[h] = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-      const int p = c0 + warp * 8 + i;
+    for (int h = 0; h < REP; h++) mx[h] = -INFINITY;
+    float* srow = A.S + ((size_t)t * A.nh + kvh * REP) * A.s_stride;
+#pragma unroll 2
+    for (int i8 = 0; i8 < 8; i8++) {
+      const int p = c0 + warp * 8 + i8;
+      if (p >= n) break;
+      const float* kp = p == pos ? knew_s
+                                 : A.k_pool + (long long)bt[p / PAGE] * A.page_stride +
+                                       ((long long)kvh * PAGE + (p % PAGE)) * HD;
       float kr[E];
-      if (p < n) {
-        const float *kp, *vp;
-        if (p == pos) {
-          kp = knew_s + lane * E;
-          vp = vnew_s + lane * E;
-        } else {
-          long long off = (long long)bt[p / PAGE] * A.page_stride + ((long long)kvh * PAGE + (p % PAGE)) * HD + lane * E;
-          kp = A.k_pool + off;
-          vp = A.v_pool + off;
-        }
 #pragma unroll
-        for (int j = 0; j < E; j++) {
-          kr[j] = kp[j];
-          vr[i][j] = vp[j];
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < E; j++) {
-          kr[j] = 0.0f;
-          vr[i][j] = 0.0f;
-        }
-      }
+      for (int i = 0; i < E; i++) kr[i] = kp[32 * i + lane];
 #pragma unroll
       for (int h = 0; h < REP; h++) {
-        float s = 0.0f;
+        // ops::dot: lane = 8m + l accumulates elements 32i + lane (FMA, i ascending), then
+        // (a0+a1)+(a2+a3) per SIMD lane and the 8-lane tree
+        float acc = 0.0f;
 #pragma unroll
-        for (int j = 0; j < E; j++) s += qreg[h][j] * kr[j];
-        s = warp_sum(s) * scale;
-        sc[i][h] = p < n ? s : -INFINITY;
-        m[h] = fmaxf(m[h], sc[i][h]);
+        for (int i = 0; i < E; i++) acc = __fmaf_rn(qreg[h][i], kr[i], acc);
+        acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 8));
+        acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 16));
+        float sc = fmul(hsum8_group(acc), scale);
+        if (lane == 0) srow[(size_t)h * A.s_stride + p] = sc;
+        mx[h] = fmaxf(mx[h], sc);
       }
     }
-    float o[REP][E], l[REP];
+    if (lane == 0)
 #pragma unroll
-    for (int h = 0; h < REP; h++) {
-      l[h] = 0.0f;
-#pragma unroll
-      for (int j = 0; j < E; j++) o[h][j] = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        float pr = sc[i][h] == -INFINITY ? 0.0f : expf(sc[i][h] - m[h]);
-        l[h] += pr;
-#pragma unroll
-        for (int j = 0; j < E; j++) o[h][j] += pr * vr[i][j];
-      }
-    }
-#pragma unroll
-    for (int h = 0; h < REP; h++) {
-      if (lane == 0) {
-        wm_s[warp][h] = m[h];
-        wl_s[warp][h] = l[h];
-      }
-#pragma unroll
-      for (int j = 0; j < E; j++) wo_s[warp][h][lane * E + j] = o[h][j];
-    }
+      for (int h = 0; h < REP; h++) wmax_s[warp][h] = mx[h];
     __syncthreads();
-    // combine the 8 warps: threads over (head, dim)
-    for (int idx = threadIdx.x; idx < REP * HD; idx += blockDim.x) {
-      int h = idx / HD, dd = idx - h * HD;
-      float M = -INFINITY;
-      for (int w = 0; w < 8; w++) M = fmaxf(M, wm_s[w][h]);
-      float L = 0.0f, O = 0.0f;
-      for (int w = 0; w < 8; w++) {
-        float f = wm_s[w][h] == -INFINITY ? 0.0f : expf(wm_s[w][h] - M);
-        L += wl_s[w][h] * f;
-        O += wo_s[w][h][dd] * f;
-      }
-      float* pp = A.part + (((size_t)t * A.nh + kvh * REP + h) * A.max_chunks + c) * (HD + 2);
-      pp[2 + dd] = O;
-      if (dd == 0) {
-        pp[0] = M;
-        pp[1] = L;
-      }
+    if (threadIdx.x < REP) {
+      float m = -INFINITY;
+      for (int w = 0; w < 8; w++) m = fmaxf(m, wmax_s[w][threadIdx.x]);
+      A.cmax[((size_t)t * A.nh + kvh * REP + threadIdx.x) * A.max_chunks + c] = m;
     }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int old = atomicAdd(&A.cnt[t * A.nkv + kvh], 1);
-      last_s = (old == nch - 1);
-    }
-    __syncthreads();
-    if (!last_s) continue;
-    __threadfence();
-    // final combine over chunks for the REP heads of this kv head
-    for (int idx = threadIdx.x; idx < REP * HD; idx += blockDim.x) {
-      int h = idx / HD, dd = idx - h * HD;
-      const float* pb = A.part + (((size_t)t * A.nh + kvh * REP + h) * A.max_chunks) * (HD + 2);
-      float M = -INFINITY;
-      for (int cc = 0; cc < nch; cc++) M = fmaxf(M, __ldcg(pb + (size_t)cc * (HD + 2)));
-      float L = 0.0f, O = 0.0f;
-      for (int cc = 0; cc < nch; cc++) {
-        const float* p2 = pb + (size_t)cc * (HD + 2);
-        float f = expf(__ldcg(p2) - M);
-        L += __ldcg(p2 + 1) * f;
-        O += __ldcg(p2 + 2 + dd) * f;
-      }
-      float ov = O / L;
-      wo_s[0][h][dd] = ov;
-      if (A.out) A.out[(size_t)t * qd + (kvh * REP + h) * HD + dd] = ov;
-    }
-    __syncthreads();
-    if (A.qo) {
-      const int nbq = qd >> 5, nblk = REP * HD / 32, b0 = kvh * nblk;
-      for (int b = warp; b < nblk; b += 8) {
-        float dq;
-        int8_t q = quant_lane((&wo_s[0][0][0])[b * 32 + lane], &dq);
-        A.qo[(size_t)t * qd + q8_pos((b0 + b) * 32 + lane, nbq)] = q;
-        if (lane == 0) A.so[(size_t)t * q8_ss(nbq) + b0 + b] = dq;
-      }
-    }
-    if (threadIdx.x == 0) A.cnt[t * A.nkv + kvh] = 0;
   }
+}
+
+// ---- mbarrier / bulk-copy helpers (sm_90+ PTX) ----
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// Bounded wait for phase `parity` of an mbarrier: gives up after ~1 s (globaltimer) and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done = 0;
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  while (true) {
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (done) return true;
+    uint64_t t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    if (t1 - t0 > 1000000000ull) return false;
+  }
+}
+
+constexpr int ATT_STAGES = 8;  // V pages in flight per CTA
+constexpr int ATT_ECH = 512;   // softmax positions per sum chunk
+
+template <int HD, int REP>
+__global__ void __launch_bounds__(REP * HD) k_attn_out(AttnArgs A) {
+  constexpr int NT = REP * HD, NW = NT / 32;
+  constexpr uint32_t PAGE_BYTES = PAGE * HD * 4;
+  extern __shared__ __align__(128) unsigned char ring[];  // ATT_STAGES pages of [16][HD] f32
+  __shared__ __align__(8) uint64_t bar[ATT_STAGES];
+  __shared__ float ebuf[REP][ATT_ECH];
+  __shared__ float m_s[REP], inv_s[REP];
+  __shared__ int fail_s;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = tid / HD, di = tid % HD;
+  const int t = blockIdx.x / A.nkv, kvh = blockIdx.x % A.nkv;
+  const int pos = A.pos[t];
+  if (pos < 0 || pos >= A.max_pos) return;  // flagged by k_attn_scores
+  const int n = pos + 1, nch = (n + ATT_CHUNK - 1) / ATT_CHUNK, npages = (n + PAGE - 1) / PAGE;
+  const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
+  float* srow = A.S + ((size_t)t * A.nh + kvh * REP) * A.s_stride;
+  if (tid == 0) {
+    fail_s = 0;
+    for (int s = 0; s < ATT_STAGES; s++) mbar_init(&bar[s], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  // start streaming V pages (independent of the softmax)
+  const float* vbase = A.v_pool + (long long)kvh * PAGE * HD;
+  if (tid == 0) {
+    for (int p = 0; p < ATT_STAGES && p < npages; p++) {
+      mbar_expect_tx(&bar[p], PAGE_BYTES);
+      bulk_g2s(ring + (size_t)p * PAGE_BYTES, vbase + (long long)bt[p] * A.page_stride, PAGE_BYTES, &bar[p]);
+    }
+  }
+  // global max per head over the chunk maxima
+  if (tid < REP) {
+    float m = -INFINITY;
+    const float* cm = A.cmax + ((size_t)t * A.nh + kvh * REP + tid) * A.max_chunks;
+    for (int c = 0; c < nch; c++) m = fmaxf(m, cm[c]);
+    m_s[tid] = m;
+  }
+  __syncthreads();
+  // e_j = exp(s_j - max) in parallel (written back in place), sum sequential per head in chunks
+  float sum = 0.0f;  // meaningful in warp h < REP
+  for (int j0 = 0; j0 < n; j0 += ATT_ECH) {
+    const int cnt = min(ATT_ECH, n - j0);
+    for (int i = tid; i < REP * cnt; i += NT) {
+      const int hh = i / cnt, j = i - hh * cnt;
+      float e = exp_cr(__fsub_rn(srow[(size_t)hh * A.s_stride + j0 + j], m_s[hh]));
+      ebuf[hh][j] = e;
+      srow[(size_t)hh * A.s_stride + j0 + j] = e;
+    }
+    __syncthreads();
+    if (warp < REP) {  // every lane of warp h runs the same chain (broadcast reads)
+#pragma unroll 8
+      for (int j = 0; j < cnt; j++) sum = fadd(sum, ebuf[warp][j]);
+    }
+    __syncthreads();
+  }
+  if (warp < REP && lane == 0) inv_s[warp] = __fdiv_rn(1.0f, sum);
+  __syncthreads();
+  const float inv = inv_s[h];
+  const float* erow = srow + (size_t)h * A.s_stride;
+  // o[h][di] = sum_j (e_j * inv) * v_j[di], sequential in j
+  float acc = 0.0f;
+  float e_next = lane < PAGE && lane < n ? erow[lane] : 0.0f;
+  int p = 0;
+  for (; p < npages; p++) {
+    const int st = p % ATT_STAGES;
+    const uint32_t parity = (uint32_t)(p / ATT_STAGES) & 1u;
+    const float e_cur = e_next;
+    const int jn = p * PAGE + PAGE + lane;
+    e_next = (lane < PAGE && jn < n) ? erow[jn] : 0.0f;
+    if (!mbar_wait(&bar[st], parity)) {
+      if (lane == 0) atomicExch(&fail_s, 1);
+    }
+    const float* vs = reinterpret_cast<const float*>(ring + (size_t)st * PAGE_BYTES);
+    const int rows = min(PAGE, n - p * PAGE);
+    for (int r = 0; r < rows; r++) {
+      const float pr = fmul(__shfl_sync(0xffffffffu, e_cur, r), inv);
+      acc = fadd(acc, fmul(pr, vs[r * HD + di]));
+    }
+    __syncthreads();
+    if (fail_s) break;
+    if (tid == 0 && p + ATT_STAGES < npages) {
+      const int q = p + ATT_STAGES;
+      mbar_expect_tx(&bar[st], PAGE_BYTES);
+      bulk_g2s(ring + (size_t)st * PAGE_BYTES, vbase + (long long)bt[q] * A.page_stride, PAGE_BYTES, &bar[st]);
+    }
+  }
+  if (fail_s) {
+    // a bulk copy did not complete in time: report, then wait (bounded) for the pages still in
+    // flight (p .. p + ATT_STAGES - 1) so no copy lands in shared memory after this CTA exits
+    if (tid == 0) {
+      if (A.err) atomicExch(A.err, HG_ERR_TIMEOUT);
+      for (int q = p; q < p + ATT_STAGES && q < npages; q++)
+        mbar_wait(&bar[q % ATT_STAGES], (uint32_t)(q / ATT_STAGES) & 1u);
+    }
+    __syncthreads();
+    return;
+  }
+  const int hg = kvh * REP + h;
+  const int qd = A.nh * HD;
+  if (A.out) A.out[(size_t)t * qd + hg * HD + di] = acc;
+  if (A.qo) {
+    // each warp holds 32 consecutive dims of one head = one 32-block
+    float dq;
+    int8_t q = quant_lane(acc, &dq);
+    const int nbq = qd >> 5;
+    A.qo[(size_t)t * qd + q8_pos(hg * HD + di, nbq)] = q;
+    if (lane == 0) A.so[(size_t)t * q8_ss(nbq) + ((hg * HD + di) >> 5)] = dq;
+  }
+  (void)NW;
 }
 
 // ------------------------------------------------------------------------------------------
@@ -781,16 +870,39 @@ int attn_grid(int T, int nkv, int max_chunks) {
   return (int)(g > 0 ? g : 1);
 }
 
+template <int HD, int REP>
+static cudaError_t launch_attn_t(const AttnArgs& A, int grid, cudaStream_t st) {
+  k_attn_scores<HD, REP><<<grid, 256, 0, st>>>(A);
+  const size_t smem = (size_t)ATT_STAGES * PAGE * HD * 4;
+  k_attn_out<HD, REP><<<A.T * A.nkv, REP * HD, smem, st>>>(A);
+  return cudaGetLastError();
+}
+
+// Opt in to the ring's dynamic shared memory on the current device (call before any launch or
+// graph capture).
+cudaError_t prepare_attn(int hd, int rep) {
+  auto set = [](const void* fn, size_t bytes) {
+    return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  };
+  const size_t s128 = (size_t)ATT_STAGES * PAGE * 128 * 4, s64 = (size_t)ATT_STAGES * PAGE * 64 * 4;
+  if (hd == 128 && rep == 4) return set((const void*)k_attn_out<128, 4>, s128);
+  if (hd == 64 && rep == 4) return set((const void*)k_attn_out<64, 4>, s64);
+  if (hd == 128 && rep == 2) return set((const void*)k_attn_out<128, 2>, s128);
+  if (hd == 64 && rep == 2) return set((const void*)k_attn_out<64, 2>, s64);
+  if (hd == 128 && rep == 1) return set((const void*)k_attn_out<128, 1>, s128);
+  if (hd == 64 && rep == 1) return set((const void*)k_attn_out<64, 1>, s64);
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t launch_attn_args(const AttnArgs& A, int grid, cudaStream_t st) {
   int rep = A.nh / A.nkv;
-  if (A.hd == 128 && rep == 4) k_attn<128, 4><<<grid, 256, 0, st>>>(A);
-  else if (A.hd == 64 && rep == 4) k_attn<64, 4><<<grid, 256, 0, st>>>(A);
-  else if (A.hd == 128 && rep == 2) k_attn<128, 2><<<grid, 256, 0, st>>>(A);
-  else if (A.hd == 64 && rep == 2) k_attn<64, 2><<<grid, 256, 0, st>>>(A);
-  else if (A.hd == 128 && rep == 1) k_attn<128, 1><<<grid, 256, 0, st>>>(A);
-  else if (A.hd == 64 && rep == 1) k_attn<64, 1><<<grid, 256, 0, st>>>(A);
-  else return cudaErrorInvalidValue;
-  return cudaGetLastError();
+  if (A.hd == 128 && rep == 4) return launch_attn_t<128, 4>(A, grid, st);
+  if (A.hd == 64 && rep == 4) return launch_attn_t<64, 4>(A, grid, st);
+  if (A.hd == 128 && rep == 2) return launch_attn_t<128, 2>(A, grid, st);
+  if (A.hd == 64 && rep == 2) return launch_attn_t<64, 2>(A, grid, st);
+  if (A.hd == 128 && rep == 1) return launch_attn_t<128, 1>(A, grid, st);
+  if (A.hd == 64 && rep == 1) return launch_attn_t<64, 1>(A, grid, st);
+  return cudaErrorInvalidValue;
 }
 
 void launch_quant_rows(const float* x, int rows, int cols, int8_t* q, float* s, cudaStream_t st) {

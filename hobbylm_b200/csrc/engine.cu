@@ -222,8 +222,9 @@ void alloc_work(hg_engine* e) {
   B.act = a.take<float>((size_t)T * act_stride);
   B.act_stride = act_stride;
   B.y = a.take<float>((size_t)T * (k + 1) * d);
-  B.part = a.take<float>((size_t)T * c.n_heads * max_chunks * (c.head_dim + 2));
-  B.cnt = a.take<int32_t>((size_t)T * c.n_kv_heads);
+  B.s_stride = ((long long)c.context_length + 15) & ~15LL;
+  B.S = a.take<float>((size_t)T * c.n_heads * B.s_stride);
+  B.cmax = a.take<float>((size_t)T * c.n_heads * max_chunks);
   B.max_chunks = max_chunks;
   B.logits = a.take<float>((size_t)T * c.vocab_size);
   B.amax = a.take<unsigned long long>(T);
@@ -271,6 +272,7 @@ void load_engine(hg_engine* e, const char* path, const hg_engine_opts& o) {
     if (!g.tensor(t)) throw Error(HG_ERR_MISSING, std::string("tensor `") + t + "` not found");
   HG_CUDA(cudaSetDevice(e->device));
   HG_CUDA(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+  HG_CUDA(prepare_attn(c.head_dim, c.n_heads / c.n_kv_heads));
   e->cfg = c;
   Dims& D = e->D;
   D.d = c.d_model;
@@ -436,8 +438,9 @@ AttnArgs make_attn_args(hg_engine* e, const DecodeBufs& B, int l) {
   A.k_pool = e->kv + (long long)l * e->layer_stride;
   A.v_pool = A.k_pool + e->layer_stride / 2;
   A.page_stride = e->page_stride;
-  A.part = B.part;
-  A.cnt = B.cnt;
+  A.S = B.S;
+  A.s_stride = B.s_stride;
+  A.cmax = B.cmax;
   A.out = nullptr;
   A.qo = B.qo;
   A.so = B.so;
@@ -878,10 +881,11 @@ MoeScratch moe_scratch_layout(const hg_moe_weights* w, int ntok) {
   return s;
 }
 
+size_t kv_s_stride(const hg_kv_attn_args* a) { return ((size_t)a->max_pos + 15) & ~size_t(15); }
 size_t kv_scratch_bytes(const hg_kv_attn_args* a) {
   int max_chunks = (a->max_pos + ATT_CHUNK - 1) / ATT_CHUNK;
-  return align256((size_t)a->n_seqs * a->n_heads * max_chunks * (a->head_dim + 2) * 4) +
-         align256((size_t)a->n_seqs * a->n_kv_heads * 4) + 256;
+  return align256((size_t)a->n_seqs * a->n_heads * kv_s_stride(a) * 4) +
+         align256((size_t)a->n_seqs * a->n_heads * max_chunks * 4) + 256;
 }
 
 }  // namespace
@@ -1137,6 +1141,11 @@ int hg_op_kv_attn(const hg_kv_attn_args* a, void* scratch, void* stream) {
     cudaStream_t st = as_stream(stream);
     int max_chunks = (a->max_pos + ATT_CHUNK - 1) / ATT_CHUNK;
     char* base = static_cast<char*>(scratch);
+    {
+      cudaError_t pe = prepare_attn(a->head_dim, a->n_heads / a->n_kv_heads);
+      if (pe == cudaErrorInvalidValue) throw Error(HG_ERR_INVALID, "unsupported head_dim / GQA group");
+      HG_CUDA(pe);
+    }
     AttnArgs A{};
     A.T = a->n_seqs;
     A.nh = a->n_heads;
@@ -1158,14 +1167,13 @@ int hg_op_kv_attn(const hg_kv_attn_args* a, void* scratch, void* stream) {
     A.k_pool = a->k_pool;
     A.v_pool = a->v_pool;
     A.page_stride = a->page_stride;
-    size_t part_bytes = align256((size_t)a->n_seqs * a->n_heads * max_chunks * (a->head_dim + 2) * 4);
-    A.part = reinterpret_cast<float*>(base);
-    A.cnt = reinterpret_cast<int32_t*>(base + part_bytes);
+    A.s_stride = (long long)kv_s_stride(a);
+    A.S = reinterpret_cast<float*>(base);
+    A.cmax = reinterpret_cast<float*>(base + align256((size_t)a->n_seqs * a->n_heads * A.s_stride * 4));
     A.err = nullptr;
     A.out = a->out;
     A.qo = nullptr;
     A.so = nullptr;
-    HG_CUDA(cudaMemsetAsync(A.cnt, 0, (size_t)a->n_seqs * a->n_kv_heads * 4, st));
     cudaError_t err = launch_attn_args(A, attn_grid(A.T, A.nkv, max_chunks), st);
     if (err == cudaErrorInvalidValue) throw Error(HG_ERR_INVALID, "unsupported head_dim / GQA group");
     HG_CUDA(err);

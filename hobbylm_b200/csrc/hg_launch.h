@@ -21,6 +21,7 @@ void launch_moe_combine(const Dims& D, const DecodeBufs& B, float* y_out, cudaSt
 void launch_quant_rows(const float* x, int rows, int cols, int8_t* q, float* s, cudaStream_t st);
 int attn_grid(int T, int nkv, int max_chunks);
 cudaError_t launch_attn_args(const AttnArgs& A, int grid, cudaStream_t st);
+cudaError_t prepare_attn(int hd, int rep);
 
 // prefill.cu
 void launch_kp_norm(float* in, const float* add, int rows, int d, const float* w, float eps, float* h_out, int8_t* q,

@@ -71,8 +71,9 @@ struct DecodeBufs {
   float* act;              // [T][act_stride] SwiGLU activations per (token, slot)
   int act_stride;          // floats per token (max(dense_ffn, (k + 1) * expert_ffn))
   float* y;                // [T][k + 1][d] expert outputs per (token, slot)
-  float* part;             // [T][nh][max_chunks][hd + 2] attention partials
-  int32_t* cnt;            // [T][nkv] attention arrival counters (zero between steps)
+  float* S;                // [T][nh][s_stride] attention scores / exp weights
+  long long s_stride;
+  float* cmax;             // [T][nh][max_chunks] chunk maxima of the scores
   int max_chunks;
   float* logits;           // [T][vocab] or null
   unsigned long long* amax;// [T]
@@ -96,8 +97,9 @@ struct AttnArgs {
   float* k_pool;
   float* v_pool;
   long long page_stride;
-  float* part;
-  int32_t* cnt;
+  float* S;        // [T][nh][s_stride] scores, then exp(score - max)
+  long long s_stride;  // >= max_pos, multiple of 16
+  float* cmax;     // [T][nh][max_chunks] chunk maxima of the scores
   float* out;      // [T][nh*hd] or null
   int8_t* qo;      // [T][nh*hd] or null
   float* so;       // [T][ss(nh*hd/32)]
