@@ -1,0 +1,433 @@
+#!/usr/bin/env python
+"""Decode throughput of the hobbylm_b200 engine (the hobby-rs decode path on B200).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
+
+Workload (the headline): the 500M preset, random-init seed 0, Q8_0 GGUF
+(context_length 16384 so prompt + decode fits), 256 sequences with prompt lengths ~ U[1024, 8192]
+of random ids (torch.Generator seed 5). Sequences are sharded round-robin over the ranks with
+replicated weights and no collective on the decode path (strong scaling: the 256 are fixed). A step
+is one batched greedy decode step of every sequence; value = tokens of all ranks / max-over-ranks
+device time. At N=1 the line also carries config 4 (bs1: 2048-token prompt seed 4, 512 greedy
+steps) under "bs1". The reference arm (--impl reference) times the CPU oracle (a C++ restatement
+of hobby-rs, which cannot be built here) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s (bs1, bs256) 500M Q8_0 at 1/2/4/8 B200; HBM GB/s vs ~8 TB/s"
+N_SEQS = 256
+CTX = 16384
+VALID = 50257
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=32)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-bs1", action="store_true", help="skip the config-4 bs1 sub-measurement")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--seqs", type=int, default=N_SEQS, help=argparse.SUPPRESS)
+    return ap.parse_args()
+
+
+def workload(n_seqs: int = N_SEQS, seed: int = 5):
+    """Prompt lengths ~ U[1024, 8192] and ids ~ U[0, 50257) from torch.Generator(seed)."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(1024, 8193, (n_seqs,), generator=g).tolist()
+    prompts = [torch.randint(0, VALID, (n,), generator=g).numpy().astype("uint32") for n in lens]
+    return prompts
+
+
+def shard(n: int, rank: int, world: int) -> list[int]:
+    """Round-robin assignment of sequence indices to ranks (no collective on the decode path)."""
+    return list(range(rank, n, world))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200", "-i", str(device)], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        self.f.seek(0)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        os.unlink(self.f.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        from datetime import timedelta
+
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=timedelta(seconds=900))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def reduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def reduce_sum(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def model_path(rank: int, world: int) -> str:
+    from hobbylm_b200 import synth
+
+    if rank == 0:
+        p = synth.cached_model("500M", 0, context_length=CTX)
+    barrier(world)
+    if rank != 0:
+        p = synth.cached_model("500M", 0, context_length=CTX)
+    return p
+
+
+def kv_bytes_per_pos(cfg) -> int:
+    return cfg["n_layers"] * 2 * cfg["n_kv_heads"] * cfg["head_dim"] * 4
+
+
+def weight_bytes_per_token(cfg) -> int:
+    """Algorithmic weight bytes one bs1 token streams: int8 + f32 scale per 32 of every matrix a
+    token touches (attention, dense layers, k routed + shared experts, lm_head) + the f32 router."""
+    d, f, df, L, nd = cfg["d_model"], cfg["expert_ffn"], cfg["dense_ffn"], cfg["n_layers"], cfg["n_dense"]
+    qd, kvd = cfg["n_heads"] * cfg["head_dim"], cfg["n_kv_heads"] * cfg["head_dim"]
+    k, nsh, ne, V = cfg["top_k"], cfg["n_shared"], cfg["n_experts"], cfg["vocab_size"]
+    q8 = lambda r, c: r * c * 1.125  # int8 + one f32 scale per 32
+    per_layer_attn = q8(qd + 2 * kvd, d) + q8(d, qd)
+    dense = q8(2 * df, d) + q8(d, df)
+    expert = q8(2 * f, d) + q8(d, f)
+    moe = (k + nsh) * expert + ne * d * 4
+    return int(L * per_layer_attn + nd * dense + (L - nd) * moe + q8(V, d))
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    from hobbylm_b200 import Engine, synth
+
+    rank, world, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    path = model_path(rank, world)
+    prompts_all = workload(args.seqs)
+    mine = shard(len(prompts_all), rank, world)
+    prompts = [prompts_all[i] for i in mine]
+    n_local = len(prompts)
+    total_steps = args.warmup + 2 * args.steps + 2
+    pool = sum(len(p) + total_steps + 32 for p in prompts)
+    eng = Engine.load(path, device=local, max_batch=max(n_local, 1), kv_pool_tokens=pool)
+    cfg = eng.cfg
+    t0 = time.time()
+    caches, toks = [], []
+    for p in prompts:
+        c = eng.new_cache()
+        lg = eng.prefill(c, p)
+        lg[VALID:] = -np.inf
+        caches.append(c)
+        toks.append(int(np.argmax(lg)))
+    prefill_s = time.time() - t0
+    stream = torch.cuda.ExternalStream(eng.stream(), device=local)
+    # warm-up (captures the step graph)
+    if args.warmup:
+        out = eng.decode_greedy(caches, toks, args.warmup)
+        toks = [int(v) for v in out[-1]]
+    kernels_per_step = eng.decode_kernel_count(n_local)
+    ctx_start = [c.len for c in caches]
+    # ---- timed: K steps driven on the device (inputs resident in HBM) ----
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    out = eng.decode_greedy(caches, toks, args.steps, want_ids=True)
+    ev1.record(stream)
+    ev1.synchronize()
+    clk = clocks.stop()
+    torch.cuda.synchronize()
+    barrier(world)
+    dev_s = ev0.elapsed_time(ev1) / 1e3
+    toks = [int(v) for v in out[-1]]
+    max_s = reduce_max(dev_s, world)
+    total_tokens = reduce_sum(n_local * args.steps, world)
+    value = total_tokens / max_s
+    # ---- e2e: the same steps through the per-step C-ABI call with host buffers ----
+    barrier(world)
+    torch.cuda.synchronize()
+    w0 = time.perf_counter()
+    for _ in range(args.steps):
+        nxt, _ = eng.decode_batch(caches, toks)
+        toks = [int(v) for v in nxt]
+    torch.cuda.synchronize()
+    e2e_s = reduce_max(time.perf_counter() - w0, world)
+    # ---- attention roofline (the dominant kernels) on this step's state ----
+    ms_s, ms_o = eng.time_attention(caches, iters=5)
+    ctx_now = [c.len for c in caches]
+    kvd = cfg["n_kv_heads"] * cfg["head_dim"]
+    kv_bytes = sum(2 * n * kvd * 4 for n in ctx_now)  # K + V read by one layer's attention
+    hbm, peak_kind = peaks()
+    att_gbs = kv_bytes / ((ms_s + ms_o) / 1e3) / 1e9
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "attention_traffic.json")
+    if os.path.exists(tf):
+        with open(tf) as f:
+            tr = json.load(f)
+        # captured on a smaller case; bytes scale with the positions read
+        traffic = tr["bytes_per_position"] * sum(ctx_now)
+    res = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(max_s / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8 dot / f32",
+        "data": "synthetic (random-init seed-0 weights, random prompt ids)",
+        "config": {"workload": "config5: 500M Q8_0, 256 seqs, prompts U[1024,8192] seed 5, greedy decode",
+                   "global_batch": args.seqs, "seqs_per_gpu": n_local, "parallelism": f"seq-shard x{world}",
+                   "context_at_start": {"min": min(reduce_min_list(ctx_start, world)),
+                                        "mean": sum(ctx_start) / max(n_local, 1)},
+                   "l2": "inputs larger than L2 (KV cache ~60 GB)", "prefill_s_rank0": round(prefill_s, 1)},
+        "e2e": {"value": round(total_tokens / e2e_s, 1), "unit": "tok/s",
+                "h2d_bytes_per_step": int(reduce_sum(n_local * 12, world)),
+                "d2h_bytes_per_step": int(reduce_sum(n_local * 8 + 4, world))},
+        "roofline": {"bound": "hbm", "kernel": "attention (k_attn_scores + k_attn_out), one layer",
+                     "achieved": round(att_gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(att_gbs / hbm, 4), "peak_kind": peak_kind,
+                     "traffic": traffic, "ms_scores": round(ms_s, 4), "ms_out": round(ms_o, 4),
+                     "algorithmic_bytes": kv_bytes},
+        "clocks": clk,
+        "gpu_launches": int(reduce_sum(kernels_per_step * args.steps, world)),
+    }
+    if world == 1 and not args.no_bs1:
+        res["bs1"] = run_bs1(eng_path=path, local=local)
+    if world == 1 and not args.no_cpu and rank == 0:
+        res["cpu_baseline"] = cpu_sample(path, prompts_all, steps=4, n_sample=2)
+    for c in caches:
+        c.close()
+    eng.close()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def reduce_min_list(v, world):
+    return [min(v)] if v else [0]
+
+
+def run_bs1(eng_path: str, local: int, prompt_len: int = 2048, steps: int = 512) -> dict:
+    """Config 4: 500M, bs1, 2048-token prompt (seed 4), 512 greedy steps (device-driven)."""
+    import numpy as np
+    import torch
+
+    from hobbylm_b200 import Engine, synth
+
+    eng = Engine.load(eng_path, device=local, max_batch=1, kv_pool_tokens=prompt_len + steps + 64)
+    cfg = eng.cfg
+    with eng.new_cache() as kv:
+        lg = eng.prefill(kv, synth.prompt_ids(prompt_len, 4))
+        lg[VALID:] = -np.inf
+        tok = int(np.argmax(lg))
+        out = eng.decode_greedy([kv], [tok], 8)
+        tok = int(out[-1][0])
+        n0 = kv.len
+        stream = torch.cuda.ExternalStream(eng.stream(), device=local)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        eng.decode_greedy([kv], [tok], steps, want_ids=False)
+        e1.record(stream)
+        e1.synchronize()
+        s = e0.elapsed_time(e1) / 1e3
+        n1 = kv.len
+    eng.close()
+    mean_ctx = (n0 + n1) / 2
+    bytes_tok = weight_bytes_per_token(cfg) + kv_bytes_per_pos(cfg) * (mean_ctx + 1)
+    hbm, kind = peaks()
+    gbs = bytes_tok * steps / s / 1e9
+    return {"workload": "config4: 500M Q8_0 bs1, 2048-token prompt seed 4, 512 greedy steps",
+            "tok_s": round(steps / s, 1), "us_per_token": round(s / steps * 1e6, 1),
+            "algorithmic_bytes_per_token": int(bytes_tok), "achieved_gbs": round(gbs, 1),
+            "roofline_frac": round(gbs / hbm, 4), "peak_kind": kind}
+
+
+def cpu_sample(path: str, prompts_all, steps: int = 4, n_sample: int = 2) -> dict:
+    """The CPU oracle (hobby-rs restated, OpenMP over output rows like rayon) decoding `steps`
+    tokens for `n_sample` sequences of the workload. Their prompt K/V are synthetic (random) rows:
+    the decode cost depends only on the context length, and a CPU prefill of these prompts would
+    take minutes."""
+    import numpy as np
+
+    import oracle
+
+    ora = oracle.Engine(path, quant=True)
+    kvd = ora.cfg["n_kv_heads"] * ora.cfg["head_dim"]
+    rng = np.random.default_rng(0)
+    tot_s, tot_tok, ctxs = 0.0, 0, []
+    for p in prompts_all[:n_sample]:
+        c = ora.new_cache()
+        n = len(p)
+        c.fill(rng.standard_normal((n, kvd)).astype(np.float32), rng.standard_normal((n, kvd)).astype(np.float32))
+        tok = int(p[-1])
+        for i in range(steps):
+            t = time.perf_counter()
+            lg = ora.forward(c, tok, n + i)
+            tot_s += time.perf_counter() - t
+            tot_tok += 1
+            lg[VALID:] = -np.inf
+            tok = int(np.argmax(lg))
+        ctxs.append(n)
+        c.close()
+    ora.close()
+    return {"value": round(tot_tok / tot_s, 2), "unit": "tok/s", "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"{n_sample} sequences x {steps} decode tokens at contexts {ctxs} (synthetic prompt KV), "
+                      f"500M Q8_0, sequential like hobby-rs"}
+
+
+def run_reference(args):
+    """The reference arm: the CPU oracle on the host cores, rank 0 only."""
+    rank, world, local = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), 0
+    if rank != 0:
+        return
+    import numpy as np
+
+    import oracle
+    from hobbylm_b200 import synth
+
+    path = synth.cached_model("500M", 0, context_length=CTX)
+    prompts_all = workload(args.seqs)
+    ora = oracle.Engine(path, quant=True)
+    kvd = ora.cfg["n_kv_heads"] * ora.cfg["head_dim"]
+    rng = np.random.default_rng(0)
+    sample = prompts_all[:2]
+    caches, toks = [], []
+    for p in sample:
+        c = ora.new_cache()
+        n = len(p)
+        c.fill(rng.standard_normal((n, kvd)).astype(np.float32), rng.standard_normal((n, kvd)).astype(np.float32))
+        caches.append(c)
+        toks.append(int(p[-1]))
+
+    def step():
+        for i, c in enumerate(caches):
+            lg = ora.forward(c, toks[i], len(c))
+            lg[VALID:] = -np.inf
+            toks[i] = int(np.argmax(lg))
+
+    for _ in range(args.warmup):
+        step()
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    s = time.perf_counter() - t
+    v = len(sample) * args.steps / s
+    res = {"metric": METRIC, "value": round(v, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(s / args.steps * 1e3, 2), "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": "int8 dot / f32", "impl": "reference",
+           "data": "synthetic", "config": {"workload": "config5 sample: the first 2 of the 256 sequences",
+                                          "global_batch": args.seqs},
+           "cpu_baseline": {"value": round(v, 2), "unit": "tok/s", "cores": oracle.num_threads(), "kind": "port",
+                            "sample": f"2 sequences (contexts {[len(p) for p in sample]}, synthetic prompt KV) "
+                                      f"x {args.steps} steps; hobby-rs serves sequences one after another"},
+           "e2e": {"value": round(v, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(res), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -24,6 +24,7 @@ EXPORTS = (
     "hg_seq_len", "hg_prefill", "hg_forward", "hg_decode_batch", "hg_generate", "hg_debug_last_routing",
     "hg_q8_pack", "hg_q8_scale_stride", "hg_q8_unpack_qs", "hg_op_q8_matvec", "hg_op_q8_matmul",
     "hg_op_moe_scratch_bytes", "hg_op_moe_ffn", "hg_op_kv_attn_scratch_bytes", "hg_op_kv_attn", "hg_rope_tables",
+    "hg_decode_greedy", "hg_engine_stream", "hg_decode_kernel_count", "hg_debug_time_attention",
 )
 
 
@@ -111,6 +112,10 @@ def lib():
         "hg_op_kv_attn_scratch_bytes": (sz, [C.POINTER(KvAttnArgs)]),
         "hg_op_kv_attn": (i32, [C.POINTER(KvAttnArgs), vp, vp]),
         "hg_rope_tables": (i32, [i32, i32, f32, vp, vp]),
+        "hg_decode_greedy": (i32, [vp, vp, i32, vp, i32, vp]),
+        "hg_engine_stream": (vp, [vp]),
+        "hg_decode_kernel_count": (i32, [vp, i32]),
+        "hg_debug_time_attention": (i32, [vp, vp, i32, i32, C.POINTER(f32), C.POINTER(f32)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

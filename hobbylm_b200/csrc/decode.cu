@@ -501,9 +501,20 @@ __device__ __forceinline__ void norm_rope_warp(const float* src, const float* w,
   __syncwarp();
 }
 
-// item prefix over tokens: items(t) = nchunks(t) * nkv (positions beyond max_pos raise an error)
-__device__ inline int attn_item_prefix(const AttnArgs& A, int* prefix_s) {
+// Work split of k_attn_scores: each item is (token, kv head, run of G consecutive chunks) with G
+// chosen so the items roughly fill the grid. prefix_s[t] = first item of token t; returns the
+// item count and writes G to *g_out. Positions beyond max_pos raise an error.
+__device__ inline int attn_item_prefix(const AttnArgs& A, int* prefix_s, int* g_s) {
   if (threadIdx.x == 0) {
+    long long chunks = 0;
+    for (int t = 0; t < A.T; t++) {
+      int p = A.pos[t];
+      int nch = (p + 1 + ATT_CHUNK - 1) / ATT_CHUNK;
+      if (p >= 0 && p < A.max_pos && nch <= A.max_chunks) chunks += nch;
+    }
+    long long want = (long long)gridDim.x;
+    int G = (int)((chunks * A.nkv + want - 1) / want);
+    G = G < 1 ? 1 : G;
     int acc = 0;
     prefix_s[0] = 0;
     for (int t = 0; t < A.T; t++) {
@@ -513,9 +524,10 @@ __device__ inline int attn_item_prefix(const AttnArgs& A, int* prefix_s) {
         nch = 0;
         if (A.err) atomicExch(A.err, HG_ERR_CONTEXT);
       }
-      acc += nch * A.nkv;
+      acc += ((nch + G - 1) / G) * A.nkv;
       prefix_s[t + 1] = acc;
     }
+    *g_s = G;
   }
   __syncthreads();
   return prefix_s[A.T];
@@ -528,8 +540,10 @@ __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
   __shared__ __align__(16) float knew_s[HD];
   __shared__ float wmax_s[8][REP];
   __shared__ int prefix_s[257];
+  __shared__ int g_s;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total = attn_item_prefix(A, prefix_s);
+  const int total = attn_item_prefix(A, prefix_s, &g_s);
+  const int G = g_s;
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
   for (int item = blockIdx.x; item < total; item += gridDim.x) {
     int lo = 0, hi = A.T - 1;
@@ -539,15 +553,16 @@ __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
       else hi = mid - 1;
     }
     const int t = lo, rem = item - prefix_s[t];
-    const int kvh = rem % A.nkv, c = rem / A.nkv;
+    const int kvh = rem % A.nkv, cg = rem / A.nkv;
     const int pos = A.pos[t], n = pos + 1;
+    const int nch = (n + ATT_CHUNK - 1) / ATT_CHUNK;
+    const int cbeg = cg * G, cend = min(nch, cbeg + G);
     const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
     const float* qkv = A.qkv + (size_t)t * A.qkv_stride;
     const int qd = A.nh * HD, kvd = A.nkv * HD;
     const float* cs = A.rope_cos + (size_t)pos * (HD / 2);
     const float* sn = A.rope_sin + (size_t)pos * (HD / 2);
-    const int c0 = c * ATT_CHUNK;
-    const bool has_new = pos >= c0 && pos < c0 + ATT_CHUNK;
+    const bool has_new = (pos / ATT_CHUNK) >= cbeg && (pos / ATT_CHUNK) < cend;
     __syncthreads();
     if (warp < REP) norm_rope_warp<HD>(qkv + (kvh * REP + warp) * HD, A.q_norm, A.eps, cs, sn, q_s[warp]);
     if (has_new) {
@@ -568,42 +583,46 @@ __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
     for (int h = 0; h < REP; h++)
 #pragma unroll
       for (int i = 0; i < E; i++) qreg[h][i] = q_s[h][32 * i + lane];
-    float mx[REP];
-#pragma unroll
-    for (int h = 0; h < REP; h++) mx[h] = -INFINITY;
     float* srow = A.S + ((size_t)t * A.nh + kvh * REP) * A.s_stride;
+    for (int c = cbeg; c < cend; c++) {
+      const int c0 = c * ATT_CHUNK;
+      float mx[REP];
+#pragma unroll
+      for (int h = 0; h < REP; h++) mx[h] = -INFINITY;
 #pragma unroll 2
-    for (int i8 = 0; i8 < 8; i8++) {
-      const int p = c0 + warp * 8 + i8;
-      if (p >= n) break;
-      const float* kp = p == pos ? knew_s
-                                 : A.k_pool + (long long)bt[p / PAGE] * A.page_stride +
-                                       ((long long)kvh * PAGE + (p % PAGE)) * HD;
-      float kr[E];
+      for (int i8 = 0; i8 < 8; i8++) {
+        const int p = c0 + warp * 8 + i8;
+        if (p >= n) break;
+        const float* kp = p == pos ? knew_s
+                                   : A.k_pool + (long long)bt[p / PAGE] * A.page_stride +
+                                         ((long long)kvh * PAGE + (p % PAGE)) * HD;
+        float kr[E];
 #pragma unroll
-      for (int i = 0; i < E; i++) kr[i] = kp[32 * i + lane];
+        for (int i = 0; i < E; i++) kr[i] = kp[32 * i + lane];
 #pragma unroll
-      for (int h = 0; h < REP; h++) {
-        // ops::dot: lane = 8m + l accumulates elements 32i + lane (FMA, i ascending), then
-        // (a0+a1)+(a2+a3) per SIMD lane and the 8-lane tree
-        float acc = 0.0f;
+        for (int h = 0; h < REP; h++) {
+          // ops::dot: lane = 8m + l accumulates elements 32i + lane (FMA, i ascending), then
+          // (a0+a1)+(a2+a3) per SIMD lane and the 8-lane tree
+          float acc = 0.0f;
 #pragma unroll
-        for (int i = 0; i < E; i++) acc = __fmaf_rn(qreg[h][i], kr[i], acc);
-        acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 8));
-        acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 16));
-        float sc = fmul(hsum8_group(acc), scale);
-        if (lane == 0) srow[(size_t)h * A.s_stride + p] = sc;
-        mx[h] = fmaxf(mx[h], sc);
+          for (int i = 0; i < E; i++) acc = __fmaf_rn(qreg[h][i], kr[i], acc);
+          acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 8));
+          acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 16));
+          float sc = fmul(hsum8_group(acc), scale);
+          if (lane == 0) srow[(size_t)h * A.s_stride + p] = sc;
+          mx[h] = fmaxf(mx[h], sc);
+        }
       }
-    }
-    if (lane == 0)
+      if (lane == 0)
 #pragma unroll
-      for (int h = 0; h < REP; h++) wmax_s[warp][h] = mx[h];
-    __syncthreads();
-    if (threadIdx.x < REP) {
-      float m = -INFINITY;
-      for (int w = 0; w < 8; w++) m = fmaxf(m, wmax_s[w][threadIdx.x]);
-      A.cmax[((size_t)t * A.nh + kvh * REP + threadIdx.x) * A.max_chunks + c] = m;
+        for (int h = 0; h < REP; h++) wmax_s[warp][h] = mx[h];
+      __syncthreads();
+      if (threadIdx.x < REP) {
+        float m = -INFINITY;
+        for (int w = 0; w < 8; w++) m = fmaxf(m, wmax_s[w][threadIdx.x]);
+        A.cmax[((size_t)t * A.nh + kvh * REP + threadIdx.x) * A.max_chunks + c] = m;
+      }
+      __syncthreads();
     }
   }
 }
@@ -707,40 +726,68 @@ __global__ void __launch_bounds__(REP * HD) k_attn_out(AttnArgs A) {
   __syncthreads();
   const float inv = inv_s[h];
   const float* erow = srow + (size_t)h * A.s_stride;
-  // o[h][di] = sum_j (e_j * inv) * v_j[di], sequential in j
+  // o[h][di] = sum_j (e_j * inv) * v_j[di], sequential in j. Positions go in groups of 32 (two
+  // pages); lane i of each warp holds e of position 32g + i, prefetched EPF groups ahead so the
+  // L2 latency stays off the add chain.
+  constexpr int EPF = 4;
+  const int ngroups = (n + 31) / 32;
+  float epf[EPF];
+#pragma unroll
+  for (int k = 0; k < EPF; k++) {
+    const int j = 32 * k + lane;
+    epf[k] = (k < ngroups && j < n) ? erow[j] : 0.0f;
+  }
   float acc = 0.0f;
-  float e_next = lane < PAGE && lane < n ? erow[lane] : 0.0f;
-  int p = 0;
-  for (; p < npages; p++) {
-    const int st = p % ATT_STAGES;
-    const uint32_t parity = (uint32_t)(p / ATT_STAGES) & 1u;
-    const float e_cur = e_next;
-    const int jn = p * PAGE + PAGE + lane;
-    e_next = (lane < PAGE && jn < n) ? erow[jn] : 0.0f;
-    if (!mbar_wait(&bar[st], parity)) {
-      if (lane == 0) atomicExch(&fail_s, 1);
+  int p = 0;  // next page to wait for
+  for (int g = 0; g < ngroups; g++) {
+    const float e_cur = epf[0];
+#pragma unroll
+    for (int k = 0; k < EPF - 1; k++) epf[k] = epf[k + 1];
+    {
+      const int j = 32 * (g + EPF) + lane;
+      epf[EPF - 1] = j < n ? erow[j] : 0.0f;
     }
-    const float* vs = reinterpret_cast<const float*>(ring + (size_t)st * PAGE_BYTES);
-    const int rows = min(PAGE, n - p * PAGE);
-    for (int r = 0; r < rows; r++) {
-      const float pr = fmul(__shfl_sync(0xffffffffu, e_cur, r), inv);
-      acc = fadd(acc, fmul(pr, vs[r * HD + di]));
+    const float pr = fmul(e_cur, inv);
+    const int p0 = 2 * g, p1 = min(2 * g + 1, npages - 1);
+    bool ok = mbar_wait(&bar[p0 % ATT_STAGES], (uint32_t)(p0 / ATT_STAGES) & 1u);
+    if (p1 != p0) ok = mbar_wait(&bar[p1 % ATT_STAGES], (uint32_t)(p1 / ATT_STAGES) & 1u) && ok;
+    if (!ok && lane == 0) atomicExch(&fail_s, 1);
+    const float* v0 = reinterpret_cast<const float*>(ring + (size_t)(p0 % ATT_STAGES) * PAGE_BYTES) + di;
+    const float* v1 = reinterpret_cast<const float*>(ring + (size_t)(p1 % ATT_STAGES) * PAGE_BYTES) + di;
+    const int rows = min(32, n - 32 * g);
+    if (rows == 32) {
+      float pv[32], vv[32];
+#pragma unroll
+      for (int r = 0; r < 32; r++) {
+        pv[r] = __shfl_sync(0xffffffffu, pr, r);
+        vv[r] = r < 16 ? v0[r * HD] : v1[(r - 16) * HD];
+      }
+#pragma unroll
+      for (int r = 0; r < 32; r++) acc = fadd(acc, fmul(pv[r], vv[r]));
+    } else {
+      for (int r = 0; r < rows; r++) {
+        const float pj = __shfl_sync(0xffffffffu, pr, r);
+        acc = fadd(acc, fmul(pj, r < 16 ? v0[r * HD] : v1[(r - 16) * HD]));
+      }
     }
+    p = p1 + 1;
     __syncthreads();
     if (fail_s) break;
-    if (tid == 0 && p + ATT_STAGES < npages) {
-      const int q = p + ATT_STAGES;
-      mbar_expect_tx(&bar[st], PAGE_BYTES);
-      bulk_g2s(ring + (size_t)st * PAGE_BYTES, vbase + (long long)bt[q] * A.page_stride, PAGE_BYTES, &bar[st]);
+    if (tid == 0) {  // refill the two stages just released
+      for (int q = p0 + ATT_STAGES; q <= p1 + ATT_STAGES && q < npages; q++) {
+        const int st = q % ATT_STAGES;
+        mbar_expect_tx(&bar[st], PAGE_BYTES);
+        bulk_g2s(ring + (size_t)st * PAGE_BYTES, vbase + (long long)bt[q] * A.page_stride, PAGE_BYTES, &bar[st]);
+      }
     }
   }
   if (fail_s) {
-    // a bulk copy did not complete in time: report, then wait (bounded) for the pages still in
-    // flight (p .. p + ATT_STAGES - 1) so no copy lands in shared memory after this CTA exits
+    // a bulk copy did not complete in time: report, then wait (bounded) for the pages that may
+    // still be in flight so no copy lands in shared memory after this CTA exits
     if (tid == 0) {
       if (A.err) atomicExch(A.err, HG_ERR_TIMEOUT);
-      for (int q = p; q < p + ATT_STAGES && q < npages; q++)
-        mbar_wait(&bar[q % ATT_STAGES], (uint32_t)(q / ATT_STAGES) & 1u);
+      for (int q = p - 2; q < p + ATT_STAGES && q < npages; q++)
+        if (q >= 0) mbar_wait(&bar[q % ATT_STAGES], (uint32_t)(q / ATT_STAGES) & 1u);
     }
     __syncthreads();
     return;
@@ -757,6 +804,31 @@ __global__ void __launch_bounds__(REP * HD) k_attn_out(AttnArgs A) {
     if (lane == 0) A.so[(size_t)t * q8_ss(nbq) + ((hg * HD + di) >> 5)] = dq;
   }
   (void)NW;
+}
+
+// ------------------------------------------------------------------------------------------
+// Greedy feedback at the end of a decode step: each token's masked argmax (sample.rs:53-64)
+// becomes its next input, the position advances, and the id is stored in a ring of generated ids
+// (gen[(step % gen_cap) * T + t]) whose step counter lives in device memory.
+// ------------------------------------------------------------------------------------------
+__global__ void k_feedback(DecodeBufs B, int32_t* tok, int32_t* pos, int32_t* gen, int gen_cap, int32_t* step) {
+  const int t = threadIdx.x;
+  const int s = *step;
+  __syncthreads();
+  if (t < B.T) {
+    const unsigned long long key = B.amax[t];
+    const int32_t next = (int32_t)(0xffffffffu - (uint32_t)(key & 0xffffffffull));
+    tok[t] = next;
+    pos[t] = pos[t] + 1;
+    gen[(size_t)(s % gen_cap) * B.T + t] = next;
+  }
+  __syncthreads();
+  if (t == 0) *step = s + 1;
+}
+
+void launch_feedback(const DecodeBufs& B, int32_t* tok, int32_t* pos, int32_t* gen, int gen_cap, int32_t* step,
+                     cudaStream_t st) {
+  k_feedback<<<1, 256, 0, st>>>(B, tok, pos, gen, gen_cap, step);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -871,12 +943,27 @@ int attn_grid(int T, int nkv, int max_chunks) {
 }
 
 template <int HD, int REP>
-static cudaError_t launch_attn_t(const AttnArgs& A, int grid, cudaStream_t st) {
-  k_attn_scores<HD, REP><<<grid, 256, 0, st>>>(A);
+static cudaError_t launch_attn_t(const AttnArgs& A, int grid, cudaStream_t st, int which) {
+  if (which & 1) k_attn_scores<HD, REP><<<grid, 256, 0, st>>>(A);
   const size_t smem = (size_t)ATT_STAGES * PAGE * HD * 4;
-  k_attn_out<HD, REP><<<A.T * A.nkv, REP * HD, smem, st>>>(A);
+  if (which & 2) k_attn_out<HD, REP><<<A.T * A.nkv, REP * HD, smem, st>>>(A);
   return cudaGetLastError();
 }
+
+static cudaError_t launch_attn_which(const AttnArgs& A, int grid, cudaStream_t st, int which) {
+  int rep = A.nh / A.nkv;
+  if (A.hd == 128 && rep == 4) return launch_attn_t<128, 4>(A, grid, st, which);
+  if (A.hd == 64 && rep == 4) return launch_attn_t<64, 4>(A, grid, st, which);
+  if (A.hd == 128 && rep == 2) return launch_attn_t<128, 2>(A, grid, st, which);
+  if (A.hd == 64 && rep == 2) return launch_attn_t<64, 2>(A, grid, st, which);
+  if (A.hd == 128 && rep == 1) return launch_attn_t<128, 1>(A, grid, st, which);
+  if (A.hd == 64 && rep == 1) return launch_attn_t<64, 1>(A, grid, st, which);
+  return cudaErrorInvalidValue;
+}
+cudaError_t launch_attn_scores_only(const AttnArgs& A, int grid, cudaStream_t st) {
+  return launch_attn_which(A, grid, st, 1);
+}
+cudaError_t launch_attn_out_only(const AttnArgs& A, cudaStream_t st) { return launch_attn_which(A, 1, st, 2); }
 
 // Opt in to the ring's dynamic shared memory on the current device (call before any launch or
 // graph capture).
@@ -894,16 +981,7 @@ cudaError_t prepare_attn(int hd, int rep) {
   return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_attn_args(const AttnArgs& A, int grid, cudaStream_t st) {
-  int rep = A.nh / A.nkv;
-  if (A.hd == 128 && rep == 4) return launch_attn_t<128, 4>(A, grid, st);
-  if (A.hd == 64 && rep == 4) return launch_attn_t<64, 4>(A, grid, st);
-  if (A.hd == 128 && rep == 2) return launch_attn_t<128, 2>(A, grid, st);
-  if (A.hd == 64 && rep == 2) return launch_attn_t<64, 2>(A, grid, st);
-  if (A.hd == 128 && rep == 1) return launch_attn_t<128, 1>(A, grid, st);
-  if (A.hd == 64 && rep == 1) return launch_attn_t<64, 1>(A, grid, st);
-  return cudaErrorInvalidValue;
-}
+cudaError_t launch_attn_args(const AttnArgs& A, int grid, cudaStream_t st) { return launch_attn_which(A, grid, st, 3); }
 
 void launch_quant_rows(const float* x, int rows, int cols, int8_t* q, float* s, cudaStream_t st) {
   k_quant_rows<<<rows, 256, 0, st>>>(x, cols, q, s);

@@ -93,6 +93,9 @@ struct hg_engine {
   unsigned long long* h_amax = nullptr;  // pinned [max_batch]
   int32_t* h_err = nullptr;    // pinned
   std::map<int, cudaGraphExec_t> graphs;
+  std::map<int, int> graph_kernels;  // kernel nodes per step graph
+  int32_t* d_gen = nullptr;          // [GEN_CAP][max_batch] generated ids ring
+  int32_t* d_step = nullptr;         // ring step counter
   // prefill buffers
   int pf_rows = 0;
   struct Pf {
@@ -101,7 +104,7 @@ struct hg_engine {
     float *sa, *sact;
     int32_t *ids, *sel, *ecount, *elist, *a_idx, *o_idx, *gm, *go, *gc;
   } pf{};
-  int pf_tq = 256;
+  int pf_tq = 1024;
   std::vector<int32_t> last_sel;  // [n_layers][max_batch][k] from the last decode step
   int last_T = 0;
   size_t device_bytes() const { return weights.cap + work.cap; }
@@ -116,6 +119,8 @@ struct hg_seq {
 };
 
 namespace {
+
+constexpr int GEN_CAP = 64;
 
 template <class T>
 T* dev_alloc(Arena& a, size_t n) {
@@ -256,6 +261,8 @@ void alloc_work(hg_engine* e) {
   P.gm = a.take<int32_t>(ne);
   P.go = a.take<int32_t>(ne);
   P.gc = a.take<int32_t>(ne);
+  e->d_gen = a.take<int32_t>((size_t)GEN_CAP * T);
+  e->d_step = a.take<int32_t>(4);
   }
   HG_CUDA(cudaMemset(a.base, 0, a.cap));
 }
@@ -370,7 +377,7 @@ void load_engine(hg_engine* e, const char* path, const hg_engine_opts& o) {
   HG_CUDA(cudaMalloc((void**)&e->d_bt, (size_t)e->max_rows * e->bt_stride * 4));
   HG_CUDA(cudaMemset(e->d_bt, 0, (size_t)e->max_rows * e->bt_stride * 4));
   for (int r = e->max_rows - 1; r >= 0; r--) e->free_rows.push_back(r);
-  e->pf_rows = 512;
+  e->pf_rows = 1024;
   alloc_work(e);
   HG_CUDA(cudaMallocHost((void**)&e->h_meta, 3 * e->max_batch * 4));
   HG_CUDA(cudaMallocHost((void**)&e->h_amax, e->max_batch * 8));
@@ -465,17 +472,23 @@ void record_decode(hg_engine* e, const DecodeBufs& B) {
   int mode = e->layers[D.L - 1].moe ? 2 : 1;
   launch_pre_norm(D, B, mode, e->embd, e->out_norm, B.qa, B.sa, nullptr, 0, 1, st);
   launch_lmhead(D, B, e->lm, B.qa, B.sa, B.logits, st);
+  // greedy feedback for device-driven multi-step decode; host-driven steps overwrite tok/pos
+  launch_feedback(B, const_cast<int32_t*>(B.tok), const_cast<int32_t*>(B.pos), e->d_gen, GEN_CAP, e->d_step, st);
 }
 
-// One decode step for T tokens whose metadata is already in h_meta.
-void decode_step(hg_engine* e, int T) {
+DecodeBufs step_bufs(hg_engine* e, int T) {
   DecodeBufs B = e->buf;
   B.T = T;
   B.tok = e->d_meta;
   B.pos = e->d_meta + T;
   B.bt_row = e->d_meta + 2 * T;
+  return B;
+}
+
+// The step graph for T tokens (captured on first use).
+cudaGraphExec_t step_graph(hg_engine* e, int T) {
+  DecodeBufs B = step_bufs(e, T);
   cudaStream_t st = e->stream;
-  HG_CUDA(cudaMemcpyAsync(e->d_meta, e->h_meta, 3 * T * 4, cudaMemcpyHostToDevice, st));
   auto it = e->graphs.find(T);
   if (it == e->graphs.end()) {
     cudaGraph_t graph;
@@ -487,12 +500,31 @@ void decode_step(hg_engine* e, int T) {
       throw;
     }
     HG_CUDA(cudaStreamEndCapture(st, &graph));
+    size_t nodes = 0;
+    HG_CUDA(cudaGraphGetNodes(graph, nullptr, &nodes));
+    std::vector<cudaGraphNode_t> nv(nodes);
+    HG_CUDA(cudaGraphGetNodes(graph, nv.data(), &nodes));
+    int kernels = 0;
+    for (auto nd : nv) {
+      cudaGraphNodeType ty;
+      HG_CUDA(cudaGraphNodeGetType(nd, &ty));
+      kernels += ty == cudaGraphNodeTypeKernel;
+    }
     cudaGraphExec_t exec;
     HG_CUDA(cudaGraphInstantiate(&exec, graph, 0));
     cudaGraphDestroy(graph);
     it = e->graphs.emplace(T, exec).first;
+    e->graph_kernels[T] = kernels;
   }
-  HG_CUDA(cudaGraphLaunch(it->second, st));
+  return it->second;
+}
+
+// One decode step for T tokens whose metadata is already in h_meta.
+void decode_step(hg_engine* e, int T) {
+  DecodeBufs B = step_bufs(e, T);
+  cudaStream_t st = e->stream;
+  HG_CUDA(cudaMemcpyAsync(e->d_meta, e->h_meta, 3 * T * 4, cudaMemcpyHostToDevice, st));
+  HG_CUDA(cudaGraphLaunch(step_graph(e, T), st));
   HG_CUDA(cudaMemcpyAsync(e->h_amax, B.amax, T * 8, cudaMemcpyDeviceToHost, st));
   HG_CUDA(cudaMemcpyAsync(e->h_err, B.err, 4, cudaMemcpyDeviceToHost, st));
   e->last_T = T;
@@ -552,6 +584,45 @@ void decode_batch(hg_engine* e, hg_seq** seqs, int n, const uint32_t* tokens, ui
     seqs[i]->len += 1;
     if (next) next[i] = amax_index(e->h_amax[i]);
   }
+}
+
+// K greedy steps for n sequences, driven on the device: the step graph is replayed back to back
+// and its feedback kernel turns each argmax into the next input token.
+void decode_greedy(hg_engine* e, hg_seq** seqs, int n, const uint32_t* tokens, int steps, uint32_t* out_ids) {
+  if (n <= 0 || n > e->max_batch) throw Error(HG_ERR_INVALID, "batch size out of range (max_batch)");
+  if (steps <= 0) return;
+  for (int i = 0; i < n; i++) {
+    if (!seqs[i] || seqs[i]->e != e) throw Error(HG_ERR_INVALID, "sequence does not belong to this engine");
+    for (int j = 0; j < i; j++)
+      if (seqs[j] == seqs[i]) throw Error(HG_ERR_INVALID, "a sequence appears twice in one batch");
+    if ((int64_t)tokens[i] >= e->cfg.vocab_size) throw Error(HG_ERR_TOKEN, "token id out of range");
+    if (seqs[i]->len + steps > seqs[i]->max_ctx) throw Error(HG_ERR_CONTEXT, "steps exceed the sequence's max context");
+    ensure_pages(seqs[i], seqs[i]->len + steps);
+  }
+  for (int i = 0; i < n; i++) {
+    e->h_meta[i] = (int32_t)tokens[i];
+    e->h_meta[n + i] = seqs[i]->len;
+    e->h_meta[2 * n + i] = seqs[i]->row;
+  }
+  cudaStream_t st = e->stream;
+  HG_CUDA(cudaMemcpyAsync(e->d_meta, e->h_meta, 3 * n * 4, cudaMemcpyHostToDevice, st));
+  HG_CUDA(cudaMemsetAsync(e->d_step, 0, 4, st));
+  cudaGraphExec_t g = step_graph(e, n);
+  std::vector<int32_t> ring((size_t)GEN_CAP * n);
+  for (int k0 = 0; k0 < steps; k0 += GEN_CAP) {
+    const int kn = std::min(GEN_CAP, steps - k0);
+    for (int k = 0; k < kn; k++) HG_CUDA(cudaGraphLaunch(g, st));
+    if (out_ids) {
+      HG_CUDA(cudaMemcpyAsync(ring.data(), e->d_gen, ring.size() * 4, cudaMemcpyDeviceToHost, st));
+      HG_CUDA(cudaStreamSynchronize(st));
+      for (int k = 0; k < kn; k++)
+        for (int i = 0; i < n; i++) out_ids[(size_t)(k0 + k) * n + i] = (uint32_t)ring[(size_t)k * n + i];
+    }
+  }
+  HG_CUDA(cudaMemcpyAsync(e->h_err, e->buf.err, 4, cudaMemcpyDeviceToHost, st));
+  e->last_T = n;
+  finish_step(e);
+  for (int i = 0; i < n; i++) seqs[i]->len += steps;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -988,6 +1059,66 @@ int hg_generate(hg_engine* e, const uint32_t* ids, int n, const hg_gen_opts* opt
     set_last_error(ex.what());
     return HG_ERR_INVALID;
   }
+}
+
+int hg_decode_greedy(hg_engine* e, hg_seq** seqs, int n, const uint32_t* tokens, int steps, uint32_t* out_ids) {
+  HG_API_TRY({
+    need(e && seqs && tokens && steps >= 0, "bad argument");
+    DeviceGuard g(e->device);
+    decode_greedy(e, seqs, n, tokens, steps, out_ids);
+  })
+}
+
+void* hg_engine_stream(const hg_engine* e) { return e ? (void*)e->stream : nullptr; }
+
+int hg_decode_kernel_count(hg_engine* e, int n) {
+  try {
+    need(e && n > 0 && n <= e->max_batch, "bad argument");
+    DeviceGuard g(e->device);
+    step_graph(e, n);
+    return e->graph_kernels[n];
+  } catch (const ::hg::Error& ex) {
+    set_last_error(ex.what());
+    return ex.code;
+  }
+}
+
+int hg_debug_time_attention(hg_engine* e, hg_seq** seqs, int n, int iters, float* ms_scores, float* ms_out) {
+  HG_API_TRY({
+    need(e && seqs && n > 0 && n <= e->max_batch && iters > 0, "bad argument");
+    DeviceGuard g(e->device);
+    for (int i = 0; i < n; i++) {
+      need(seqs[i] && seqs[i]->e == e && seqs[i]->len > 0, "sequences must have decoded at least one step");
+      e->h_meta[i] = 0;
+      e->h_meta[n + i] = seqs[i]->len - 1;  // re-run the last step: the append rewrites the same K/V row
+      e->h_meta[2 * n + i] = seqs[i]->row;
+    }
+    cudaStream_t st = e->stream;
+    HG_CUDA(cudaMemcpyAsync(e->d_meta, e->h_meta, 3 * n * 4, cudaMemcpyHostToDevice, st));
+    DecodeBufs B = step_bufs(e, n);
+    // the qkv buffer holds the last decode step's projections of the last layer
+    AttnArgs A = make_attn_args(e, B, e->cfg.n_layers - 1);
+    const int grid = attn_grid(n, e->D.nkv, B.max_chunks);
+    cudaEvent_t ev[3];
+    for (auto& x : ev) HG_CUDA(cudaEventCreate(&x));
+    float tot_s = 0, tot_o = 0;
+    for (int it = 0; it < iters; it++) {
+      HG_CUDA(cudaEventRecord(ev[0], st));
+      HG_CUDA(launch_attn_scores_only(A, grid, st));
+      HG_CUDA(cudaEventRecord(ev[1], st));
+      HG_CUDA(launch_attn_out_only(A, st));
+      HG_CUDA(cudaEventRecord(ev[2], st));
+      HG_CUDA(cudaEventSynchronize(ev[2]));
+      float a, b;
+      HG_CUDA(cudaEventElapsedTime(&a, ev[0], ev[1]));
+      HG_CUDA(cudaEventElapsedTime(&b, ev[1], ev[2]));
+      tot_s += a;
+      tot_o += b;
+    }
+    for (auto& x : ev) cudaEventDestroy(x);
+    if (ms_scores) *ms_scores = tot_s / iters;
+    if (ms_out) *ms_out = tot_o / iters;
+  })
 }
 
 int hg_debug_last_routing(hg_engine* e, int slot, int32_t* sel) {

@@ -22,6 +22,10 @@ void launch_quant_rows(const float* x, int rows, int cols, int8_t* q, float* s, 
 int attn_grid(int T, int nkv, int max_chunks);
 cudaError_t launch_attn_args(const AttnArgs& A, int grid, cudaStream_t st);
 cudaError_t prepare_attn(int hd, int rep);
+cudaError_t launch_attn_scores_only(const AttnArgs& A, int grid, cudaStream_t st);
+cudaError_t launch_attn_out_only(const AttnArgs& A, cudaStream_t st);
+void launch_feedback(const DecodeBufs& B, int32_t* tok, int32_t* pos, int32_t* gen, int gen_cap, int32_t* step,
+                     cudaStream_t st);
 
 // prefill.cu
 void launch_kp_norm(float* in, const float* add, int rows, int d, const float* w, float eps, float* h_out, int8_t* q,

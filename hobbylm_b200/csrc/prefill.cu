@@ -266,23 +266,54 @@ __global__ void __launch_bounds__(256) kp_scores(const float* q, int qd, int t0,
   }
 }
 
-// Softmax rows (ops.rs:112-128): thread per R. Writes exp(s - max) in place and inv = 1/sum.
-__global__ void kp_softmax(float* S, int nR, int rep, int base, int t0, float* inv) {
-  int R = blockIdx.x * blockDim.x + threadIdx.x;
-  if (R >= nR) return;
-  int n = base + t0 + R / rep + 1;
+// Softmax of 32 score rows (ops.rs:112-128) per CTA of 1024 threads: the row maxima in parallel
+// (order does not matter for a max), then in chunks of 256 positions e = exp(s - max) is written
+// back in place and staged in shared memory, where lane r of warp 0 adds row r's values in
+// position order (the reference's sequential sum). inv[R] = 1 / sum.
+__global__ void __launch_bounds__(1024) kp_softmax_rows(float* S, int nR, int rep, int base, int t0, float* inv) {
+  __shared__ float ch[256][33];
+  __shared__ float mred[32][33];
+  __shared__ float m_s[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int R = blockIdx.x * 32 + lane;
+  const bool valid = R < nR;
+  const int n = valid ? base + t0 + R / rep + 1 : 0;
+  const int Rl = min(blockIdx.x * 32 + 31, nR - 1);
+  const int nmax = base + t0 + Rl / rep + 1;
   float m = -INFINITY;
-  for (int j = 0; j < n; j++) {
-    float v = S[(size_t)j * nR + R];
-    if (v > m) m = v;
+  for (int j = warp; j < nmax; j += 32)
+    if (j < n) {
+      float v = S[(size_t)j * nR + R];
+      if (v > m) m = v;
+    }
+  mred[warp][lane] = m;
+  __syncthreads();
+  if (warp == 0) {
+    float mm = -INFINITY;
+    for (int w = 0; w < 32; w++) mm = fmaxf(mm, mred[w][lane]);
+    m_s[lane] = mm;
   }
+  __syncthreads();
+  const float mrow = m_s[lane];
   float sum = 0.0f;
-  for (int j = 0; j < n; j++) {
-    float e = exp_cr(__fsub_rn(S[(size_t)j * nR + R], m));
-    S[(size_t)j * nR + R] = e;
-    sum = fadd(sum, e);
+  for (int j0 = 0; j0 < nmax; j0 += 256) {
+    for (int jj = warp; jj < 256; jj += 32) {
+      const int j = j0 + jj;
+      float e = 0.0f;
+      if (j < n) {
+        e = exp_cr(__fsub_rn(S[(size_t)j * nR + R], mrow));
+        S[(size_t)j * nR + R] = e;
+      }
+      ch[jj][lane] = e;
+    }
+    __syncthreads();
+    if (warp == 0) {  // adding the zeros past a row's end leaves its sum unchanged (sum >= +0)
+#pragma unroll 8
+      for (int jj = 0; jj < 256; jj++) sum = fadd(sum, ch[jj][lane]);
+    }
+    __syncthreads();
   }
-  inv[R] = __fdiv_rn(1.0f, sum);
+  if (warp == 0 && valid) inv[R] = __fdiv_rn(1.0f, sum);
 }
 
 // O[t][h][dd] = sum_j (e_j * inv) * v_j[dd], sequential in j (model.rs:426-432). Tile: 32 R x HD.
@@ -535,7 +566,7 @@ void launch_kp_attention(const float* q, int qd, int t0, int tq, int base, int n
     dim3 gs((nR + 31) / 32, (nmax + 31) / 32);
     if (hd == 128) kp_scores<128><<<gs, 256, 0, st>>>(q, qd, t0, tq, base, rep, g, bt, k_pool, page_stride, S, nR);
     else kp_scores<64><<<gs, 256, 0, st>>>(q, qd, t0, tq, base, rep, g, bt, k_pool, page_stride, S, nR);
-    kp_softmax<<<(nR + 127) / 128, 128, 0, st>>>(S, nR, rep, base, t0, inv);
+    kp_softmax_rows<<<(nR + 31) / 32, 1024, 0, st>>>(S, nR, rep, base, t0, inv);
     dim3 gp((nR + 31) / 32);
     if (hd == 128) kp_pv<128><<<gp, 256, 0, st>>>(S, inv, nR, rep, base, t0, g, bt, v_pool, page_stride, o, qd);
     else kp_pv<64><<<gp, 256, 0, st>>>(S, inv, nR, rep, base, t0, g, bt, v_pool, page_stride, o, qd);

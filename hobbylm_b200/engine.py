@@ -140,6 +140,30 @@ class Engine:
                                     logits.ctypes.data if want_logits else None))
         return nxt, logits
 
+    def decode_greedy(self, caches: Sequence[KvCache], tokens: Sequence[int], steps: int,
+                      want_ids: bool = True):
+        """``steps`` greedy steps for the batch, driven on the device; returns [steps][n] ids."""
+        n = len(caches)
+        arr = (C.c_void_p * n)(*[c.h.value for c in caches])
+        toks = _u32(tokens)
+        out = np.empty((steps, n), np.uint32) if want_ids else None
+        check(lib().hg_decode_greedy(self.h, arr, n, toks.ctypes.data, steps,
+                                     out.ctypes.data if want_ids else None))
+        return out
+
+    def stream(self) -> int:
+        return int(lib().hg_engine_stream(self.h) or 0)
+
+    def decode_kernel_count(self, n: int) -> int:
+        return check(lib().hg_decode_kernel_count(self.h, n))
+
+    def time_attention(self, caches: Sequence[KvCache], iters: int = 10):
+        n = len(caches)
+        arr = (C.c_void_p * n)(*[c.h.value for c in caches])
+        a, b = C.c_float(), C.c_float()
+        check(lib().hg_debug_time_attention(self.h, arr, n, iters, C.byref(a), C.byref(b)))
+        return a.value, b.value
+
     def last_routing(self, slot: int = 0) -> np.ndarray:
         sel = np.empty((self.cfg["n_layers"], self.cfg["top_k"]), np.int32)
         check(lib().hg_debug_last_routing(self.h, slot, sel.ctypes.data))

@@ -106,6 +106,23 @@ int hg_forward(hg_engine* e, hg_seq* s, uint32_t token, float* logits_or_null, u
 int hg_decode_batch(hg_engine* e, hg_seq** seqs, int n, const uint32_t* tokens, uint32_t* next_ids,
                     float* logits_or_null);
 
+/* `steps` greedy decode steps for n sequences driven on the device: each step's masked argmax is
+ * fed back as the sequence's next token without a host round trip (the multi-token form of the
+ * lib.rs:131-160 loop with temp = 0, without the EOS stop). tokens: the first step's inputs;
+ * out_ids (may be NULL): [steps][n] generated ids. */
+int hg_decode_greedy(hg_engine* e, hg_seq** seqs, int n, const uint32_t* tokens, int steps, uint32_t* out_ids);
+
+/* The engine's CUDA stream (a cudaStream_t), for callers that order or time work around it. */
+void* hg_engine_stream(const hg_engine* e);
+
+/* Kernels one decode step of batch size n launches (kernel nodes of its CUDA graph), or < 0. */
+int hg_decode_kernel_count(hg_engine* e, int n);
+
+/* Device time in ms (CUDA events on the engine stream, mean over iters) of the attention kernels
+ * of one decode step of the last layer for these sequences, re-run on their current state (each
+ * must have decoded at least one step; the K/V append rewrites the same row). */
+int hg_debug_time_attention(hg_engine* e, hg_seq** seqs, int n, int iters, float* ms_scores, float* ms_out);
+
 /* Engine::generate (lib.rs:107-162) on token ids: prefill, then per step mask ids >= 50257,
  * sample (greedy when temp <= 0), stop on EOS, stream the id, stop at context_length.
  * out_ids (may be NULL) receives up to opts->max_new ids. Returns the count (>= 0) or an error. */

@@ -30,12 +30,34 @@ def test_prefill_bitexact_config1(engine130, oracle130):
 
 
 def test_prefill_chunked_equals_whole(engine130):
-    ids = synth.prompt_ids(700, 7)  # spans two 512-row prefill chunks
+    ids = synth.prompt_ids(1300, 7)  # spans two 1024-row prefill chunks
     with engine130.new_cache() as a, engine130.new_cache() as b:
         whole = engine130.prefill(a, ids)
         engine130.prefill(b, ids[:300])
         split = engine130.prefill(b, ids[300:])
         assert np.array_equal(whole.view(np.uint32), split.view(np.uint32))
+
+
+def test_device_greedy_equals_host_loop(engine130):
+    """hg_decode_greedy (argmax fed back on the device) equals step-by-step hg_decode_batch."""
+    prompts = [synth.prompt_ids(n, 40 + n) for n in (33, 80, 150)]
+    ca = [engine130.new_cache() for _ in prompts]
+    cb = [engine130.new_cache() for _ in prompts]
+    t0 = []
+    for p, a, b in zip(prompts, ca, cb):
+        la = engine130.prefill(a, p)
+        engine130.prefill(b, p)
+        la[50257:] = -np.inf
+        t0.append(int(np.argmax(la)))
+    dev = engine130.decode_greedy(ca, t0, 70)  # crosses the 64-step id ring
+    toks = list(t0)
+    for k in range(70):
+        nxt, _ = engine130.decode_batch(cb, toks)
+        assert [int(v) for v in nxt] == [int(v) for v in dev[k]], f"step {k}"
+        toks = [int(v) for v in nxt]
+    assert [c.len for c in ca] == [c.len for c in cb]
+    for c in ca + cb:
+        c.close()
 
 
 def test_greedy_decode_config1(engine130, oracle130):
