@@ -578,41 +578,59 @@ __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
       asm volatile("fence.proxy.async.global;" ::: "memory");
     }
     __syncthreads();
-    float qreg[REP][E];
+    // ops::dot lane mapping: accumulator m's SIMD lane l sums elements 32i + 8m + l (FMA, i
+    // ascending); lane sums are (a0+a1)+(a2+a3), then the 8-lane tree. Here a group of 8 threads
+    // (l = lane % 8) owns one position, so the 4 accumulators stay in registers and only the tree
+    // needs shuffles (3 per head); a warp scores 4 positions at a time.
+    const int l = lane & 7, pp = lane >> 3;
+    float qv[REP][E][4];
 #pragma unroll
     for (int h = 0; h < REP; h++)
 #pragma unroll
-      for (int i = 0; i < E; i++) qreg[h][i] = q_s[h][32 * i + lane];
+      for (int i = 0; i < E; i++)
+#pragma unroll
+        for (int m = 0; m < 4; m++) qv[h][i][m] = q_s[h][32 * i + 8 * m + l];
     float* srow = A.S + ((size_t)t * A.nh + kvh * REP) * A.s_stride;
     for (int c = cbeg; c < cend; c++) {
       const int c0 = c * ATT_CHUNK;
       float mx[REP];
 #pragma unroll
       for (int h = 0; h < REP; h++) mx[h] = -INFINITY;
-#pragma unroll 2
-      for (int i8 = 0; i8 < 8; i8++) {
-        const int p = c0 + warp * 8 + i8;
-        if (p >= n) break;
-        const float* kp = p == pos ? knew_s
-                                   : A.k_pool + (long long)bt[p / PAGE] * A.page_stride +
-                                         ((long long)kvh * PAGE + (p % PAGE)) * HD;
-        float kr[E];
+      // this warp's 8 positions: c0 + 8 warp + 4 sub + pp, both sub-groups' K loads issued first
+      float kv[2][E][4];
 #pragma unroll
-        for (int i = 0; i < E; i++) kr[i] = kp[32 * i + lane];
+      for (int sub = 0; sub < 2; sub++) {
+        const int p = c0 + warp * 8 + sub * 4 + pp;
+        const float* kp = p == pos ? knew_s
+                                   : A.k_pool + (long long)bt[(p < n ? p : 0) / PAGE] * A.page_stride +
+                                         ((long long)kvh * PAGE + ((p < n ? p : 0) % PAGE)) * HD;
+#pragma unroll
+        for (int i = 0; i < E; i++)
+#pragma unroll
+          for (int m = 0; m < 4; m++) kv[sub][i][m] = p < n ? kp[32 * i + 8 * m + l] : 0.0f;
+      }
+#pragma unroll
+      for (int sub = 0; sub < 2; sub++) {
+        const int p = c0 + warp * 8 + sub * 4 + pp;
 #pragma unroll
         for (int h = 0; h < REP; h++) {
-          // ops::dot: lane = 8m + l accumulates elements 32i + lane (FMA, i ascending), then
-          // (a0+a1)+(a2+a3) per SIMD lane and the 8-lane tree
-          float acc = 0.0f;
+          float a[4];
 #pragma unroll
-          for (int i = 0; i < E; i++) acc = __fmaf_rn(qreg[h][i], kr[i], acc);
-          acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 8));
-          acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 16));
-          float sc = fmul(hsum8_group(acc), scale);
-          if (lane == 0) srow[(size_t)h * A.s_stride + p] = sc;
-          mx[h] = fmaxf(mx[h], sc);
+          for (int m = 0; m < 4; m++) {
+            float cacc = 0.0f;
+#pragma unroll
+            for (int i = 0; i < E; i++) cacc = __fmaf_rn(qv[h][i][m], kv[sub][i][m], cacc);
+            a[m] = cacc;
+          }
+          float sc = fmul(hsum8_group(fadd(fadd(a[0], a[1]), fadd(a[2], a[3]))), scale);
+          if (p < n) {
+            if (l == 0) srow[(size_t)h * A.s_stride + p] = sc;
+            mx[h] = fmaxf(mx[h], sc);
+          }
         }
       }
+#pragma unroll
+      for (int h = 0; h < REP; h++) mx[h] = warp_max(mx[h]);
       if (lane == 0)
 #pragma unroll
         for (int h = 0; h < REP; h++) wmax_s[warp][h] = mx[h];
@@ -645,33 +663,39 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
-// Bounded wait for phase `parity` of an mbarrier: gives up after ~1 s (globaltimer) and returns false.
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// Bounded wait for phase `parity` of an mbarrier: gives up after ~1 s (globaltimer, read only once
+// the phase is late) and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t done = 0;
-  uint64_t t0;
+  if (mbar_try(bar, parity)) return true;
+  uint64_t t0, t1;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
   while (true) {
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    if (done) return true;
-    uint64_t t1;
+    for (int k = 0; k < 64; k++)
+      if (mbar_try(bar, parity)) return true;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
     if (t1 - t0 > 1000000000ull) return false;
   }
 }
 
-constexpr int ATT_STAGES = 8;  // V pages in flight per CTA
+constexpr int ATT_MAX_STAGES = 24;  // V pages in flight per CTA (runtime count A.stages <= this)
 constexpr int ATT_ECH = 512;   // softmax positions per sum chunk
 
 template <int HD, int REP>
 __global__ void __launch_bounds__(REP * HD) k_attn_out(AttnArgs A) {
   constexpr int NT = REP * HD, NW = NT / 32;
   constexpr uint32_t PAGE_BYTES = PAGE * HD * 4;
-  extern __shared__ __align__(128) unsigned char ring[];  // ATT_STAGES pages of [16][HD] f32
-  __shared__ __align__(8) uint64_t bar[ATT_STAGES];
+  extern __shared__ __align__(128) unsigned char ring[];  // A.stages pages of [16][HD] f32
+  __shared__ __align__(8) uint64_t bar[ATT_MAX_STAGES];
+  const int ATT_STAGES = A.stages;
   __shared__ float ebuf[REP][ATT_ECH];
   __shared__ float m_s[REP], inv_s[REP];
   __shared__ int fail_s;
@@ -945,7 +969,7 @@ int attn_grid(int T, int nkv, int max_chunks) {
 template <int HD, int REP>
 static cudaError_t launch_attn_t(const AttnArgs& A, int grid, cudaStream_t st, int which) {
   if (which & 1) k_attn_scores<HD, REP><<<grid, 256, 0, st>>>(A);
-  const size_t smem = (size_t)ATT_STAGES * PAGE * HD * 4;
+  const size_t smem = (size_t)A.stages * PAGE * HD * 4;
   if (which & 2) k_attn_out<HD, REP><<<A.T * A.nkv, REP * HD, smem, st>>>(A);
   return cudaGetLastError();
 }
@@ -971,7 +995,7 @@ cudaError_t prepare_attn(int hd, int rep) {
   auto set = [](const void* fn, size_t bytes) {
     return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
   };
-  const size_t s128 = (size_t)ATT_STAGES * PAGE * 128 * 4, s64 = (size_t)ATT_STAGES * PAGE * 64 * 4;
+  const size_t s128 = (size_t)ATT_MAX_STAGES * PAGE * 128 * 4, s64 = (size_t)ATT_MAX_STAGES * PAGE * 64 * 4;
   if (hd == 128 && rep == 4) return set((const void*)k_attn_out<128, 4>, s128);
   if (hd == 64 && rep == 4) return set((const void*)k_attn_out<64, 4>, s64);
   if (hd == 128 && rep == 2) return set((const void*)k_attn_out<128, 2>, s128);

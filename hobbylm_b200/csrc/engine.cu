@@ -448,6 +448,7 @@ AttnArgs make_attn_args(hg_engine* e, const DecodeBufs& B, int l) {
   A.S = B.S;
   A.s_stride = B.s_stride;
   A.cmax = B.cmax;
+  A.stages = B.T < 8 ? 24 : 8;  // few CTAs: each streams its V alone, so keep more pages in flight
   A.out = nullptr;
   A.qo = B.qo;
   A.so = B.so;
@@ -1302,6 +1303,7 @@ int hg_op_kv_attn(const hg_kv_attn_args* a, void* scratch, void* stream) {
     A.S = reinterpret_cast<float*>(base);
     A.cmax = reinterpret_cast<float*>(base + align256((size_t)a->n_seqs * a->n_heads * A.s_stride * 4));
     A.err = nullptr;
+    A.stages = a->n_seqs < 8 ? 24 : 8;
     A.out = a->out;
     A.qo = nullptr;
     A.so = nullptr;

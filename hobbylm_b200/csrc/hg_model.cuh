@@ -100,6 +100,7 @@ struct AttnArgs {
   float* S;        // [T][nh][s_stride] scores, then exp(score - max)
   long long s_stride;  // >= max_pos, multiple of 16
   float* cmax;     // [T][nh][max_chunks] chunk maxima of the scores
+  int stages;      // V pages in flight per k_attn_out CTA (2..24, even)
   float* out;      // [T][nh*hd] or null
   int8_t* qo;      // [T][nh*hd] or null
   float* so;       // [T][ss(nh*hd/32)]
