@@ -538,7 +538,6 @@ __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
   constexpr int E = HD / 32;
   __shared__ __align__(16) float q_s[REP][HD];
   __shared__ __align__(16) float knew_s[HD];
-  __shared__ float wmax_s[8][REP];
   __shared__ int prefix_s[257];
   __shared__ int g_s;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -629,18 +628,16 @@ __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
           }
         }
       }
+      // per-warp maximum of this chunk: cmax[t][h][c * 8 + warp] (no block barrier needed)
 #pragma unroll
       for (int h = 0; h < REP; h++) mx[h] = warp_max(mx[h]);
-      if (lane == 0)
+      if (lane < REP) {
+        float mv = mx[0];
 #pragma unroll
-        for (int h = 0; h < REP; h++) wmax_s[warp][h] = mx[h];
-      __syncthreads();
-      if (threadIdx.x < REP) {
-        float m = -INFINITY;
-        for (int w = 0; w < 8; w++) m = fmaxf(m, wmax_s[w][threadIdx.x]);
-        A.cmax[((size_t)t * A.nh + kvh * REP + threadIdx.x) * A.max_chunks + c] = m;
+        for (int h = 1; h < REP; h++)
+          if (lane == h) mv = mx[h];
+        A.cmax[((size_t)t * A.nh + kvh * REP + lane) * (size_t)A.max_chunks * 8 + c * 8 + warp] = mv;
       }
-      __syncthreads();
     }
   }
 }
@@ -686,84 +683,97 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
-constexpr int ATT_MAX_STAGES = 24;  // V pages in flight per CTA (runtime count A.stages <= this)
-constexpr int ATT_ECH = 512;   // softmax positions per sum chunk
+constexpr int ATT_MAX_STAGES = 24;  // V pages in flight per CTA (runtime count A.stages <= this, even)
+constexpr int ATT_ECH = 512;        // softmax positions per sum chunk
 
-template <int HD, int REP>
-__global__ void __launch_bounds__(REP * HD) k_attn_out(AttnArgs A) {
-  constexpr int NT = REP * HD, NW = NT / 32;
+// One CTA per (token, q head), HD threads (thread = output dim). The kv head's V pages start
+// streaming into the ring at entry; meanwhile the softmax sum runs: warps 1.. compute
+// e = exp(s - max) for the next chunk (into shared memory and back into S) while warp 0 adds the
+// current chunk in position order. Then o[di] += (e_j * inv) * v_j[di] over j in order.
+template <int HD>
+__global__ void __launch_bounds__(HD) k_attn_out(AttnArgs A) {
   constexpr uint32_t PAGE_BYTES = PAGE * HD * 4;
+  constexpr int NW = HD / 32;
   extern __shared__ __align__(128) unsigned char ring[];  // A.stages pages of [16][HD] f32
   __shared__ __align__(8) uint64_t bar[ATT_MAX_STAGES];
-  const int ATT_STAGES = A.stages;
-  __shared__ float ebuf[REP][ATT_ECH];
-  __shared__ float m_s[REP], inv_s[REP];
+  __shared__ float ebuf[2][ATT_ECH];
+  __shared__ float inv_s, m_s;
   __shared__ int fail_s;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int h = tid / HD, di = tid % HD;
-  const int t = blockIdx.x / A.nkv, kvh = blockIdx.x % A.nkv;
+  const int S = A.stages;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, di = tid;
+  const int t = blockIdx.x / A.nh, h = blockIdx.x - t * A.nh;
+  const int rep = A.nh / A.nkv, kvh = h / rep;
   const int pos = A.pos[t];
   if (pos < 0 || pos >= A.max_pos) return;  // flagged by k_attn_scores
   const int n = pos + 1, nch = (n + ATT_CHUNK - 1) / ATT_CHUNK, npages = (n + PAGE - 1) / PAGE;
   const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
-  float* srow = A.S + ((size_t)t * A.nh + kvh * REP) * A.s_stride;
-  if (tid == 0) {
-    fail_s = 0;
-    for (int s = 0; s < ATT_STAGES; s++) mbar_init(&bar[s], 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-  // start streaming V pages (independent of the softmax)
+  float* erow = A.S + ((size_t)t * A.nh + h) * A.s_stride;
   const float* vbase = A.v_pool + (long long)kvh * PAGE * HD;
   if (tid == 0) {
-    for (int p = 0; p < ATT_STAGES && p < npages; p++) {
+    fail_s = 0;
+    for (int s = 0; s < S; s++) mbar_init(&bar[s], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int p = 0; p < S && p < npages; p++) {
       mbar_expect_tx(&bar[p], PAGE_BYTES);
       bulk_g2s(ring + (size_t)p * PAGE_BYTES, vbase + (long long)bt[p] * A.page_stride, PAGE_BYTES, &bar[p]);
     }
   }
-  // global max per head over the chunk maxima
-  if (tid < REP) {
+  if (warp == 0) {  // max over the per-warp chunk maxima
+    const float* cm = A.cmax + ((size_t)t * A.nh + h) * (size_t)A.max_chunks * 8;
     float m = -INFINITY;
-    const float* cm = A.cmax + ((size_t)t * A.nh + kvh * REP + tid) * A.max_chunks;
-    for (int c = 0; c < nch; c++) m = fmaxf(m, cm[c]);
-    m_s[tid] = m;
+    for (int c = lane; c < nch * 8; c += 32) m = fmaxf(m, cm[c]);
+    m = warp_max(m);
+    if (lane == 0) m_s = m;
   }
   __syncthreads();
-  // e_j = exp(s_j - max) in parallel (written back in place), sum sequential per head in chunks
-  float sum = 0.0f;  // meaningful in warp h < REP
-  for (int j0 = 0; j0 < n; j0 += ATT_ECH) {
-    const int cnt = min(ATT_ECH, n - j0);
-    for (int i = tid; i < REP * cnt; i += NT) {
-      const int hh = i / cnt, j = i - hh * cnt;
-      float e = exp_cr(__fsub_rn(srow[(size_t)hh * A.s_stride + j0 + j], m_s[hh]));
-      ebuf[hh][j] = e;
-      srow[(size_t)hh * A.s_stride + j0 + j] = e;
-    }
-    __syncthreads();
-    if (warp < REP) {  // every lane of warp h runs the same chain (broadcast reads)
+  const float mrow = m_s;
+  // ---- softmax denominator: sequential f32 sum over positions (ops.rs:118-122) ----
+  const int nchunks = (n + ATT_ECH - 1) / ATT_ECH;
+  for (int j = tid; j < min(ATT_ECH, n); j += HD) {
+    const float e = exp_cr(__fsub_rn(erow[j], mrow));
+    ebuf[0][j] = e;
+    erow[j] = e;
+  }
+  __syncthreads();
+  float sum = 0.0f;
+  for (int c = 0; c < nchunks; c++) {
+    const int j0 = c * ATT_ECH, cnt = min(ATT_ECH, n - j0);
+    if (warp == 0 || NW == 1) {
+      const float* eb = ebuf[c & 1];
 #pragma unroll 8
-      for (int j = 0; j < cnt; j++) sum = fadd(sum, ebuf[warp][j]);
+      for (int j = 0; j < cnt; j++) sum = fadd(sum, eb[j]);
+    }
+    if ((warp > 0 || NW == 1) && c + 1 < nchunks) {
+      const int j1 = j0 + ATT_ECH, cn1 = min(ATT_ECH, n - j1);
+      const int nt = NW == 1 ? HD : HD - 32, t1 = NW == 1 ? tid : tid - 32;
+      float* eb = ebuf[(c + 1) & 1];
+      for (int j = t1; j < cn1; j += nt) {
+        const float e = exp_cr(__fsub_rn(erow[j1 + j], mrow));
+        eb[j] = e;
+        erow[j1 + j] = e;
+      }
     }
     __syncthreads();
   }
-  if (warp < REP && lane == 0) inv_s[warp] = __fdiv_rn(1.0f, sum);
+  if (tid == 0) inv_s = __fdiv_rn(1.0f, sum);
   __syncthreads();
-  const float inv = inv_s[h];
-  const float* erow = srow + (size_t)h * A.s_stride;
-  // o[h][di] = sum_j (e_j * inv) * v_j[di], sequential in j. Positions go in groups of 32 (two
-  // pages); lane i of each warp holds e of position 32g + i, prefetched EPF groups ahead so the
-  // L2 latency stays off the add chain.
+  const float inv = inv_s;
+  // ---- o[di] = sum_j (e_j * inv) * v_j[di], sequential in j (model.rs:227-232) ----
+  // groups of 32 positions (two pages); lane i holds e of position 32g + i, EPF groups ahead.
   constexpr int EPF = 4;
   const int ngroups = (n + 31) / 32;
   float epf[EPF];
 #pragma unroll
   for (int k = 0; k < EPF; k++) {
     const int j = 32 * k + lane;
-    epf[k] = (k < ngroups && j < n) ? erow[j] : 0.0f;
+    epf[k] = j < n ? erow[j] : 0.0f;
   }
   float acc = 0.0f;
-  int p = 0;  // next page to wait for
-  for (int g = 0; g < ngroups; g++) {
+  int cst = 0, cpar = 0;          // stage / parity of the next page to consume
+  int ist = 0;                     // stage of the next refill (stages are released in order)
+  int next_issue = S;              // next page to issue
+  int g = 0;
+  for (; g < ngroups; g++) {
     const float e_cur = epf[0];
 #pragma unroll
     for (int k = 0; k < EPF - 1; k++) epf[k] = epf[k + 1];
@@ -772,12 +782,18 @@ __global__ void __launch_bounds__(REP * HD) k_attn_out(AttnArgs A) {
       epf[EPF - 1] = j < n ? erow[j] : 0.0f;
     }
     const float pr = fmul(e_cur, inv);
-    const int p0 = 2 * g, p1 = min(2 * g + 1, npages - 1);
-    bool ok = mbar_wait(&bar[p0 % ATT_STAGES], (uint32_t)(p0 / ATT_STAGES) & 1u);
-    if (p1 != p0) ok = mbar_wait(&bar[p1 % ATT_STAGES], (uint32_t)(p1 / ATT_STAGES) & 1u) && ok;
+    const bool two = 2 * g + 1 < npages;
+    const int s0 = cst, p0par = cpar;
+    int s1 = cst + 1, p1par = cpar;
+    if (s1 == S) {
+      s1 = 0;
+      p1par ^= 1;
+    }
+    bool ok = mbar_wait(&bar[s0], (uint32_t)p0par);
+    if (two) ok = mbar_wait(&bar[s1], (uint32_t)p1par) && ok;
     if (!ok && lane == 0) atomicExch(&fail_s, 1);
-    const float* v0 = reinterpret_cast<const float*>(ring + (size_t)(p0 % ATT_STAGES) * PAGE_BYTES) + di;
-    const float* v1 = reinterpret_cast<const float*>(ring + (size_t)(p1 % ATT_STAGES) * PAGE_BYTES) + di;
+    const float* v0 = reinterpret_cast<const float*>(ring + (size_t)s0 * PAGE_BYTES) + di;
+    const float* v1 = reinterpret_cast<const float*>(ring + (size_t)s1 * PAGE_BYTES) + di;
     const int rows = min(32, n - 32 * g);
     if (rows == 32) {
       float pv[32], vv[32];
@@ -794,40 +810,50 @@ __global__ void __launch_bounds__(REP * HD) k_attn_out(AttnArgs A) {
         acc = fadd(acc, fmul(pj, r < 16 ? v0[r * HD] : v1[(r - 16) * HD]));
       }
     }
-    p = p1 + 1;
     __syncthreads();
     if (fail_s) break;
-    if (tid == 0) {  // refill the two stages just released
-      for (int q = p0 + ATT_STAGES; q <= p1 + ATT_STAGES && q < npages; q++) {
-        const int st = q % ATT_STAGES;
-        mbar_expect_tx(&bar[st], PAGE_BYTES);
-        bulk_g2s(ring + (size_t)st * PAGE_BYTES, vbase + (long long)bt[q] * A.page_stride, PAGE_BYTES, &bar[st]);
+    // advance the consume cursor by the pages of this group
+    const int used = two ? 2 : 1;
+    for (int u = 0; u < used; u++)
+      if (++cst == S) {
+        cst = 0;
+        cpar ^= 1;
+      }
+    if (tid == 0) {  // refill the stages just released
+      for (int u = 0; u < used && next_issue < npages; u++, next_issue++) {
+        mbar_expect_tx(&bar[ist], PAGE_BYTES);
+        bulk_g2s(ring + (size_t)ist * PAGE_BYTES, vbase + (long long)bt[next_issue] * A.page_stride, PAGE_BYTES,
+                 &bar[ist]);
+        if (++ist == S) ist = 0;
       }
     }
   }
   if (fail_s) {
-    // a bulk copy did not complete in time: report, then wait (bounded) for the pages that may
-    // still be in flight so no copy lands in shared memory after this CTA exits
+    // a bulk copy did not complete in time: report, then wait (bounded) for every page issued
+    // but not consumed so no copy lands in shared memory after this CTA exits
     if (tid == 0) {
       if (A.err) atomicExch(A.err, HG_ERR_TIMEOUT);
-      for (int q = p - 2; q < p + ATT_STAGES && q < npages; q++)
-        if (q >= 0) mbar_wait(&bar[q % ATT_STAGES], (uint32_t)(q / ATT_STAGES) & 1u);
+      int st = cst, par = cpar;
+      for (int q = 2 * g; q < next_issue && q < npages; q++) {
+        mbar_wait(&bar[st], (uint32_t)par);
+        if (++st == S) {
+          st = 0;
+          par ^= 1;
+        }
+      }
     }
     __syncthreads();
     return;
   }
-  const int hg = kvh * REP + h;
   const int qd = A.nh * HD;
-  if (A.out) A.out[(size_t)t * qd + hg * HD + di] = acc;
-  if (A.qo) {
-    // each warp holds 32 consecutive dims of one head = one 32-block
+  if (A.out) A.out[(size_t)t * qd + h * HD + di] = acc;
+  if (A.qo) {  // each warp holds one 32-block of the head
     float dq;
     int8_t q = quant_lane(acc, &dq);
     const int nbq = qd >> 5;
-    A.qo[(size_t)t * qd + q8_pos(hg * HD + di, nbq)] = q;
-    if (lane == 0) A.so[(size_t)t * q8_ss(nbq) + ((hg * HD + di) >> 5)] = dq;
+    A.qo[(size_t)t * qd + q8_pos(h * HD + di, nbq)] = q;
+    if (lane == 0) A.so[(size_t)t * q8_ss(nbq) + ((h * HD + di) >> 5)] = dq;
   }
-  (void)NW;
 }
 
 // ------------------------------------------------------------------------------------------
@@ -970,12 +996,13 @@ template <int HD, int REP>
 static cudaError_t launch_attn_t(const AttnArgs& A, int grid, cudaStream_t st, int which) {
   if (which & 1) k_attn_scores<HD, REP><<<grid, 256, 0, st>>>(A);
   const size_t smem = (size_t)A.stages * PAGE * HD * 4;
-  if (which & 2) k_attn_out<HD, REP><<<A.T * A.nkv, REP * HD, smem, st>>>(A);
+  if (which & 2) k_attn_out<HD><<<A.T * A.nh, HD, smem, st>>>(A);
   return cudaGetLastError();
 }
 
 static cudaError_t launch_attn_which(const AttnArgs& A, int grid, cudaStream_t st, int which) {
   int rep = A.nh / A.nkv;
+  if (A.stages < 2 || A.stages > ATT_MAX_STAGES || (A.stages & 1)) return cudaErrorInvalidValue;
   if (A.hd == 128 && rep == 4) return launch_attn_t<128, 4>(A, grid, st, which);
   if (A.hd == 64 && rep == 4) return launch_attn_t<64, 4>(A, grid, st, which);
   if (A.hd == 128 && rep == 2) return launch_attn_t<128, 2>(A, grid, st, which);
@@ -992,16 +1019,13 @@ cudaError_t launch_attn_out_only(const AttnArgs& A, cudaStream_t st) { return la
 // Opt in to the ring's dynamic shared memory on the current device (call before any launch or
 // graph capture).
 cudaError_t prepare_attn(int hd, int rep) {
-  auto set = [](const void* fn, size_t bytes) {
-    return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-  };
-  const size_t s128 = (size_t)ATT_MAX_STAGES * PAGE * 128 * 4, s64 = (size_t)ATT_MAX_STAGES * PAGE * 64 * 4;
-  if (hd == 128 && rep == 4) return set((const void*)k_attn_out<128, 4>, s128);
-  if (hd == 64 && rep == 4) return set((const void*)k_attn_out<64, 4>, s64);
-  if (hd == 128 && rep == 2) return set((const void*)k_attn_out<128, 2>, s128);
-  if (hd == 64 && rep == 2) return set((const void*)k_attn_out<64, 2>, s64);
-  if (hd == 128 && rep == 1) return set((const void*)k_attn_out<128, 1>, s128);
-  if (hd == 64 && rep == 1) return set((const void*)k_attn_out<64, 1>, s64);
+  if (rep != 1 && rep != 2 && rep != 4) return cudaErrorInvalidValue;
+  if (hd == 128)
+    return cudaFuncSetAttribute((const void*)k_attn_out<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                ATT_MAX_STAGES * PAGE * 128 * 4);
+  if (hd == 64)
+    return cudaFuncSetAttribute((const void*)k_attn_out<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                ATT_MAX_STAGES * PAGE * 64 * 4);
   return cudaErrorInvalidValue;
 }
 

@@ -229,7 +229,7 @@ void alloc_work(hg_engine* e) {
   B.y = a.take<float>((size_t)T * (k + 1) * d);
   B.s_stride = ((long long)c.context_length + 15) & ~15LL;
   B.S = a.take<float>((size_t)T * c.n_heads * B.s_stride);
-  B.cmax = a.take<float>((size_t)T * c.n_heads * max_chunks);
+  B.cmax = a.take<float>((size_t)T * c.n_heads * max_chunks * 8);
   B.max_chunks = max_chunks;
   B.logits = a.take<float>((size_t)T * c.vocab_size);
   B.amax = a.take<unsigned long long>(T);
@@ -957,7 +957,7 @@ size_t kv_s_stride(const hg_kv_attn_args* a) { return ((size_t)a->max_pos + 15) 
 size_t kv_scratch_bytes(const hg_kv_attn_args* a) {
   int max_chunks = (a->max_pos + ATT_CHUNK - 1) / ATT_CHUNK;
   return align256((size_t)a->n_seqs * a->n_heads * kv_s_stride(a) * 4) +
-         align256((size_t)a->n_seqs * a->n_heads * max_chunks * 4) + 256;
+         align256((size_t)a->n_seqs * a->n_heads * max_chunks * 8 * 4) + 256;
 }
 
 }  // namespace
