@@ -540,6 +540,7 @@ __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
   __shared__ __align__(16) float knew_s[HD];
   __shared__ int prefix_s[257];
   __shared__ int g_s;
+  __shared__ int pg_s[1024];  // page ids of the item's chunks (ATT_CHUNK / PAGE per chunk)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total = attn_item_prefix(A, prefix_s, &g_s);
   const int G = g_s;
@@ -563,6 +564,8 @@ __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
     const float* sn = A.rope_sin + (size_t)pos * (HD / 2);
     const bool has_new = (pos / ATT_CHUNK) >= cbeg && (pos / ATT_CHUNK) < cend;
     __syncthreads();
+    const int pg0 = cbeg * (ATT_CHUNK / PAGE), npg = min((cend - cbeg) * (ATT_CHUNK / PAGE), 1024);
+    for (int i = threadIdx.x; i < npg; i += blockDim.x) pg_s[i] = pg0 + i < A.bt_stride ? bt[pg0 + i] : 0;
     if (warp < REP) norm_rope_warp<HD>(qkv + (kvh * REP + warp) * HD, A.q_norm, A.eps, cs, sn, q_s[warp]);
     if (has_new) {
       const long long off =
@@ -600,9 +603,12 @@ __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
 #pragma unroll
       for (int sub = 0; sub < 2; sub++) {
         const int p = c0 + warp * 8 + sub * 4 + pp;
+        const int pc = p < n ? p : c0;  // positions past the end read a valid row, unused
+        const int pgi = pc / PAGE - pg0;
+        const int page = pgi < 1024 ? pg_s[pgi] : bt[pc / PAGE];
         const float* kp = p == pos ? knew_s
-                                   : A.k_pool + (long long)bt[(p < n ? p : 0) / PAGE] * A.page_stride +
-                                         ((long long)kvh * PAGE + ((p < n ? p : 0) % PAGE)) * HD;
+                                   : A.k_pool + (long long)page * A.page_stride +
+                                         ((long long)kvh * PAGE + (pc % PAGE)) * HD;
 #pragma unroll
         for (int i = 0; i < E; i++)
 #pragma unroll
@@ -685,6 +691,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 
 constexpr int ATT_MAX_STAGES = 24;  // V pages in flight per CTA (runtime count A.stages <= this, even)
 constexpr int ATT_ECH = 512;        // softmax positions per sum chunk
+constexpr int ATT_MAX_BT = 4096;    // block-table entries held in shared memory (contexts <= 65536)
 
 // One CTA per (token, q head), HD threads (thread = output dim). The kv head's V pages start
 // streaming into the ring at entry; meanwhile the softmax sum runs: warps 1.. compute
@@ -694,12 +701,14 @@ template <int HD>
 __global__ void __launch_bounds__(HD) k_attn_out(AttnArgs A) {
   constexpr uint32_t PAGE_BYTES = PAGE * HD * 4;
   constexpr int NW = HD / 32;
-  extern __shared__ __align__(128) unsigned char ring[];  // A.stages pages of [16][HD] f32
+  // dynamic shared memory: A.stages pages of [16][HD] f32, then the sequence's page ids
+  extern __shared__ __align__(128) unsigned char ring[];
   __shared__ __align__(8) uint64_t bar[ATT_MAX_STAGES];
   __shared__ float ebuf[2][ATT_ECH];
   __shared__ float inv_s, m_s;
   __shared__ int fail_s;
   const int S = A.stages;
+  int* bt_s = reinterpret_cast<int*>(ring + (size_t)S * PAGE_BYTES);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, di = tid;
   const int t = blockIdx.x / A.nh, h = blockIdx.x - t * A.nh;
   const int rep = A.nh / A.nkv, kvh = h / rep;
@@ -709,13 +718,17 @@ __global__ void __launch_bounds__(HD) k_attn_out(AttnArgs A) {
   const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
   float* erow = A.S + ((size_t)t * A.nh + h) * A.s_stride;
   const float* vbase = A.v_pool + (long long)kvh * PAGE * HD;
+  for (int p = tid; p < npages; p += HD) bt_s[p] = bt[p];  // page ids: no global load per refill
   if (tid == 0) {
     fail_s = 0;
     for (int s = 0; s < S; s++) mbar_init(&bar[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (tid == 0) {
     for (int p = 0; p < S && p < npages; p++) {
       mbar_expect_tx(&bar[p], PAGE_BYTES);
-      bulk_g2s(ring + (size_t)p * PAGE_BYTES, vbase + (long long)bt[p] * A.page_stride, PAGE_BYTES, &bar[p]);
+      bulk_g2s(ring + (size_t)p * PAGE_BYTES, vbase + (long long)bt_s[p] * A.page_stride, PAGE_BYTES, &bar[p]);
     }
   }
   if (warp == 0) {  // max over the per-warp chunk maxima
@@ -822,7 +835,7 @@ __global__ void __launch_bounds__(HD) k_attn_out(AttnArgs A) {
     if (tid == 0) {  // refill the stages just released
       for (int u = 0; u < used && next_issue < npages; u++, next_issue++) {
         mbar_expect_tx(&bar[ist], PAGE_BYTES);
-        bulk_g2s(ring + (size_t)ist * PAGE_BYTES, vbase + (long long)bt[next_issue] * A.page_stride, PAGE_BYTES,
+        bulk_g2s(ring + (size_t)ist * PAGE_BYTES, vbase + (long long)bt_s[next_issue] * A.page_stride, PAGE_BYTES,
                  &bar[ist]);
         if (++ist == S) ist = 0;
       }
@@ -995,14 +1008,15 @@ int attn_grid(int T, int nkv, int max_chunks) {
 template <int HD, int REP>
 static cudaError_t launch_attn_t(const AttnArgs& A, int grid, cudaStream_t st, int which) {
   if (which & 1) k_attn_scores<HD, REP><<<grid, 256, 0, st>>>(A);
-  const size_t smem = (size_t)A.stages * PAGE * HD * 4;
+  const size_t smem = (size_t)A.stages * PAGE * HD * 4 + (size_t)A.bt_stride * 4;
   if (which & 2) k_attn_out<HD><<<A.T * A.nh, HD, smem, st>>>(A);
   return cudaGetLastError();
 }
 
 static cudaError_t launch_attn_which(const AttnArgs& A, int grid, cudaStream_t st, int which) {
   int rep = A.nh / A.nkv;
-  if (A.stages < 2 || A.stages > ATT_MAX_STAGES || (A.stages & 1)) return cudaErrorInvalidValue;
+  if (A.stages < 2 || A.stages > ATT_MAX_STAGES || (A.stages & 1) || A.bt_stride > ATT_MAX_BT)
+    return cudaErrorInvalidValue;
   if (A.hd == 128 && rep == 4) return launch_attn_t<128, 4>(A, grid, st, which);
   if (A.hd == 64 && rep == 4) return launch_attn_t<64, 4>(A, grid, st, which);
   if (A.hd == 128 && rep == 2) return launch_attn_t<128, 2>(A, grid, st, which);
@@ -1020,12 +1034,13 @@ cudaError_t launch_attn_out_only(const AttnArgs& A, cudaStream_t st) { return la
 // graph capture).
 cudaError_t prepare_attn(int hd, int rep) {
   if (rep != 1 && rep != 2 && rep != 4) return cudaErrorInvalidValue;
+  // the ring plus up to ATT_MAX_BT page ids
   if (hd == 128)
     return cudaFuncSetAttribute((const void*)k_attn_out<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                ATT_MAX_STAGES * PAGE * 128 * 4);
+                                ATT_MAX_STAGES * PAGE * 128 * 4 + ATT_MAX_BT * 4);
   if (hd == 64)
     return cudaFuncSetAttribute((const void*)k_attn_out<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                ATT_MAX_STAGES * PAGE * 64 * 4);
+                                ATT_MAX_STAGES * PAGE * 64 * 4 + ATT_MAX_BT * 4);
   return cudaErrorInvalidValue;
 }
 

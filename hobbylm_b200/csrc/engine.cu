@@ -272,9 +272,10 @@ void load_engine(hg_engine* e, const char* path, const hg_engine_opts& o) {
   // the file is parsed and validated before any CUDA call, so format errors need no GPU
   Gguf g(path);
   hg_config c = config_from_gguf(g);
-  validate_cfg(c);
+  // lib.rs:88 builds the tokenizer (tokenizer.rs:55-61 requires both arrays) before the model
   if (!g.has_str_array("tokenizer.ggml.tokens")) throw Error(HG_ERR_MISSING, "missing tokenizer.ggml.tokens");
   if (!g.has_str_array("tokenizer.ggml.merges")) throw Error(HG_ERR_MISSING, "missing tokenizer.ggml.merges");
+  validate_cfg(c);
   for (const char* t : {"token_embd.weight", "output.weight", "output_norm.weight"})
     if (!g.tensor(t)) throw Error(HG_ERR_MISSING, std::string("tensor `") + t + "` not found");
   HG_CUDA(cudaSetDevice(e->device));

@@ -1,0 +1,117 @@
+"""CPU checks that pin the synthetic-model producer and the oracle to the reference's own code.
+
+* synth_digests_*.json: per-tensor digests of the F32 GGUF written by the reference exporter
+  (export/to_gguf.py) from the reference's seed-0 MoETransformer (tests/golden/make_golden.py);
+  hobbylm_b200.synth must reproduce every tensor bit for bit.
+* torch_logits_130M.npz: the reference PyTorch forward (hobbylm/model.py) of the 130M model;
+  the oracle's F32 path (hobby-rs --quant f32 semantics) must match it within f32 reordering
+  tolerance (the two sum in different orders).
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from hobbylm_b200 import synth
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.mark.parametrize("preset", ["130M", "500M"])
+def test_synth_matches_reference_export(preset):
+    with open(os.path.join(GOLDEN, f"synth_digests_{preset}.json")) as f:
+        g = json.load(f)
+    got = synth.digests(preset, seed=0)
+    assert set(got) == set(g["digests"])
+    bad = [k for k, v in g["digests"].items() if got[k] != v]
+    assert not bad, f"{len(bad)} tensors differ, e.g. {bad[:3]}"
+    m = g["meta"]
+    p = synth.PRESETS[preset]
+    assert m["hobbylm.embedding_length"] == p.d_model and m["hobbylm.block_count"] == p.n_layers
+    assert m["hobbylm.expert_used_count"] == p.top_k and m["hobbylm.rope.freq_base"] == p.rope_theta
+
+
+def test_oracle_f32_matches_reference_torch(oracle_mod):
+    g = np.load(os.path.join(GOLDEN, "torch_logits_130M.npz"))
+    path = synth.cached_model("130M", 0, quant="f32", rms_eps=1e-6)
+    eng = oracle_mod.Engine(path, quant=False)
+    c = eng.new_cache()
+    last = eng.prefill(c, g["ids"])
+    rel = np.linalg.norm(last - g["last"]) / np.linalg.norm(g["last"])
+    assert rel < 1e-5, rel
+    assert np.array_equal(np.argsort(-last)[:8], g["top_ids"][-1])
+    # the decode path (Model::forward) over the same tokens, one position at a time
+    c2 = eng.new_cache()
+    lg = eng.prefill(c2, g["ids"][:1])
+    for pos in range(1, len(g["ids"])):
+        top = np.argsort(-lg)[:8]
+        assert np.array_equal(top, g["top_ids"][pos - 1]), pos
+        lse = np.log(np.exp(lg - lg.max()).sum()) + lg.max()
+        assert abs(lse - g["lse"][pos - 1]) < 1e-4
+        lg = eng.forward(c2, int(g["ids"][pos]), pos)
+    rel = np.linalg.norm(lg - g["last"]) / np.linalg.norm(g["last"])
+    assert rel < 1e-5, rel
+
+
+def test_q8_0_fixture_dequant_matches_gguf_py(oracle_mod):
+    """The oracle's Q8_0 dequant (gguf.rs:365-375) equals gguf-py's on a synthetic file's tensor."""
+    import gguf
+
+    path = synth.cached_model("130M", 0)
+    r = gguf.GGUFReader(path)
+    t = next(t for t in r.tensors if t.name == "blk.1.attn_qkv.weight")
+    raw = np.asarray(t.data).view(np.uint8).ravel()
+    n = int(np.prod(t.shape))
+    ours = oracle_mod.dequant(8, raw, n)
+    ref = gguf.quants.dequantize(np.asarray(t.data), gguf.GGMLQuantizationType.Q8_0).ravel()
+    assert np.array_equal(ours.view(np.uint32), ref.astype(np.float32).view(np.uint32))
+
+
+def test_requant_is_identity_on_full_range_blocks(oracle_mod):
+    """quant.rs:78-102 applied to Q8_0 data whose blocks reach +-127 returns the same int8 codes and
+    the f16 scale as f32 (the model weights' case); blocks without +-127 are rescaled."""
+    rng = np.random.default_rng(0)
+    q = rng.integers(-127, 128, (64, 256)).astype(np.float32)
+    q[:, ::32] = 127.0  # every block holds +127
+    d16 = (np.abs(rng.standard_normal((64, 8))) * 0.01).astype(np.float16).astype(np.float32)
+    w = (q.reshape(64, 8, 32) * d16[:, :, None]).reshape(64, 256).astype(np.float32)
+    qs, sc = oracle_mod.q8_quantize(w)
+    assert np.array_equal(qs.astype(np.float32), q)
+    assert np.array_equal(sc, d16)
+    q2 = q.copy()
+    q2[:, ::32] = 100.0
+    q2 = np.clip(q2, -100, 100)
+    w2 = (q2.reshape(64, 8, 32) * d16[:, :, None]).reshape(64, 256).astype(np.float32)
+    qs2, sc2 = oracle_mod.q8_quantize(w2)
+    assert np.abs(qs2).max() == 127 and not np.array_equal(sc2, d16)
+
+
+def test_oracle_exp_pin(oracle_mod):
+    """The oracle pins f32::exp to (float)exp((double)x); libm mode switches to glibc expf."""
+    xs = np.linspace(-30, 30, 2001, dtype=np.float32)
+    ours = np.array([oracle_mod.expf(float(x)) for x in xs], np.float32)
+    ref = np.exp(xs.astype(np.float64)).astype(np.float32)
+    assert np.array_equal(ours.view(np.uint32), ref.view(np.uint32))
+    oracle_mod.set_exp_mode(True)
+    try:
+        libm = np.array([oracle_mod.expf(float(x)) for x in xs], np.float32)
+    finally:
+        oracle_mod.set_exp_mode(False)
+    # glibc's expf differs from the correctly rounded value on a small fraction of inputs, by 1 ulp
+    d = np.abs(libm.view(np.int32).astype(np.int64) - ours.view(np.int32).astype(np.int64))
+    assert d.max() <= 1
+
+
+def test_oracle_exp_choice_keeps_config1_tokens(oracle_mod):
+    """The exp pin does not change config 1's greedy tokens (libm expf vs correctly rounded)."""
+    path = synth.cached_model("130M", 0)
+    ids = synth.prompt_ids(128, 1)
+    eng = oracle_mod.Engine(path, quant=True)
+    a, _, _, _ = eng.generate(ids, 32)
+    oracle_mod.set_exp_mode(True)
+    try:
+        b, _, _, _ = eng.generate(ids, 32)
+    finally:
+        oracle_mod.set_exp_mode(False)
+    assert list(a) == list(b)

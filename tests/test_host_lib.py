@@ -1,0 +1,168 @@
+"""Host-side checks of libhobbygpu.so that need no GPU: exported symbols, the load-time
+re-quantization + lane-chunked packing, RoPE tables, GGUF parsing and its error paths."""
+import ctypes as C
+import os
+import re
+
+import numpy as np
+import pytest
+
+from hobbylm_b200 import _native, synth
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _header_functions():
+    txt = open(os.path.join(ROOT, "include", "hobbygpu.h")).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(hg_[a-z0-9_]+)\s*\(", txt)))
+
+
+def test_library_exports_every_header_symbol(native):
+    names = _header_functions()
+    assert names, "no functions parsed from include/hobbygpu.h"
+    lib = native.lib()
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    assert sorted(set(native.EXPORTS)) == names
+
+
+def _pack(native, w):
+    rows, cols = w.shape
+    ss = native.lib().hg_q8_scale_stride(cols)
+    qs = np.empty((rows, cols), np.int8)
+    sc = np.empty((rows, ss), np.float32)
+    native.check(native.lib().hg_q8_pack(w.ctypes.data, rows, cols, qs.ctypes.data, sc.ctypes.data))
+    un = np.empty_like(qs)
+    native.check(native.lib().hg_q8_unpack_qs(qs.ctypes.data, rows, cols, un.ctypes.data))
+    return un, sc, qs
+
+
+@pytest.mark.parametrize("rows,cols", [(7, 768), (5, 320), (3, 192), (4, 2304), (9, 64), (2, 4128)])
+def test_q8_pack_equals_oracle_requant(native, oracle_mod, rows, cols):
+    rng = np.random.default_rng(rows * cols)
+    w = (rng.standard_normal((rows, cols)) * 0.05).astype(np.float32)
+    w[0, :32] = 0.0  # an all-zero block (d = 0, id = 0)
+    w[1, 5] = 0.5 / 127.0 * np.abs(w[1, :32]).max() * 127.0  # values near rounding ties
+    un, sc, packed = _pack(native, w)
+    oq, osc = oracle_mod.q8_quantize(w)
+    nb = cols // 32
+    assert np.array_equal(un, oq)
+    assert np.array_equal(sc[:, :nb].view(np.uint32), osc.view(np.uint32))
+    assert not sc[:, nb:].any()
+    # the lane-chunked permutation: lane l of a 4-block chunk holds bytes 4l..4l+3 of each block
+    if nb >= 4:
+        for l in range(8):
+            for b in range(4):
+                assert np.array_equal(packed[:, l * 16 + b * 4: l * 16 + b * 4 + 4], oq[:, b * 32 + 4 * l: b * 32 + 4 * l + 4])
+
+
+def test_q8_pack_from_q8_0_blocks_matches_oracle(native, oracle_mod):
+    """Config-2 style weights (int8 ~ U[-127,127] with |N(0,0.01)| f16 scales, dequantized as
+    gguf.rs does) through the re-quantizer: bit-identical codes and scales."""
+    inp = synth.moe_op_inputs(seed=2, T=1)
+    w = inp["down_exps"][0]
+    un, sc, _ = _pack(native, w)
+    oq, osc = oracle_mod.q8_quantize(w)
+    assert np.array_equal(un, oq) and np.array_equal(sc[:, : w.shape[1] // 32], osc)
+
+
+def test_rope_tables_match_oracle(native, oracle_mod):
+    hd, mp, theta = 128, 300, 10000.0
+    c = np.empty((mp, hd // 2), np.float32)
+    s = np.empty_like(c)
+    native.check(native.lib().hg_rope_tables(hd, mp, theta, c.ctypes.data, s.ctypes.data))
+    r = oracle_mod.Rope(hd, mp, theta)
+    oc, os_ = r.tables()
+    assert np.array_equal(c, oc) and np.array_equal(s, os_)
+
+
+def _config(native, path):
+    cfg = native.Config()
+    rc = native.lib().hg_gguf_config(str(path).encode(), C.byref(cfg))
+    return rc, cfg
+
+
+def test_gguf_config_matches_oracle(native, oracle_mod, model130):
+    rc, cfg = _config(native, model130)
+    assert rc == 0
+    ora = oracle_mod.Engine(model130, quant=True)
+    d = cfg.as_dict()
+    for k, v in ora.cfg.items():
+        key = "eos_token" if k == "eos" else k
+        assert d[key] == pytest.approx(v), k
+
+
+def _write_gguf(path, meta: dict, tensors: dict, arch="hobbylm"):
+    import gguf
+
+    w = gguf.GGUFWriter(str(path), arch)
+    for k, v in meta.items():
+        if isinstance(v, bool):
+            w.add_bool(f"{arch}.{k}", v)
+        elif isinstance(v, int):
+            w.add_uint32(f"{arch}.{k}", v)
+        elif isinstance(v, float):
+            w.add_float32(f"{arch}.{k}", v)
+    for name, arr in tensors.items():
+        w.add_tensor(name, arr)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+
+
+def test_config_defaults_follow_config_rs(native, tmp_path):
+    """Optional keys take config.rs's defaults: leading_dense_block_count 1, expert_shared_count 0,
+    context_length 8192, rms_eps 1e-5, rope.freq_base 1e6, expert_weights_scale 1, head_dim = d/h,
+    vocab from token_embd rows."""
+    p = tmp_path / "m.gguf"
+    meta = {"embedding_length": 64, "block_count": 2, "attention.head_count": 2, "attention.head_count_kv": 1,
+            "feed_forward_length": 64, "expert_feed_forward_length": 32, "expert_count": 4, "expert_used_count": 2}
+    _write_gguf(p, meta, {"token_embd.weight": np.zeros((123, 64), np.float32)})
+    rc, cfg = _config(native, p)
+    assert rc == 0
+    c = cfg.as_dict()
+    assert (c["n_dense"], c["n_shared"], c["context_length"], c["head_dim"], c["vocab_size"]) == (1, 0, 8192, 32, 123)
+    assert c["rms_eps"] == pytest.approx(1e-5) and c["rope_theta"] == 1e6 and c["expert_weights_scale"] == 1.0
+    assert c["gating_sigmoid"] == 1 and c["expert_weights_norm"] == 0 and c["eos_token"] == 50256
+
+
+def test_gguf_errors(native, tmp_path):
+    lib = native.lib()
+    h = C.c_void_p()
+    assert lib.hg_engine_load(str(tmp_path / "missing.gguf").encode(), 0, C.byref(h)) == -2
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"GGML" + b"\0" * 64)
+    assert lib.hg_engine_load(str(bad).encode(), 0, C.byref(h)) == -3
+    assert b"bad magic" in lib.hg_last_error()
+    v2 = tmp_path / "v2.gguf"
+    v2.write_bytes(b"GGUF" + (2).to_bytes(4, "little") + b"\0" * 16)
+    assert lib.hg_engine_load(str(v2).encode(), 0, C.byref(h)) == -3
+    assert b"version 2" in lib.hg_last_error()
+    good = tmp_path / "g.gguf"
+    meta = {"embedding_length": 64, "block_count": 2, "attention.head_count": 2, "attention.head_count_kv": 1,
+            "feed_forward_length": 64, "expert_feed_forward_length": 32, "expert_count": 4, "expert_used_count": 2}
+    _write_gguf(good, meta, {"token_embd.weight": np.zeros((16, 64), np.float32)})
+    data = good.read_bytes()
+    trunc = tmp_path / "t.gguf"
+    trunc.write_bytes(data[:40])
+    assert lib.hg_engine_load(str(trunc).encode(), 0, C.byref(h)) == -3
+    assert b"unexpected end of file" in lib.hg_last_error()
+    # missing required metadata / tensors
+    nometa = tmp_path / "nm.gguf"
+    _write_gguf(nometa, {k: v for k, v in meta.items() if k != "expert_count"},
+                {"token_embd.weight": np.zeros((16, 64), np.float32)})
+    assert lib.hg_engine_load(str(nometa).encode(), 0, C.byref(h)) == -4
+    assert b"expert_count" in lib.hg_last_error()
+    # the tokenizer arrays are required (tokenizer.rs:55-61) before any GPU work
+    assert lib.hg_engine_load(str(good).encode(), 0, C.byref(h)) == -4
+    assert b"tokenizer" in lib.hg_last_error()
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    """No fallback: without libhobbygpu.so every entry point raises."""
+    monkeypatch.setattr(_native, "_lib", None)
+    monkeypatch.setattr(_native, "LIB_PATH", str(tmp_path / "nope.so"))
+    with pytest.raises(ImportError):
+        _native.lib()

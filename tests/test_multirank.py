@@ -1,0 +1,69 @@
+"""The multi-GPU bench path on CPU ranks (gloo, world size 2): sequences are sharded with no
+collective on the decode path; the only collectives are the barrier and the max/sum reductions of
+the timing, which every rank takes in the same order."""
+import os
+import socket
+
+import pytest
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import bench
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        mine = bench.shard(256, rank, world)
+        elapsed = 1.0 + rank  # rank 1 is the slowest
+        mx = bench.reduce_max(elapsed, world)
+        tot = bench.reduce_sum(len(mine) * 32, world)
+        bench.barrier(world)
+        q.put((rank, mine, mx, tot))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_shard_and_timing_reduction():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    out.sort()
+    shards = [o[1] for o in out]
+    assert sorted(shards[0] + shards[1]) == list(range(256))
+    assert not set(shards[0]) & set(shards[1])
+    assert all(o[2] == 2.0 for o in out)  # max over ranks
+    assert all(o[3] == 256 * 32 for o in out)  # whole-job token count
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_shard_balance(world):
+    import bench
+
+    prompts = bench.workload(256)
+    loads = []
+    for r in range(world):
+        idx = bench.shard(256, r, world)
+        assert len(idx) == 256 // world
+        loads.append(sum(len(prompts[i]) for i in idx))
+    # round-robin keeps the per-rank KV (and so the step time) within a few percent
+    assert max(loads) / (sum(loads) / world) < 1.1
