@@ -25,7 +25,9 @@ EXPORTS = (
     "hg_q8_pack", "hg_q8_scale_stride", "hg_q8_unpack_qs", "hg_op_q8_matvec", "hg_op_q8_matmul",
     "hg_op_moe_scratch_bytes", "hg_op_moe_ffn", "hg_op_kv_attn_scratch_bytes", "hg_op_kv_attn", "hg_rope_tables",
     "hg_decode_greedy", "hg_engine_stream", "hg_decode_kernel_count", "hg_debug_time_attention",
+    "hg_op_q8_matvec_noalloc",
 )
+NOALLOC_SCRATCH_BYTES = 4 << 20  # HG_NOALLOC_SCRATCH_BYTES
 
 
 class HgError(RuntimeError):
@@ -107,6 +109,7 @@ def lib():
         "hg_q8_unpack_qs": (i32, [vp, i64, i64, vp]),
         "hg_op_q8_matvec": (i32, [vp, vp, i64, i64, vp, vp, i32, vp]),
         "hg_op_q8_matmul": (i32, [vp, vp, i64, i64, vp, vp, i32, vp]),
+        "hg_op_q8_matvec_noalloc": (i32, [vp, vp, i64, i64, vp, vp, i32, vp]),
         "hg_op_moe_scratch_bytes": (sz, [C.POINTER(MoeWeights), i32]),
         "hg_op_moe_ffn": (i32, [C.POINTER(MoeWeights), vp, i32, vp, vp, vp, vp]),
         "hg_op_kv_attn_scratch_bytes": (sz, [C.POINTER(KvAttnArgs)]),

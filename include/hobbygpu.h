@@ -151,6 +151,20 @@ int hg_q8_unpack_qs(const int8_t* packed, int64_t rows, int64_t cols, int8_t* qs
 int hg_op_q8_matvec(const int8_t* qs, const float* scales, int64_t rows, int64_t cols, const float* x, float* y,
                     int ntok, void* stream);
 
+/* No counterpart in the reference. The same computation as hg_op_q8_matvec, for callers that
+ * cannot allocate device memory: for example a host framework that has already handed all free
+ * device memory to its own pool, or a serving thread that must not block on the driver's
+ * allocation calls. hg_op_q8_matvec allocates its activation scratch on the stream; this variant
+ * uses a fixed HG_NOALLOC_SCRATCH_BYTES device array compiled into the library instead (every GPU
+ * that loads the library holds it until the process exits) and makes no allocation call. Sizes
+ * whose scratch (ntok * cols bytes + ntok * hg_q8_scale_stride(cols) * 4, rounded up) exceed it
+ * are rejected with HG_ERR_INVALID. All calls share the array: calls that overlap on the GPU
+ * race and must be ordered by the caller. The first call on a device looks up the array's device
+ * address with that device current; make that first call before any stream capture. */
+#define HG_NOALLOC_SCRATCH_BYTES (4u << 20)
+int hg_op_q8_matvec_noalloc(const int8_t* qs, const float* scales, int64_t rows, int64_t cols, const float* x,
+                            float* y, int ntok, void* stream);
+
 /* Q8Tensor::matmul (quant.rs:144-193): the prefill arithmetic (block-sequential mul-add). */
 int hg_op_q8_matmul(const int8_t* qs, const float* scales, int64_t rows, int64_t cols, const float* x, float* y,
                     int ntok, void* stream);
