@@ -1,16 +1,18 @@
 // Decode-step kernels (Model::forward, hobby-rs/src/model.rs:152-327) for T tokens of T sequences.
 //
 // Per layer: pre_norm (residual update + RMSNorm + activation quantization) -> QKV Q8 matvec ->
-// paged split-K attention with fused QK-norm/RoPE/append and in-kernel combine (writes the
-// quantized attention output) -> output projection with the residual add fused -> ffn RMSNorm +
+// paged attention: scores with fused QK-norm/RoPE/KV append, then the softmax denominator and the
+// probability-weighted value sums (which write the quantized attention output) -> output
+// projection with the residual add fused -> ffn RMSNorm +
 // router + top-k -> gate/up SwiGLU over active experts -> down projection. The MoE combine of a
 // layer is folded into the next layer's pre_norm. Finally output norm + lm_head + greedy argmax.
 //
 // Arithmetic: the Q8 matvec (quant.rs:44-67, 106-136), the activation quantization (quant.rs:
 // 112-123), the router dot (ops.rs:7-36), sigmoid/silu (ops.rs:75-82, exp pinned to
 // (float)exp((double)x)), top-k (model.rs:282-293) and the rank-order combine (model.rs:300-323)
-// reproduce the reference bit for bit given the same inputs. RMSNorm / QK-norm sums and the
-// attention softmax / value sums are parallel reductions (tolerance, not bit-exact).
+// reproduce the reference bit for bit given the same inputs, and so do the RMSNorm / QK-norm sums
+// and the attention softmax / value sums, which run sequentially in position order like the
+// reference's loops (one thread per chain).
 #include <cfloat>
 
 #include "hg_model.cuh"
@@ -870,6 +872,229 @@ __global__ void __launch_bounds__(HD) k_attn_out(AttnArgs A) {
 }
 
 // ------------------------------------------------------------------------------------------
+// Split attention output for batches with enough (token, kv head) pairs to fill the GPU.
+//
+// k_attn_softmax: one CTA per (token, q head). e = exp(s - max) goes back into S and the
+// sequential denominator (ops.rs:118-122) is summed by one thread from shared memory while the
+// other warps compute the next chunk's exponentials; 1/sum goes to rinv[t][h].
+// k_attn_pv: one CTA per (token, kv head), thread = output dim, one chain per q head of the group:
+// o_h[d] += (e_h,j * inv_h) * v_j[d] in position order (model.rs:227-232). The kv head's V rows
+// are read once for all its q heads, straight from the pool with a register prefetch of one page
+// (16 rows) ahead; probabilities are staged per 64-position chunk in a 3-slot shared ring.
+// ------------------------------------------------------------------------------------------
+constexpr int SMX_ECH = 1024;   // softmax positions per chunk
+constexpr int SMX_THREADS = 256;
+
+// sum = (((sum + e0) + e1) + ...) over eb[0..cnt), loads issued one 16-position group ahead
+__device__ __forceinline__ float seq_sum_smem(const float* eb, int cnt, float sum) {
+  const float4* e4 = reinterpret_cast<const float4*>(eb);
+  const int ng = cnt >> 4;
+  float4 a[4], b[4];
+  if (ng > 0) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) a[i] = e4[i];
+  }
+  int g = 0;
+  for (; g + 1 < ng; g += 2) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) b[i] = e4[(g + 1) * 4 + i];
+#pragma unroll
+    for (int i = 0; i < 4; i++) sum = fadd(fadd(fadd(fadd(sum, a[i].x), a[i].y), a[i].z), a[i].w);
+    if (g + 2 < ng) {
+#pragma unroll
+      for (int i = 0; i < 4; i++) a[i] = e4[(g + 2) * 4 + i];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) sum = fadd(fadd(fadd(fadd(sum, b[i].x), b[i].y), b[i].z), b[i].w);
+  }
+  if (g < ng) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) sum = fadd(fadd(fadd(fadd(sum, a[i].x), a[i].y), a[i].z), a[i].w);
+  }
+  for (int j = ng * 16; j < cnt; j++) sum = fadd(sum, eb[j]);
+  return sum;
+}
+
+__global__ void __launch_bounds__(SMX_THREADS) k_attn_softmax(AttnArgs A) {
+  constexpr int PER = (SMX_ECH + SMX_THREADS - 33) / (SMX_THREADS - 32);  // exps per thread (warps 1..)
+  __shared__ __align__(16) float ebuf[2][SMX_ECH];
+  __shared__ float m_s;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t = blockIdx.x / A.nh, h = blockIdx.x - t * A.nh;
+  const int pos = A.pos[t];
+  if (pos < 0 || pos >= A.max_pos) return;  // flagged by k_attn_scores
+  const int n = pos + 1, nch = (n + ATT_CHUNK - 1) / ATT_CHUNK;
+  float* erow = A.S + ((size_t)t * A.nh + h) * A.s_stride;
+  if (warp == 0) {  // max over the per-warp chunk maxima
+    const float* cm = A.cmax + ((size_t)t * A.nh + h) * (size_t)A.max_chunks * 8;
+    float m = -INFINITY;
+    for (int c = lane; c < nch * 8; c += 32) m = fmaxf(m, cm[c]);
+    m = warp_max(m);
+    if (lane == 0) m_s = m;
+  }
+  __syncthreads();
+  const float mrow = m_s;
+  const int nchunks = (n + SMX_ECH - 1) / SMX_ECH;
+  {
+    const int cnt = min(SMX_ECH, n);
+    float sv[SMX_ECH / SMX_THREADS];
+#pragma unroll
+    for (int k = 0; k < SMX_ECH / SMX_THREADS; k++) {
+      const int j = tid + k * SMX_THREADS;
+      sv[k] = j < cnt ? erow[j] : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < SMX_ECH / SMX_THREADS; k++) {
+      const int j = tid + k * SMX_THREADS;
+      if (j < cnt) {
+        const float e = exp_cr(__fsub_rn(sv[k], mrow));
+        ebuf[0][j] = e;
+        erow[j] = e;
+      }
+    }
+  }
+  __syncthreads();
+  float sum = 0.0f;
+  for (int c = 0; c < nchunks; c++) {
+    const int j0 = c * SMX_ECH, cnt = min(SMX_ECH, n - j0);
+    if (tid == 0) {
+      sum = seq_sum_smem(ebuf[c & 1], cnt, sum);
+    } else if (warp > 0 && c + 1 < nchunks) {
+      const int j1 = j0 + SMX_ECH, cn1 = min(SMX_ECH, n - j1), t1 = tid - 32;
+      float* eb = ebuf[(c + 1) & 1];
+      float sv[PER];
+#pragma unroll
+      for (int k = 0; k < PER; k++) {
+        const int j = t1 + k * (SMX_THREADS - 32);
+        sv[k] = j < cn1 ? erow[j1 + j] : 0.0f;
+      }
+#pragma unroll
+      for (int k = 0; k < PER; k++) {
+        const int j = t1 + k * (SMX_THREADS - 32);
+        if (j < cn1) {
+          const float e = exp_cr(__fsub_rn(sv[k], mrow));
+          eb[j] = e;
+          erow[j1 + j] = e;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (tid == 0) A.rinv[(size_t)t * A.nh + h] = __fdiv_rn(1.0f, sum);
+}
+
+template <int HD, int REP>
+__global__ void __launch_bounds__(HD, 8) k_attn_pv(AttnArgs A) {
+  constexpr int PC = 64;                          // positions per probability chunk (4 pages)
+  constexpr int PE = (PC * REP + HD - 1) / HD;    // staged probabilities per thread per chunk
+  extern __shared__ int bt_s[];                   // the sequence's page ids
+  __shared__ __align__(16) float p_s[3][PC][4];   // p of position j for the group's heads
+  __shared__ float inv_s[REP];
+  const int tid = threadIdx.x, lane = tid & 31, d = tid;
+  const int t = blockIdx.x / A.nkv, kvh = blockIdx.x - t * A.nkv;
+  const int pos = A.pos[t];
+  if (pos < 0 || pos >= A.max_pos) return;  // flagged by k_attn_scores
+  const int n = pos + 1, npages = (n + PAGE - 1) / PAGE, nchunk = (n + PC - 1) / PC;
+  const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
+  for (int p = tid; p < npages; p += HD) bt_s[p] = bt[p];
+  const int h0 = kvh * REP;
+  if (tid < REP) inv_s[tid] = A.rinv[(size_t)t * A.nh + h0 + tid];
+  const float* erow0 = A.S + ((size_t)t * A.nh + h0) * A.s_stride;
+  auto load_e = [&](int c, float (&ev)[PE]) {
+#pragma unroll
+    for (int k = 0; k < PE; k++) {
+      const int idx = tid + k * HD, r = idx / PC, jj = c * PC + (idx % PC);
+      ev[k] = (idx < PC * REP && jj < n) ? erow0[(size_t)r * A.s_stride + jj] : 0.0f;
+    }
+  };
+  auto store_p = [&](int c, const float (&ev)[PE]) {
+#pragma unroll
+    for (int k = 0; k < PE; k++) {
+      const int idx = tid + k * HD;
+      if (idx < PC * REP) p_s[c % 3][idx % PC][idx / PC] = fmul(ev[k], inv_s[idx / PC]);
+    }
+  };
+  const float* vbase = A.v_pool + (long long)kvh * PAGE * HD + d;
+  auto load_v = [&](int pg, float (&v)[PAGE]) {
+    const float* vp = vbase + (long long)bt_s[pg] * A.page_stride;
+    const int rows = min(PAGE, n - pg * PAGE);
+    if (rows == PAGE) {
+#pragma unroll
+      for (int r = 0; r < PAGE; r++) v[r] = vp[r * HD];
+    } else {
+#pragma unroll
+      for (int r = 0; r < PAGE; r++) v[r] = r < rows ? vp[r * HD] : 0.0f;
+    }
+  };
+  float o[REP];
+#pragma unroll
+  for (int r = 0; r < REP; r++) o[r] = 0.0f;
+  auto chain = [&](int pg, const float (&v)[PAGE], const float4* pq) {
+    const int rows = min(PAGE, n - pg * PAGE);
+    if (rows == PAGE) {
+#pragma unroll
+      for (int r = 0; r < PAGE; r++) {
+        const float4 p = pq[r];
+        o[0] = fadd(o[0], fmul(p.x, v[r]));
+        if (REP > 1) o[REP > 1 ? 1 : 0] = fadd(o[REP > 1 ? 1 : 0], fmul(p.y, v[r]));
+        if (REP > 2) o[REP > 2 ? 2 : 0] = fadd(o[REP > 2 ? 2 : 0], fmul(p.z, v[r]));
+        if (REP > 3) o[REP > 3 ? 3 : 0] = fadd(o[REP > 3 ? 3 : 0], fmul(p.w, v[r]));
+      }
+    } else {
+#pragma unroll
+      for (int r = 0; r < PAGE; r++) {
+        if (r < rows) {
+          const float4 p = pq[r];
+          o[0] = fadd(o[0], fmul(p.x, v[r]));
+          if (REP > 1) o[REP > 1 ? 1 : 0] = fadd(o[REP > 1 ? 1 : 0], fmul(p.y, v[r]));
+          if (REP > 2) o[REP > 2 ? 2 : 0] = fadd(o[REP > 2 ? 2 : 0], fmul(p.z, v[r]));
+          if (REP > 3) o[REP > 3 ? 3 : 0] = fadd(o[REP > 3 ? 3 : 0], fmul(p.w, v[r]));
+        }
+      }
+    }
+  };
+  float ev[PE];
+  load_e(0, ev);
+  __syncthreads();  // bt_s, inv_s
+  store_p(0, ev);
+  if (nchunk > 1) load_e(1, ev);
+  float va[PAGE], vb[PAGE];
+  load_v(0, va);
+  for (int c = 0; c < nchunk; c++) {
+    if (c + 1 < nchunk) store_p(c + 1, ev);
+    if (c + 2 < nchunk) load_e(c + 2, ev);
+    __syncthreads();  // chunk c's probabilities are staged; slot (c + 1) % 3 is no longer read
+    const float4* pc = reinterpret_cast<const float4*>(&p_s[c % 3][0][0]);
+    // pages 4c .. 4c+3 in pairs, ping-ponging between the two register buffers
+#pragma unroll
+    for (int q = 0; q < PC / PAGE; q += 2) {
+      const int pg = c * (PC / PAGE) + q;
+      if (pg < npages) {
+        if (pg + 1 < npages) load_v(pg + 1, vb);
+        chain(pg, va, pc + q * PAGE);
+      }
+      if (pg + 1 < npages) {
+        if (pg + 2 < npages) load_v(pg + 2, va);
+        chain(pg + 1, vb, pc + (q + 1) * PAGE);
+      }
+    }
+  }
+  const int qd = A.nh * HD;
+#pragma unroll
+  for (int r = 0; r < REP; r++) {
+    const int hd = (h0 + r) * HD + d;
+    if (A.out) A.out[(size_t)t * qd + hd] = o[r];
+    if (A.qo) {  // a warp holds one 32-block of the head
+      float dq;
+      int8_t q = quant_lane(o[r], &dq);
+      const int nbq = qd >> 5;
+      A.qo[(size_t)t * qd + q8_pos(hd, nbq)] = q;
+      if (lane == 0) A.so[(size_t)t * q8_ss(nbq) + (hd >> 5)] = dq;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
 // Greedy feedback at the end of a decode step: each token's masked argmax (sample.rs:53-64)
 // becomes its next input, the position advances, and the id is stored in a ring of generated ids
 // (gen[(step % gen_cap) * T + t]) whose step counter lives in device memory.
@@ -1005,11 +1230,25 @@ int attn_grid(int T, int nkv, int max_chunks) {
   return (int)(g > 0 ? g : 1);
 }
 
+// Batches whose (token, kv head) pairs fill at least this many CTAs take the split output path
+// (k_attn_softmax + k_attn_pv); smaller ones keep one CTA per (token, q head) with a V ring.
+constexpr int ATT_SPLIT_MIN_CTAS = 64;
+
+bool attn_split(int T, int nkv) { return T * nkv >= ATT_SPLIT_MIN_CTAS; }
+
 template <int HD, int REP>
 static cudaError_t launch_attn_t(const AttnArgs& A, int grid, cudaStream_t st, int which) {
   if (which & 1) k_attn_scores<HD, REP><<<grid, 256, 0, st>>>(A);
-  const size_t smem = (size_t)A.stages * PAGE * HD * 4 + (size_t)A.bt_stride * 4;
-  if (which & 2) k_attn_out<HD><<<A.T * A.nh, HD, smem, st>>>(A);
+  if (which & 2) {
+    if (attn_split(A.T, A.nkv)) {
+      if (!A.rinv) return cudaErrorInvalidValue;
+      k_attn_softmax<<<A.T * A.nh, SMX_THREADS, 0, st>>>(A);
+      k_attn_pv<HD, REP><<<A.T * A.nkv, HD, (size_t)A.bt_stride * 4, st>>>(A);
+    } else {
+      const size_t smem = (size_t)A.stages * PAGE * HD * 4 + (size_t)A.bt_stride * 4;
+      k_attn_out<HD><<<A.T * A.nh, HD, smem, st>>>(A);
+    }
+  }
   return cudaGetLastError();
 }
 

@@ -10,6 +10,7 @@
 #include <numeric>
 #include <random>
 #include <string>
+#include <unordered_set>
 #include <vector>
 
 #include "hg_host.h"
@@ -85,6 +86,7 @@ struct hg_engine {
   int32_t* d_bt = nullptr;  // [max_rows][bt_stride]
   int bt_stride = 0, max_rows = 0;
   std::vector<int> free_rows;
+  std::unordered_set<hg_seq*> live_seqs;  // detached (s->e = null) when the engine is freed
   // decode buffers
   int max_batch = 1;
   DecodeBufs buf{};
@@ -231,6 +233,7 @@ void alloc_work(hg_engine* e) {
   B.S = a.take<float>((size_t)T * c.n_heads * B.s_stride);
   B.cmax = a.take<float>((size_t)T * c.n_heads * max_chunks * 8);
   B.max_chunks = max_chunks;
+  B.rinv = a.take<float>((size_t)T * c.n_heads);
   B.logits = a.take<float>((size_t)T * c.vocab_size);
   B.amax = a.take<unsigned long long>(T);
   B.dbg_sel = a.take<int32_t>((size_t)c.n_layers * T * k);
@@ -389,6 +392,8 @@ void load_engine(hg_engine* e, const char* path, const hg_engine_opts& o) {
 
 void free_engine(hg_engine* e) {
   if (!e) return;
+  for (hg_seq* s : e->live_seqs) s->e = nullptr;  // their pages go with the pool below
+  e->live_seqs.clear();
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
   for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
@@ -449,6 +454,7 @@ AttnArgs make_attn_args(hg_engine* e, const DecodeBufs& B, int l) {
   A.S = B.S;
   A.s_stride = B.s_stride;
   A.cmax = B.cmax;
+  A.rinv = B.rinv;
   A.stages = B.T < 8 ? 24 : 8;  // few CTAs: each streams its V alone, so keep more pages in flight
   A.out = nullptr;
   A.qo = B.qo;
@@ -821,14 +827,17 @@ hg_seq* seq_create(hg_engine* e, int max_ctx) {
   s->row = e->free_rows.back();
   e->free_rows.pop_back();
   s->max_ctx = max_ctx;
+  e->live_seqs.insert(s);
   return s;
 }
 
 void seq_free(hg_seq* s) {
   if (!s) return;
-  hg_engine* e = s->e;
-  for (int p : s->pages) e->free_pages.push_back(p);
-  e->free_rows.push_back(s->row);
+  if (hg_engine* e = s->e) {
+    for (int p : s->pages) e->free_pages.push_back(p);
+    e->free_rows.push_back(s->row);
+    e->live_seqs.erase(s);
+  }
   delete s;
 }
 
@@ -958,7 +967,8 @@ size_t kv_s_stride(const hg_kv_attn_args* a) { return ((size_t)a->max_pos + 15) 
 size_t kv_scratch_bytes(const hg_kv_attn_args* a) {
   int max_chunks = (a->max_pos + ATT_CHUNK - 1) / ATT_CHUNK;
   return align256((size_t)a->n_seqs * a->n_heads * kv_s_stride(a) * 4) +
-         align256((size_t)a->n_seqs * a->n_heads * max_chunks * 8 * 4) + 256;
+         align256((size_t)a->n_seqs * a->n_heads * max_chunks * 8 * 4) +
+         align256((size_t)a->n_seqs * a->n_heads * 4) + 256;
 }
 
 }  // namespace
@@ -1302,7 +1312,9 @@ int hg_op_kv_attn(const hg_kv_attn_args* a, void* scratch, void* stream) {
     A.page_stride = a->page_stride;
     A.s_stride = (long long)kv_s_stride(a);
     A.S = reinterpret_cast<float*>(base);
-    A.cmax = reinterpret_cast<float*>(base + align256((size_t)a->n_seqs * a->n_heads * A.s_stride * 4));
+    const size_t s_bytes = align256((size_t)a->n_seqs * a->n_heads * A.s_stride * 4);
+    A.cmax = reinterpret_cast<float*>(base + s_bytes);
+    A.rinv = reinterpret_cast<float*>(base + s_bytes + align256((size_t)a->n_seqs * a->n_heads * max_chunks * 8 * 4));
     A.err = nullptr;
     A.stages = a->n_seqs < 8 ? 24 : 8;
     A.out = a->out;

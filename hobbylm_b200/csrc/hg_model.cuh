@@ -73,6 +73,7 @@ struct DecodeBufs {
   float* y;                // [T][k + 1][d] expert outputs per (token, slot)
   float* S;                // [T][nh][s_stride] attention scores / exp weights
   long long s_stride;
+  float* rinv;             // [T][nh] 1 / softmax denominator
   float* cmax;             // [T][nh][max_chunks][8] per-warp chunk maxima of the scores
   int max_chunks;
   float* logits;           // [T][vocab] or null
@@ -99,6 +100,7 @@ struct AttnArgs {
   long long page_stride;
   float* S;        // [T][nh][s_stride] scores, then exp(score - max)
   long long s_stride;  // >= max_pos, multiple of 16
+  float* rinv;     // [T][nh] 1 / softmax denominator (split path)
   float* cmax;     // [T][nh][max_chunks][8] per-warp chunk maxima of the scores
   int stages;      // V pages in flight per k_attn_out CTA (2..24, even)
   float* out;      // [T][nh*hd] or null

@@ -89,6 +89,8 @@ uint64_t hg_engine_device_bytes(const hg_engine* e);
 /* KvCache::new (model.rs:66-75): a sequence with room for max_ctx positions (<= context_length),
  * backed by pages of the engine's pool. */
 int hg_seq_create(hg_engine* e, int max_ctx, hg_seq** out);
+/* Returns the sequence's pages to its engine. A sequence still open when its engine is freed loses
+ * its pages with the engine; hg_seq_free is then the only call it may still be passed to. */
 void hg_seq_free(hg_seq* s);
 int hg_seq_len(const hg_seq* s);
 

@@ -135,6 +135,52 @@ def test_batched_decode_equals_single(engine130):
         c.close()
 
 
+def test_wide_batch_equals_single(model130):
+    """48 sequences fill enough (token, kv head) CTAs for the split softmax / value-sum kernels;
+    each row must equal the one-sequence path bit for bit (lengths cross page, 64-position chunk
+    and 1024-position softmax chunk boundaries)."""
+    from hobbylm_b200 import Engine
+
+    lens = [1, 15, 16, 17, 63, 64, 65, 127, 1023, 1024, 1025, 2100] + [30 + 37 * i for i in range(36)]
+    eng = Engine.load(model130, max_batch=96, kv_pool_tokens=80000)
+    try:
+        prompts = [synth.prompt_ids(n, 500 + i) for i, n in enumerate(lens)]
+        cb = [eng.new_cache() for _ in prompts]
+        cs = [eng.new_cache() for _ in prompts]
+        toks = []
+        for p, a, b in zip(prompts, cb, cs):
+            la = eng.prefill(a, p)
+            eng.prefill(b, p)
+            la[50257:] = -np.inf
+            toks.append(int(np.argmax(la)))
+        tb, ts = list(toks), list(toks)
+        for _ in range(3):
+            nb, lb = eng.decode_batch(cb, tb, want_logits=True)
+            for i, c in enumerate(cs):
+                ls, n1 = eng.forward(c, ts[i])
+                assert np.array_equal(ls.view(np.uint32), lb[i].view(np.uint32)), (i, lens[i])
+                ts[i] = n1
+            tb = [int(v) for v in nb]
+            assert tb == ts
+        for c in cb + cs:
+            c.close()
+    finally:
+        eng.close()
+
+
+def test_engine_freed_before_its_caches(model130):
+    """Sequences left open when their engine is freed can still be closed (no use after free)."""
+    from hobbylm_b200 import Engine
+
+    eng = Engine.load(model130, max_batch=2)
+    a, b = eng.new_cache(), eng.new_cache()
+    eng.prefill(a, [1, 2, 3])
+    eng.close()
+    assert a.len == 3
+    a.close()
+    b.close()
+
+
 def test_errors(engine130, model130):
     from hobbylm_b200 import Engine
 
