@@ -187,10 +187,13 @@ __device__ inline void stage_rows(int8_t* aq_s, float* as_s, const int8_t* q, co
 
 enum { EPI_STORE = 0, EPI_RESID = 1, EPI_LMHEAD = 2 };
 
-// Rows of one matrix against all T tokens' activations (aq/as rows t, strides cols / ss).
+// Rows of one matrix against the tokens of chunk blockIdx.y (TY tokens; aq/as rows t, strides
+// cols / ss), TT tokens staged in shared memory at a time; two tokens' dots are in flight per
+// thread so their FMA chains overlap.
 template <int NB, int ROWS, int TT, int EPI>
 __global__ void __launch_bounds__(ROWS * 8) k_mv_tokens(Dims D, DecodeBufs B, Q8M W, const int8_t* __restrict__ aq,
-                                                         const float* __restrict__ as, float* out, int ostride) {
+                                                         const float* __restrict__ as, float* out, int ostride,
+                                                         int ty) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int cols = W.cols, nb = cols >> 5, ss = W.ss;
   int8_t* aq_s = reinterpret_cast<int8_t*>(smem);
@@ -198,34 +201,42 @@ __global__ void __launch_bounds__(ROWS * 8) k_mv_tokens(Dims D, DecodeBufs B, Q8
   const int lane = threadIdx.x & 7, rl = threadIdx.x >> 3;
   const int row = blockIdx.x * ROWS + rl;
   const bool valid_row = row < W.rows;
+  const int tbeg = blockIdx.y * ty, tend = min(B.T, tbeg + ty);
+  if (tbeg >= tend) return;
   RowDot<NB> rd;
   rd.init(W.row_q(0, valid_row ? row : 0), W.row_s(0, valid_row ? row : 0), lane, nb);
   __shared__ unsigned long long best_s[TT > 0 ? TT : 1];
-  for (int t0 = 0; t0 < B.T; t0 += TT) {
-    int n = min(TT, B.T - t0);
+  auto emit = [&](int i, int t, float v) {
+    if (EPI == EPI_STORE) {
+      if (lane == 0 && valid_row) out[(size_t)t * ostride + row] = v;
+    } else if (EPI == EPI_RESID) {
+      if (lane == 0 && valid_row) {
+        float* xp = B.x + (size_t)t * D.d + row;
+        *xp = fadd(*xp, v);
+      }
+    } else {
+      if (lane == 0 && valid_row && out) out[(size_t)t * ostride + row] = v;
+      unsigned long long key = (valid_row && row < D.valid) ? argmax_key(v, (uint32_t)row) : 0ull;
+      key = max(key, __shfl_xor_sync(0xffffffffu, key, 8));
+      key = max(key, __shfl_xor_sync(0xffffffffu, key, 16));
+      if ((threadIdx.x & 31) == 0) atomicMax(&best_s[i], key);
+    }
+  };
+  for (int t0 = tbeg; t0 < tend; t0 += TT) {
+    int n = min(TT, tend - t0);
     __syncthreads();
     stage_rows(aq_s, as_s, aq + (size_t)t0 * cols, as + (size_t)t0 * ss, nullptr, n, cols, ss, cols, ss);
     if (EPI == EPI_LMHEAD && threadIdx.x < TT) best_s[threadIdx.x] = 0ull;
     __syncthreads();
+    int i = 0;
 #pragma unroll 1
-    for (int i = 0; i < n; i++) {
-      float v = hsum8_group(rd.dot(aq_s + (size_t)i * cols, as_s + (size_t)i * ss, lane));
-      int t = t0 + i;
-      if (EPI == EPI_STORE) {
-        if (lane == 0 && valid_row) out[(size_t)t * ostride + row] = v;
-      } else if (EPI == EPI_RESID) {
-        if (lane == 0 && valid_row) {
-          float* xp = B.x + (size_t)t * D.d + row;
-          *xp = fadd(*xp, v);
-        }
-      } else {
-        if (lane == 0 && valid_row && out) out[(size_t)t * ostride + row] = v;
-        unsigned long long key = (valid_row && row < D.valid) ? argmax_key(v, (uint32_t)row) : 0ull;
-        key = max(key, __shfl_xor_sync(0xffffffffu, key, 8));
-        key = max(key, __shfl_xor_sync(0xffffffffu, key, 16));
-        if ((threadIdx.x & 31) == 0) atomicMax(&best_s[i], key);
-      }
+    for (; i + 1 < n; i += 2) {
+      const float a0 = rd.dot(aq_s + (size_t)i * cols, as_s + (size_t)i * ss, lane);
+      const float a1 = rd.dot(aq_s + (size_t)(i + 1) * cols, as_s + (size_t)(i + 1) * ss, lane);
+      emit(i, t0 + i, hsum8_group(a0));
+      emit(i + 1, t0 + i + 1, hsum8_group(a1));
     }
+    if (i < n) emit(i, t0 + i, hsum8_group(rd.dot(aq_s + (size_t)i * cols, as_s + (size_t)i * ss, lane)));
     if (EPI == EPI_LMHEAD) {
       __syncthreads();
       if (threadIdx.x < n) atomicMax(&B.amax[t0 + threadIdx.x], best_s[threadIdx.x]);
@@ -322,7 +333,7 @@ __global__ void __launch_bounds__(256) k_route(Dims D, DecodeBufs B, LayerDev Ld
 // same rows of up (16 lanes per pair) and writes act = silu(g) * u for every token of the group.
 // ------------------------------------------------------------------------------------------
 template <int NB, int PAIRS, int TT>
-__global__ void __launch_bounds__(PAIRS * 16) k_ffn_up(Dims D, DecodeBufs B, LayerDev Ld) {
+__global__ void __launch_bounds__(PAIRS * 16) k_ffn_up(Dims D, DecodeBufs B, LayerDev Ld, int ez) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ int ent_s[TT];
   const int cols = D.d, nb = cols >> 5, ss = q8_ss(nb);
@@ -348,10 +359,12 @@ __global__ void __launch_bounds__(PAIRS * 16) k_ffn_up(Dims D, DecodeBufs B, Lay
   const Q8M M = grp == 0 ? (Ld.moe ? (is_up ? Ld.sup : Ld.sgate) : (is_up ? Ld.up : Ld.gate))
                          : (is_up ? Ld.up : Ld.gate);
   const int mi = grp == 0 ? 0 : expert;
+  const int ebeg = blockIdx.z * ez, eend = min(nent, ebeg + ez);
+  if (ebeg >= eend) return;
   RowDot<NB> rd;
   rd.init(M.row_q(mi, valid_row ? row : 0), M.row_s(mi, valid_row ? row : 0), lane, nb);
-  for (int e0 = 0; e0 < nent; e0 += TT) {
-    int n = min(TT, nent - e0);
+  for (int e0 = ebeg; e0 < eend; e0 += TT) {
+    int n = min(TT, eend - e0);
     __syncthreads();
     if (threadIdx.x < n) {
       int code = grp == 0 ? (e0 + threadIdx.x) * 32 : B.elist[(size_t)expert * B.T + e0 + threadIdx.x];
@@ -369,16 +382,23 @@ __global__ void __launch_bounds__(PAIRS * 16) k_ffn_up(Dims D, DecodeBufs B, Lay
       as_s[(size_t)r * ss + c] = B.sh[(size_t)t * ss + c];
     }
     __syncthreads();
-#pragma unroll 1
-    for (int i = 0; i < n; i++) {
-      float v = hsum8_group(rd.dot(aq_s + (size_t)i * cols, as_s + (size_t)i * ss, lane));
+    auto emit = [&](int i, float v) {
       float u = __shfl_down_sync(0xffffffffu, v, 8);  // up row value from the neighbouring group
       if (!is_up && lane == 0 && valid_row) {
         int code = ent_s[i], t = code >> 5, r = code & 31;
         int slot = grp == 0 ? (Ld.moe ? D.k : 0) : r;
         B.act[(size_t)t * B.act_stride + (size_t)slot * fdim + row] = fmul(silu_ref(v), u);
       }
+    };
+    int i = 0;
+#pragma unroll 1
+    for (; i + 1 < n; i += 2) {
+      const float a0 = rd.dot(aq_s + (size_t)i * cols, as_s + (size_t)i * ss, lane);
+      const float a1 = rd.dot(aq_s + (size_t)(i + 1) * cols, as_s + (size_t)(i + 1) * ss, lane);
+      emit(i, hsum8_group(a0));
+      emit(i + 1, hsum8_group(a1));
     }
+    if (i < n) emit(i, hsum8_group(rd.dot(aq_s + (size_t)i * cols, as_s + (size_t)i * ss, lane)));
   }
 }
 
@@ -388,7 +408,7 @@ __global__ void __launch_bounds__(PAIRS * 16) k_ffn_up(Dims D, DecodeBufs B, Lay
 // matrix; y[t][slot][row] = result.
 // ------------------------------------------------------------------------------------------
 template <int NB, int ROWS, int TT>
-__global__ void __launch_bounds__(ROWS * 8) k_ffn_down(Dims D, DecodeBufs B, LayerDev Ld) {
+__global__ void __launch_bounds__(ROWS * 8) k_ffn_down(Dims D, DecodeBufs B, LayerDev Ld, int ez) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ int ent_s[TT];
   const int grp = blockIdx.y;
@@ -411,10 +431,12 @@ __global__ void __launch_bounds__(ROWS * 8) k_ffn_down(Dims D, DecodeBufs B, Lay
   const int row = blockIdx.x * ROWS + rl;
   const bool valid_row = row < D.d;
   const int mi = grp == 0 ? 0 : expert;
+  const int ebeg = blockIdx.z * ez, eend = min(nent, ebeg + ez);
+  if (ebeg >= eend) return;
   RowDot<NB> rd;
   rd.init(W.row_q(mi, valid_row ? row : 0), W.row_s(mi, valid_row ? row : 0), lane, nb);
-  for (int e0 = 0; e0 < nent; e0 += TT) {
-    int n = min(TT, nent - e0);
+  for (int e0 = ebeg; e0 < eend; e0 += TT) {
+    int n = min(TT, eend - e0);
     __syncthreads();
     if (threadIdx.x < n) {
       int code = grp == 0 ? (e0 + threadIdx.x) * 32 : B.elist[(size_t)expert * B.T + e0 + threadIdx.x];
@@ -436,15 +458,22 @@ __global__ void __launch_bounds__(ROWS * 8) k_ffn_down(Dims D, DecodeBufs B, Lay
       }
     }
     __syncthreads();
-#pragma unroll 1
-    for (int i = 0; i < n; i++) {
-      float v = hsum8_group(rd.dot(aq_s + (size_t)i * cols, as_s + (size_t)i * ss, lane));
+    auto emit = [&](int i, float v) {
       if (lane == 0 && valid_row) {
         int code = ent_s[i], t = code >> 5, rk = code & 31;
         int slot = grp == 0 ? (Ld.moe ? D.k : 0) : rk;
         B.y[((size_t)t * (D.k + 1) + slot) * D.d + row] = v;
       }
+    };
+    int i = 0;
+#pragma unroll 1
+    for (; i + 1 < n; i += 2) {
+      const float a0 = rd.dot(aq_s + (size_t)i * cols, as_s + (size_t)i * ss, lane);
+      const float a1 = rd.dot(aq_s + (size_t)(i + 1) * cols, as_s + (size_t)(i + 1) * ss, lane);
+      emit(i, hsum8_group(a0));
+      emit(i + 1, hsum8_group(a1));
     }
+    if (i < n) emit(i, hsum8_group(rd.dot(aq_s + (size_t)i * cols, as_s + (size_t)i * ss, lane)));
   }
 }
 
@@ -1141,6 +1170,9 @@ __global__ void __launch_bounds__(256) k_quant_rows(const float* x, int cols, in
     default: { constexpr int NB = 0; __VA_ARGS__; } break;  \
   }
 
+constexpr int MV_TY = 16;  // tokens per CTA of the batched matvec
+constexpr int FFN_EZ = 16;  // (token, slot) entries per CTA of the batched expert kernels
+
 static inline size_t act_smem(int tt, int cols) { return (size_t)tt * cols + (size_t)tt * q8_ss(cols >> 5) * 4; }
 
 template <int EPI>
@@ -1150,11 +1182,13 @@ static void launch_mv_tokens_t(const Dims& D, const DecodeBufs& B, const Q8M& W,
   if (B.T == 1) {
     constexpr int ROWS = 8, TT = 1;
     dim3 grid((W.rows + ROWS - 1) / ROWS);
-    HG_NB_SWITCH(nb, k_mv_tokens<NB, ROWS, TT, EPI><<<grid, ROWS * 8, act_smem(TT, W.cols), st>>>(D, B, W, aq, as, out, ostride));
+    HG_NB_SWITCH(nb, k_mv_tokens<NB, ROWS, TT, EPI><<<grid, ROWS * 8, act_smem(TT, W.cols), st>>>(D, B, W, aq, as, out, ostride, 1));
   } else {
     constexpr int ROWS = 32, TT = 8;
-    dim3 grid((W.rows + ROWS - 1) / ROWS);
-    HG_NB_SWITCH(nb, k_mv_tokens<NB, ROWS, TT, EPI><<<grid, ROWS * 8, act_smem(TT, W.cols), st>>>(D, B, W, aq, as, out, ostride));
+    // token chunks of MV_TY tokens: enough CTAs for small matrices, weights re-read from L2 per chunk
+    const int ty = MV_TY;
+    dim3 grid((W.rows + ROWS - 1) / ROWS, (B.T + ty - 1) / ty);
+    HG_NB_SWITCH(nb, k_mv_tokens<NB, ROWS, TT, EPI><<<grid, ROWS * 8, act_smem(TT, W.cols), st>>>(D, B, W, aq, as, out, ostride, ty));
   }
 }
 
@@ -1202,25 +1236,27 @@ void launch_ffn(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaStrea
   const int groups = L.moe ? 1 + (D.ne < B.T * D.k ? D.ne : B.T * D.k) : 1;
   const int fdim = L.moe ? D.f : D.df;
   const int nb_up = D.d >> 5;
+  // entry chunks on grid.z: a group holds at most T entries (each token uses an expert once)
+  const int ez = B.T == 1 ? 1 : FFN_EZ, nz = (B.T + ez - 1) / ez;
   if (B.T == 1) {
     constexpr int PAIRS = 16, TT = 1;
-    dim3 grid((fdim + PAIRS - 1) / PAIRS, groups);
-    HG_NB_SWITCH(nb_up, k_ffn_up<NB, PAIRS, TT><<<grid, PAIRS * 16, act_smem(TT, D.d), st>>>(D, B, L));
+    dim3 grid((fdim + PAIRS - 1) / PAIRS, groups, nz);
+    HG_NB_SWITCH(nb_up, k_ffn_up<NB, PAIRS, TT><<<grid, PAIRS * 16, act_smem(TT, D.d), st>>>(D, B, L, ez));
   } else {
     constexpr int PAIRS = 16, TT = 8;
-    dim3 grid((fdim + PAIRS - 1) / PAIRS, groups);
-    HG_NB_SWITCH(nb_up, k_ffn_up<NB, PAIRS, TT><<<grid, PAIRS * 16, act_smem(TT, D.d), st>>>(D, B, L));
+    dim3 grid((fdim + PAIRS - 1) / PAIRS, groups, nz);
+    HG_NB_SWITCH(nb_up, k_ffn_up<NB, PAIRS, TT><<<grid, PAIRS * 16, act_smem(TT, D.d), st>>>(D, B, L, ez));
   }
   // dense layers and the shared expert use the down matrix of their own width
   const int nb_dn = fdim >> 5;
   if (B.T == 1) {
     constexpr int ROWS = 8, TT = 1;
-    dim3 grid((D.d + ROWS - 1) / ROWS, groups);
-    HG_NB_SWITCH(nb_dn, k_ffn_down<NB, ROWS, TT><<<grid, ROWS * 8, act_smem(TT, fdim), st>>>(D, B, L));
+    dim3 grid((D.d + ROWS - 1) / ROWS, groups, nz);
+    HG_NB_SWITCH(nb_dn, k_ffn_down<NB, ROWS, TT><<<grid, ROWS * 8, act_smem(TT, fdim), st>>>(D, B, L, ez));
   } else {
     constexpr int ROWS = 32, TT = 8;
-    dim3 grid((D.d + ROWS - 1) / ROWS, groups);
-    HG_NB_SWITCH(nb_dn, k_ffn_down<NB, ROWS, TT><<<grid, ROWS * 8, act_smem(TT, fdim), st>>>(D, B, L));
+    dim3 grid((D.d + ROWS - 1) / ROWS, groups, nz);
+    HG_NB_SWITCH(nb_dn, k_ffn_down<NB, ROWS, TT><<<grid, ROWS * 8, act_smem(TT, fdim), st>>>(D, B, L, ez));
   }
 }
 
