@@ -533,8 +533,12 @@ __device__ __forceinline__ void norm_rope_warp(const float* src, const float* w,
 }
 
 // Work split of k_attn_scores: each item is (token, kv head, run of G consecutive chunks) with G
-// chosen so the items roughly fill the grid. prefix_s[t] = first item of token t; returns the
+// chosen so that there are about ATT_ITEMS_PER_CTA items per CTA: items are dealt round-robin, and
+// several smaller items per CTA keep the most loaded CTA near the mean (one item per CTA left
+// some CTAs with two full items, twice the mean). prefix_s[t] = first item of token t; returns the
 // item count and writes G to *g_out. Positions beyond max_pos raise an error.
+constexpr int ATT_ITEMS_PER_CTA = 8;
+
 __device__ inline int attn_item_prefix(const AttnArgs& A, int* prefix_s, int* g_s) {
   if (threadIdx.x == 0) {
     long long chunks = 0;
@@ -543,7 +547,7 @@ __device__ inline int attn_item_prefix(const AttnArgs& A, int* prefix_s, int* g_
       int nch = (p + 1 + ATT_CHUNK - 1) / ATT_CHUNK;
       if (p >= 0 && p < A.max_pos && nch <= A.max_chunks) chunks += nch;
     }
-    long long want = (long long)gridDim.x;
+    long long want = (long long)gridDim.x * ATT_ITEMS_PER_CTA;
     int G = (int)((chunks * A.nkv + want - 1) / want);
     G = G < 1 ? 1 : G;
     int acc = 0;
@@ -624,8 +628,20 @@ __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
 #pragma unroll
         for (int m = 0; m < 4; m++) qv[h][i][m] = q_s[h][32 * i + 8 * m + l];
     float* srow = A.S + ((size_t)t * A.nh + kvh * REP) * A.s_stride;
+    const float* kbase = A.k_pool + (long long)kvh * PAGE * HD;
+    auto prefetch_rows = [&](int c) {
+      const int p = c * ATT_CHUNK + warp * 8 + (lane >> 2);
+      if (c < cend && p < n && p != pos) {
+        const int pgi = p / PAGE - pg0;
+        const int page = pgi < 1024 ? pg_s[pgi] : bt[p / PAGE];
+        const float* r = kbase + (long long)page * A.page_stride + (long long)(p % PAGE) * HD + (lane & 3) * (HD / 4);
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(r));
+      }
+    };
+    prefetch_rows(cbeg);
     for (int c = cbeg; c < cend; c++) {
       const int c0 = c * ATT_CHUNK;
+      prefetch_rows(c + 1);
       float mx[REP];
 #pragma unroll
       for (int h = 0; h < REP; h++) mx[h] = -INFINITY;
@@ -1012,102 +1028,93 @@ __global__ void __launch_bounds__(SMX_THREADS) k_attn_softmax(AttnArgs A) {
   if (tid == 0) A.rinv[(size_t)t * A.nh + h] = __fdiv_rn(1.0f, sum);
 }
 
+constexpr int PV_SLOTS = 4;  // V pages in shared memory per k_attn_pv CTA (two in flight)
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 template <int HD, int REP>
-__global__ void __launch_bounds__(HD, 8) k_attn_pv(AttnArgs A) {
-  constexpr int PC = 64;                          // positions per probability chunk (4 pages)
-  constexpr int PE = (PC * REP + HD - 1) / HD;    // staged probabilities per thread per chunk
-  extern __shared__ int bt_s[];                   // the sequence's page ids
-  __shared__ __align__(16) float p_s[3][PC][4];   // p of position j for the group's heads
+__global__ void __launch_bounds__(HD) k_attn_pv(AttnArgs A) {
+  constexpr int SEG = PAGE * HD / 4;  // 16-byte segments per V page
+  extern __shared__ __align__(16) unsigned char dsm[];
+  float* v_s = reinterpret_cast<float*>(dsm);                            // [PV_SLOTS][PAGE][HD]
+  int* bt_s = reinterpret_cast<int*>(dsm + (size_t)PV_SLOTS * PAGE * HD * 4);  // page ids
+  __shared__ __align__(16) float p_s[3][PAGE][4];  // p of each row of a page for the group's heads
   __shared__ float inv_s[REP];
   const int tid = threadIdx.x, lane = tid & 31, d = tid;
   const int t = blockIdx.x / A.nkv, kvh = blockIdx.x - t * A.nkv;
   const int pos = A.pos[t];
   if (pos < 0 || pos >= A.max_pos) return;  // flagged by k_attn_scores
-  const int n = pos + 1, npages = (n + PAGE - 1) / PAGE, nchunk = (n + PC - 1) / PC;
+  const int n = pos + 1, npages = (n + PAGE - 1) / PAGE;
   const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
   for (int p = tid; p < npages; p += HD) bt_s[p] = bt[p];
   const int h0 = kvh * REP;
   if (tid < REP) inv_s[tid] = A.rinv[(size_t)t * A.nh + h0 + tid];
   const float* erow0 = A.S + ((size_t)t * A.nh + h0) * A.s_stride;
-  auto load_e = [&](int c, float (&ev)[PE]) {
-#pragma unroll
-    for (int k = 0; k < PE; k++) {
-      const int idx = tid + k * HD, r = idx / PC, jj = c * PC + (idx % PC);
-      ev[k] = (idx < PC * REP && jj < n) ? erow0[(size_t)r * A.s_stride + jj] : 0.0f;
-    }
+  const float* vpage0 = A.v_pool + (long long)kvh * PAGE * HD;
+  // e of (head tid / PAGE, row tid % PAGE) of page pg, for the first PAGE * REP threads
+  auto load_e = [&](int pg) -> float {
+    const int jj = pg * PAGE + (tid % PAGE);
+    return (tid < PAGE * REP && jj < n) ? erow0[(size_t)(tid / PAGE) * A.s_stride + jj] : 0.0f;
   };
-  auto store_p = [&](int c, const float (&ev)[PE]) {
-#pragma unroll
-    for (int k = 0; k < PE; k++) {
-      const int idx = tid + k * HD;
-      if (idx < PC * REP) p_s[c % 3][idx % PC][idx / PC] = fmul(ev[k], inv_s[idx / PC]);
-    }
+  auto store_p = [&](int pg, float e) {
+    if (tid < PAGE * REP) p_s[pg % 3][tid % PAGE][tid / PAGE] = fmul(e, inv_s[tid / PAGE]);
   };
-  const float* vbase = A.v_pool + (long long)kvh * PAGE * HD + d;
-  auto load_v = [&](int pg, float (&v)[PAGE]) {
-    const float* vp = vbase + (long long)bt_s[pg] * A.page_stride;
-    const int rows = min(PAGE, n - pg * PAGE);
-    if (rows == PAGE) {
+  auto issue = [&](int pg) {  // page pg of V into slot pg % PV_SLOTS (one commit group per page)
+    if (pg < npages) {
+      const float* src = vpage0 + (long long)bt_s[pg] * A.page_stride;
+      float* dst = v_s + (size_t)(pg % PV_SLOTS) * PAGE * HD;
 #pragma unroll
-      for (int r = 0; r < PAGE; r++) v[r] = vp[r * HD];
-    } else {
-#pragma unroll
-      for (int r = 0; r < PAGE; r++) v[r] = r < rows ? vp[r * HD] : 0.0f;
+      for (int sg = tid; sg < SEG; sg += HD) cp_async16(dst + sg * 4, src + sg * 4);
     }
+    cp_async_commit();
   };
   float o[REP];
 #pragma unroll
   for (int r = 0; r < REP; r++) o[r] = 0.0f;
-  auto chain = [&](int pg, const float (&v)[PAGE], const float4* pq) {
+  float ev = load_e(0);
+  __syncthreads();  // bt_s, inv_s
+  store_p(0, ev);
+  ev = load_e(1);
+  issue(0);
+  issue(1);
+  for (int pg = 0; pg < npages; pg++) {
+    // slot (pg + 2) % PV_SLOTS and p slot (pg + 1) % 3 are not read by any thread still on page pg - 1
+    issue(pg + 2);
+    store_p(pg + 1, ev);
+    ev = load_e(pg + 2);
+    cp_async_wait<2>();  // this thread's copies of page pg have landed
+    __syncthreads();     // everyone's have, and p of page pg is staged
+    const float* vs = v_s + (size_t)(pg % PV_SLOTS) * PAGE * HD + d;
+    const float4* pq = reinterpret_cast<const float4*>(&p_s[pg % 3][0][0]);
     const int rows = min(PAGE, n - pg * PAGE);
     if (rows == PAGE) {
 #pragma unroll
       for (int r = 0; r < PAGE; r++) {
         const float4 p = pq[r];
-        o[0] = fadd(o[0], fmul(p.x, v[r]));
-        if (REP > 1) o[REP > 1 ? 1 : 0] = fadd(o[REP > 1 ? 1 : 0], fmul(p.y, v[r]));
-        if (REP > 2) o[REP > 2 ? 2 : 0] = fadd(o[REP > 2 ? 2 : 0], fmul(p.z, v[r]));
-        if (REP > 3) o[REP > 3 ? 3 : 0] = fadd(o[REP > 3 ? 3 : 0], fmul(p.w, v[r]));
+        const float v = vs[r * HD];
+        o[0] = fadd(o[0], fmul(p.x, v));
+        if (REP > 1) o[REP > 1 ? 1 : 0] = fadd(o[REP > 1 ? 1 : 0], fmul(p.y, v));
+        if (REP > 2) o[REP > 2 ? 2 : 0] = fadd(o[REP > 2 ? 2 : 0], fmul(p.z, v));
+        if (REP > 3) o[REP > 3 ? 3 : 0] = fadd(o[REP > 3 ? 3 : 0], fmul(p.w, v));
       }
     } else {
-#pragma unroll
-      for (int r = 0; r < PAGE; r++) {
-        if (r < rows) {
-          const float4 p = pq[r];
-          o[0] = fadd(o[0], fmul(p.x, v[r]));
-          if (REP > 1) o[REP > 1 ? 1 : 0] = fadd(o[REP > 1 ? 1 : 0], fmul(p.y, v[r]));
-          if (REP > 2) o[REP > 2 ? 2 : 0] = fadd(o[REP > 2 ? 2 : 0], fmul(p.z, v[r]));
-          if (REP > 3) o[REP > 3 ? 3 : 0] = fadd(o[REP > 3 ? 3 : 0], fmul(p.w, v[r]));
-        }
-      }
-    }
-  };
-  float ev[PE];
-  load_e(0, ev);
-  __syncthreads();  // bt_s, inv_s
-  store_p(0, ev);
-  if (nchunk > 1) load_e(1, ev);
-  float va[PAGE], vb[PAGE];
-  load_v(0, va);
-  for (int c = 0; c < nchunk; c++) {
-    if (c + 1 < nchunk) store_p(c + 1, ev);
-    if (c + 2 < nchunk) load_e(c + 2, ev);
-    __syncthreads();  // chunk c's probabilities are staged; slot (c + 1) % 3 is no longer read
-    const float4* pc = reinterpret_cast<const float4*>(&p_s[c % 3][0][0]);
-    // pages 4c .. 4c+3 in pairs, ping-ponging between the two register buffers
-#pragma unroll
-    for (int q = 0; q < PC / PAGE; q += 2) {
-      const int pg = c * (PC / PAGE) + q;
-      if (pg < npages) {
-        if (pg + 1 < npages) load_v(pg + 1, vb);
-        chain(pg, va, pc + q * PAGE);
-      }
-      if (pg + 1 < npages) {
-        if (pg + 2 < npages) load_v(pg + 2, va);
-        chain(pg + 1, vb, pc + (q + 1) * PAGE);
+      for (int r = 0; r < rows; r++) {
+        const float4 p = pq[r];
+        const float v = vs[r * HD];
+        o[0] = fadd(o[0], fmul(p.x, v));
+        if (REP > 1) o[REP > 1 ? 1 : 0] = fadd(o[REP > 1 ? 1 : 0], fmul(p.y, v));
+        if (REP > 2) o[REP > 2 ? 2 : 0] = fadd(o[REP > 2 ? 2 : 0], fmul(p.z, v));
+        if (REP > 3) o[REP > 3 ? 3 : 0] = fadd(o[REP > 3 ? 3 : 0], fmul(p.w, v));
       }
     }
   }
+  cp_async_wait<0>();  // no copy may land after the CTA exits
   const int qd = A.nh * HD;
 #pragma unroll
   for (int r = 0; r < REP; r++) {
@@ -1279,7 +1286,7 @@ static cudaError_t launch_attn_t(const AttnArgs& A, int grid, cudaStream_t st, i
     if (attn_split(A.T, A.nkv)) {
       if (!A.rinv) return cudaErrorInvalidValue;
       k_attn_softmax<<<A.T * A.nh, SMX_THREADS, 0, st>>>(A);
-      k_attn_pv<HD, REP><<<A.T * A.nkv, HD, (size_t)A.bt_stride * 4, st>>>(A);
+      k_attn_pv<HD, REP><<<A.T * A.nkv, HD, (size_t)PV_SLOTS * PAGE * HD * 4 + (size_t)A.bt_stride * 4, st>>>(A);
     } else {
       const size_t smem = (size_t)A.stages * PAGE * HD * 4 + (size_t)A.bt_stride * 4;
       k_attn_out<HD><<<A.T * A.nh, HD, smem, st>>>(A);
@@ -1307,15 +1314,23 @@ cudaError_t launch_attn_out_only(const AttnArgs& A, cudaStream_t st) { return la
 
 // Opt in to the ring's dynamic shared memory on the current device (call before any launch or
 // graph capture).
+template <int HD, int REP>
+static cudaError_t prepare_attn_t() {
+  // the rings plus up to ATT_MAX_BT page ids
+  cudaError_t e = cudaFuncSetAttribute((const void*)k_attn_out<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       ATT_MAX_STAGES * PAGE * HD * 4 + ATT_MAX_BT * 4);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute((const void*)k_attn_pv<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              PV_SLOTS * PAGE * HD * 4 + ATT_MAX_BT * 4);
+}
+
 cudaError_t prepare_attn(int hd, int rep) {
-  if (rep != 1 && rep != 2 && rep != 4) return cudaErrorInvalidValue;
-  // the ring plus up to ATT_MAX_BT page ids
-  if (hd == 128)
-    return cudaFuncSetAttribute((const void*)k_attn_out<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                ATT_MAX_STAGES * PAGE * 128 * 4 + ATT_MAX_BT * 4);
-  if (hd == 64)
-    return cudaFuncSetAttribute((const void*)k_attn_out<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                ATT_MAX_STAGES * PAGE * 64 * 4 + ATT_MAX_BT * 4);
+  if (hd == 128 && rep == 4) return prepare_attn_t<128, 4>();
+  if (hd == 64 && rep == 4) return prepare_attn_t<64, 4>();
+  if (hd == 128 && rep == 2) return prepare_attn_t<128, 2>();
+  if (hd == 64 && rep == 2) return prepare_attn_t<64, 2>();
+  if (hd == 128 && rep == 1) return prepare_attn_t<128, 1>();
+  if (hd == 64 && rep == 1) return prepare_attn_t<64, 1>();
   return cudaErrorInvalidValue;
 }
 
