@@ -257,12 +257,13 @@ def run_ours(args):
     hbm, peak_kind = peaks()
     att_gbs = kv_bytes / ((ms_s + ms_o) / 1e3) / 1e9
     traffic = None
-    tf = os.path.join(ROOT, "profiles", "attention_traffic.json")
+    tf = os.path.join(ROOT, "profiles", "attention_traffic.txt")
     if os.path.exists(tf):
         with open(tf) as f:
-            tr = json.load(f)
-        # captured on a smaller case; bytes scale with the positions read
-        traffic = tr["bytes_per_position"] * sum(ctx_now)
+            bpp = [float(ln.split(":", 1)[1]) for ln in f if ln.startswith("bytes_per_position:")]
+        # captured on a smaller case; DRAM bytes scale with the positions read
+        if bpp:
+            traffic = int(bpp[0] * sum(ctx_now))
     res = {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(max_s / args.steps * 1e3, 3), "higher_is_better": True,
