@@ -484,13 +484,14 @@ __global__ void __launch_bounds__(ROWS * 8) k_ffn_down(Dims D, DecodeBufs B, Lay
 //   positions. QK-norm (sequential sum, model.rs:753-763) + RoPE of the item's q heads, and for
 //   the chunk holding the new position the same for k, plus the k/v append to its page slot.
 //   s[t][h][j] = dot(q_h, k_j) * (1/sqrt(hd)) in the ops::dot order; the chunk maximum per head.
-// k_attn_out: one CTA per (token, kv head), REP*HD threads. Softmax (ops.rs:112-128): global max,
-//   e_j = exp(s_j - max) (parallel), sum = sequential f32 sum over j, inv = 1/sum; then every
-//   (head, dim) thread accumulates o += (e_j * inv) * v_j[dim] sequentially over j (model.rs:
-//   227-232). V pages stream through a shared-memory ring filled by TMA bulk copies
-//   (cp.async.bulk, one 16 x hd block per page) completing on mbarriers. The result is quantized
+// k_attn_softmax: softmax (ops.rs:112-128) per (token, q head): global max, e_j = exp(s_j - max)
+//   (parallel), sum = sequential f32 sum over j, inv = 1/sum.
+// k_attn_pv: every (head, dim) chain accumulates o += (e_j * inv) * v_j[dim] sequentially over j
+//   (model.rs:227-232), V pages streamed into shared memory by cp.async; the result is quantized
 //   per 32-block for the output projection (quant.rs:112-123).
 // ------------------------------------------------------------------------------------------
+
+constexpr int ATT_MAX_BT = 4096;  // block-table entries staged in shared memory (contexts <= 65536)
 
 // per-head RMSNorm with a sequential sum (model.rs:753-763) + rotate-half RoPE (ops.rs:157-166)
 // of one head vector by one warp. buf: this warp's HD-float shared scratch; dst may alias buf.
@@ -611,8 +612,6 @@ __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
       } else if (warp == REP + 1) {
         for (int j = lane; j < HD; j += 32) A.v_pool[off + j] = qkv[qd + kvd + kvh * HD + j];
       }
-      // the V/K rows are read by bulk copies in k_attn_out: order these generic writes first
-      asm volatile("fence.proxy.async.global;" ::: "memory");
     }
     __syncthreads();
     // ops::dot lane mapping: accumulator m's SIMD lane l sums elements 32i + 8m + l (FMA, i
@@ -692,227 +691,6 @@ __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
         A.cmax[((size_t)t * A.nh + kvh * REP + lane) * (size_t)A.max_chunks * 8 + c * 8 + warp] = mv;
       }
     }
-  }
-}
-
-// ---- mbarrier / bulk-copy helpers (sm_90+ PTX) ----
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-// Bounded wait for phase `parity` of an mbarrier: gives up after ~1 s (globaltimer, read only once
-// the phase is late) and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  if (mbar_try(bar, parity)) return true;
-  uint64_t t0, t1;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-  while (true) {
-    for (int k = 0; k < 64; k++)
-      if (mbar_try(bar, parity)) return true;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
-    if (t1 - t0 > 1000000000ull) return false;
-  }
-}
-
-constexpr int ATT_MAX_STAGES = 24;  // V pages in flight per CTA (runtime count A.stages <= this, even)
-constexpr int ATT_ECH = 512;        // softmax positions per sum chunk
-constexpr int ATT_MAX_BT = 4096;    // block-table entries held in shared memory (contexts <= 65536)
-
-// One CTA per (token, q head), HD threads (thread = output dim). The kv head's V pages start
-// streaming into the ring at entry; meanwhile the softmax sum runs: warps 1.. compute
-// e = exp(s - max) for the next chunk (into shared memory and back into S) while warp 0 adds the
-// current chunk in position order. Then o[di] += (e_j * inv) * v_j[di] over j in order.
-template <int HD>
-__global__ void __launch_bounds__(HD) k_attn_out(AttnArgs A) {
-  constexpr uint32_t PAGE_BYTES = PAGE * HD * 4;
-  constexpr int NW = HD / 32;
-  // dynamic shared memory: A.stages pages of [16][HD] f32, then the sequence's page ids
-  extern __shared__ __align__(128) unsigned char ring[];
-  __shared__ __align__(8) uint64_t bar[ATT_MAX_STAGES];
-  __shared__ float ebuf[2][ATT_ECH];
-  __shared__ float inv_s, m_s;
-  __shared__ int fail_s;
-  const int S = A.stages;
-  int* bt_s = reinterpret_cast<int*>(ring + (size_t)S * PAGE_BYTES);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, di = tid;
-  const int t = blockIdx.x / A.nh, h = blockIdx.x - t * A.nh;
-  const int rep = A.nh / A.nkv, kvh = h / rep;
-  const int pos = A.pos[t];
-  if (pos < 0 || pos >= A.max_pos) return;  // flagged by k_attn_scores
-  const int n = pos + 1, nch = (n + ATT_CHUNK - 1) / ATT_CHUNK, npages = (n + PAGE - 1) / PAGE;
-  const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
-  float* erow = A.S + ((size_t)t * A.nh + h) * A.s_stride;
-  const float* vbase = A.v_pool + (long long)kvh * PAGE * HD;
-  for (int p = tid; p < npages; p += HD) bt_s[p] = bt[p];  // page ids: no global load per refill
-  if (tid == 0) {
-    fail_s = 0;
-    for (int s = 0; s < S; s++) mbar_init(&bar[s], 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-  if (tid == 0) {
-    for (int p = 0; p < S && p < npages; p++) {
-      mbar_expect_tx(&bar[p], PAGE_BYTES);
-      bulk_g2s(ring + (size_t)p * PAGE_BYTES, vbase + (long long)bt_s[p] * A.page_stride, PAGE_BYTES, &bar[p]);
-    }
-  }
-  if (warp == 0) {  // max over the per-warp chunk maxima
-    const float* cm = A.cmax + ((size_t)t * A.nh + h) * (size_t)A.max_chunks * 8;
-    float m = -INFINITY;
-    for (int c = lane; c < nch * 8; c += 32) m = fmaxf(m, cm[c]);
-    m = warp_max(m);
-    if (lane == 0) m_s = m;
-  }
-  __syncthreads();
-  const float mrow = m_s;
-  // ---- softmax denominator: sequential f32 sum over positions (ops.rs:118-122) ----
-  const int nchunks = (n + ATT_ECH - 1) / ATT_ECH;
-  for (int j = tid; j < min(ATT_ECH, n); j += HD) {
-    const float e = exp_cr(__fsub_rn(erow[j], mrow));
-    ebuf[0][j] = e;
-    erow[j] = e;
-  }
-  __syncthreads();
-  float sum = 0.0f;
-  for (int c = 0; c < nchunks; c++) {
-    const int j0 = c * ATT_ECH, cnt = min(ATT_ECH, n - j0);
-    if (warp == 0 || NW == 1) {
-      const float* eb = ebuf[c & 1];
-#pragma unroll 8
-      for (int j = 0; j < cnt; j++) sum = fadd(sum, eb[j]);
-    }
-    if ((warp > 0 || NW == 1) && c + 1 < nchunks) {
-      const int j1 = j0 + ATT_ECH, cn1 = min(ATT_ECH, n - j1);
-      const int nt = NW == 1 ? HD : HD - 32, t1 = NW == 1 ? tid : tid - 32;
-      float* eb = ebuf[(c + 1) & 1];
-      for (int j = t1; j < cn1; j += nt) {
-        const float e = exp_cr(__fsub_rn(erow[j1 + j], mrow));
-        eb[j] = e;
-        erow[j1 + j] = e;
-      }
-    }
-    __syncthreads();
-  }
-  if (tid == 0) inv_s = __fdiv_rn(1.0f, sum);
-  __syncthreads();
-  const float inv = inv_s;
-  // ---- o[di] = sum_j (e_j * inv) * v_j[di], sequential in j (model.rs:227-232) ----
-  // groups of 32 positions (two pages); lane i holds e of position 32g + i, EPF groups ahead.
-  constexpr int EPF = 4;
-  const int ngroups = (n + 31) / 32;
-  float epf[EPF];
-#pragma unroll
-  for (int k = 0; k < EPF; k++) {
-    const int j = 32 * k + lane;
-    epf[k] = j < n ? erow[j] : 0.0f;
-  }
-  float acc = 0.0f;
-  int cst = 0, cpar = 0;          // stage / parity of the next page to consume
-  int ist = 0;                     // stage of the next refill (stages are released in order)
-  int next_issue = S;              // next page to issue
-  int g = 0;
-  for (; g < ngroups; g++) {
-    const float e_cur = epf[0];
-#pragma unroll
-    for (int k = 0; k < EPF - 1; k++) epf[k] = epf[k + 1];
-    {
-      const int j = 32 * (g + EPF) + lane;
-      epf[EPF - 1] = j < n ? erow[j] : 0.0f;
-    }
-    const float pr = fmul(e_cur, inv);
-    const bool two = 2 * g + 1 < npages;
-    const int s0 = cst, p0par = cpar;
-    int s1 = cst + 1, p1par = cpar;
-    if (s1 == S) {
-      s1 = 0;
-      p1par ^= 1;
-    }
-    bool ok = mbar_wait(&bar[s0], (uint32_t)p0par);
-    if (two) ok = mbar_wait(&bar[s1], (uint32_t)p1par) && ok;
-    if (!ok && lane == 0) atomicExch(&fail_s, 1);
-    const float* v0 = reinterpret_cast<const float*>(ring + (size_t)s0 * PAGE_BYTES) + di;
-    const float* v1 = reinterpret_cast<const float*>(ring + (size_t)s1 * PAGE_BYTES) + di;
-    const int rows = min(32, n - 32 * g);
-    if (rows == 32) {
-      float pv[32], vv[32];
-#pragma unroll
-      for (int r = 0; r < 32; r++) {
-        pv[r] = __shfl_sync(0xffffffffu, pr, r);
-        vv[r] = r < 16 ? v0[r * HD] : v1[(r - 16) * HD];
-      }
-#pragma unroll
-      for (int r = 0; r < 32; r++) acc = fadd(acc, fmul(pv[r], vv[r]));
-    } else {
-      for (int r = 0; r < rows; r++) {
-        const float pj = __shfl_sync(0xffffffffu, pr, r);
-        acc = fadd(acc, fmul(pj, r < 16 ? v0[r * HD] : v1[(r - 16) * HD]));
-      }
-    }
-    __syncthreads();
-    if (fail_s) break;
-    // advance the consume cursor by the pages of this group
-    const int used = two ? 2 : 1;
-    for (int u = 0; u < used; u++)
-      if (++cst == S) {
-        cst = 0;
-        cpar ^= 1;
-      }
-    if (tid == 0) {  // refill the stages just released
-      for (int u = 0; u < used && next_issue < npages; u++, next_issue++) {
-        mbar_expect_tx(&bar[ist], PAGE_BYTES);
-        bulk_g2s(ring + (size_t)ist * PAGE_BYTES, vbase + (long long)bt_s[next_issue] * A.page_stride, PAGE_BYTES,
-                 &bar[ist]);
-        if (++ist == S) ist = 0;
-      }
-    }
-  }
-  if (fail_s) {
-    // a bulk copy did not complete in time: report, then wait (bounded) for every page issued
-    // but not consumed so no copy lands in shared memory after this CTA exits
-    if (tid == 0) {
-      if (A.err) atomicExch(A.err, HG_ERR_TIMEOUT);
-      int st = cst, par = cpar;
-      for (int q = 2 * g; q < next_issue && q < npages; q++) {
-        mbar_wait(&bar[st], (uint32_t)par);
-        if (++st == S) {
-          st = 0;
-          par ^= 1;
-        }
-      }
-    }
-    __syncthreads();
-    return;
-  }
-  const int qd = A.nh * HD;
-  if (A.out) A.out[(size_t)t * qd + h * HD + di] = acc;
-  if (A.qo) {  // each warp holds one 32-block of the head
-    float dq;
-    int8_t q = quant_lane(acc, &dq);
-    const int nbq = qd >> 5;
-    A.qo[(size_t)t * qd + q8_pos(h * HD + di, nbq)] = q;
-    if (lane == 0) A.so[(size_t)t * q8_ss(nbq) + ((h * HD + di) >> 5)] = dq;
   }
 }
 
@@ -1028,7 +806,14 @@ __global__ void __launch_bounds__(SMX_THREADS) k_attn_softmax(AttnArgs A) {
   if (tid == 0) A.rinv[(size_t)t * A.nh + h] = __fdiv_rn(1.0f, sum);
 }
 
-constexpr int PV_SLOTS = 4;  // V pages in shared memory per k_attn_pv CTA (two in flight)
+// k_attn_pv shapes: NT output dims (threads, whole warps) per CTA, so HD / NT CTAs per (token, kv
+// head); SLOTS V pages in shared memory per CTA, SLOTS - 2 of them in flight (a CTA issues page
+// pg + SLOTS - 2 while warps may still read page pg - 1). Large batches: many CTAs share each SM,
+// two pages in flight each. Small batches (down to one sequence) use k_attn_pv_hw (one warp per q
+// head, pages staged through registers) because each CTA must stream its whole context alone.
+constexpr int PV_NT_LARGE = 64, PV_SLOTS_LARGE = 4;
+constexpr int PV_DEPTH_SMALL = 16;  // pages in flight per k_attn_pv_hw CTA (held in registers)
+constexpr int PV_SMALL_MAX_PAIRS = 64;  // (token, kv head) pairs up to which the small shape is used
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
@@ -1038,80 +823,88 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-template <int HD, int REP>
-__global__ void __launch_bounds__(HD) k_attn_pv(AttnArgs A) {
-  constexpr int SEG = PAGE * HD / 4;  // 16-byte segments per V page
+// CTA = (token, kv head, slice of NT output dims); thread = output dim. Splitting a head's dims over
+// HD / NT CTAs lets a long sequence's value sums run as independent CTAs (no page barrier shared
+// by all of its dims).
+template <int HD, int REP, int NT, int SLOTS>
+__global__ void __launch_bounds__(NT) k_attn_pv(AttnArgs A) {
+  static_assert(NT % 32 == 0 && HD % NT == 0, "whole warps (the output quantization is per warp)");
+  static_assert(REP == 1 || REP == 2 || REP == 4, "GQA group of 1, 2 or 4 q heads");
+  constexpr int AHEAD = SLOTS - 2;
+  constexpr int DS = HD / NT;                // CTAs per (token, kv head)
+  constexpr int RSEG = NT / 4;               // 16-byte segments per V row slice
+  constexpr int SEG = PAGE * RSEG;           // per page
+  constexpr int ESEG = REP * PAGE / 4;       // 16-byte segments of e per page (one row piece per head)
   extern __shared__ __align__(16) unsigned char dsm[];
-  float* v_s = reinterpret_cast<float*>(dsm);                            // [PV_SLOTS][PAGE][HD]
-  int* bt_s = reinterpret_cast<int*>(dsm + (size_t)PV_SLOTS * PAGE * HD * 4);  // page ids
-  __shared__ __align__(16) float p_s[3][PAGE][4];  // p of each row of a page for the group's heads
+  float* v_s = reinterpret_cast<float*>(dsm);                                   // [SLOTS][PAGE][NT]
+  float* e_s = v_s + (size_t)SLOTS * PAGE * NT;                                 // [SLOTS][REP][PAGE]
+  int* bt_s = reinterpret_cast<int*>(e_s + (size_t)SLOTS * REP * PAGE);        // page ids
+  __shared__ __align__(16) float p_s[PAGE][4];  // p of each row of the current page for the group's heads
   __shared__ float inv_s[REP];
-  const int tid = threadIdx.x, lane = tid & 31, d = tid;
-  const int t = blockIdx.x / A.nkv, kvh = blockIdx.x - t * A.nkv;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int slice = blockIdx.x % DS, tk = blockIdx.x / DS;
+  const int t = tk / A.nkv, kvh = tk - t * A.nkv, d = slice * NT + tid;
   const int pos = A.pos[t];
   if (pos < 0 || pos >= A.max_pos) return;  // flagged by k_attn_scores
   const int n = pos + 1, npages = (n + PAGE - 1) / PAGE;
   const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
-  for (int p = tid; p < npages; p += HD) bt_s[p] = bt[p];
+  for (int p = tid; p < npages; p += NT) bt_s[p] = bt[p];
   const int h0 = kvh * REP;
   if (tid < REP) inv_s[tid] = A.rinv[(size_t)t * A.nh + h0 + tid];
   const float* erow0 = A.S + ((size_t)t * A.nh + h0) * A.s_stride;
-  const float* vpage0 = A.v_pool + (long long)kvh * PAGE * HD;
-  // e of (head tid / PAGE, row tid % PAGE) of page pg, for the first PAGE * REP threads
-  auto load_e = [&](int pg) -> float {
-    const int jj = pg * PAGE + (tid % PAGE);
-    return (tid < PAGE * REP && jj < n) ? erow0[(size_t)(tid / PAGE) * A.s_stride + jj] : 0.0f;
-  };
-  auto store_p = [&](int pg, float e) {
-    if (tid < PAGE * REP) p_s[pg % 3][tid % PAGE][tid / PAGE] = fmul(e, inv_s[tid / PAGE]);
-  };
-  auto issue = [&](int pg) {  // page pg of V into slot pg % PV_SLOTS (one commit group per page)
+  const float* vpage0 = A.v_pool + (long long)kvh * PAGE * HD + slice * NT;
+  // page pg's V rows of this slice and its e (exp weights) of every head of the group into slot
+  // pg % SLOTS: one commit group per page. e rows run to s_stride >= npages * PAGE.
+  auto issue = [&](int pg) {
     if (pg < npages) {
       const float* src = vpage0 + (long long)bt_s[pg] * A.page_stride;
-      float* dst = v_s + (size_t)(pg % PV_SLOTS) * PAGE * HD;
+      float* dst = v_s + (size_t)(pg % SLOTS) * PAGE * NT;
 #pragma unroll
-      for (int sg = tid; sg < SEG; sg += HD) cp_async16(dst + sg * 4, src + sg * 4);
+      for (int sg = tid; sg < SEG; sg += NT) {
+        const int row = sg / RSEG, col = sg - row * RSEG;
+        cp_async16(dst + row * NT + col * 4, src + row * HD + col * 4);
+      }
+      if (tid < ESEG) {
+        const int r = tid / (PAGE / 4), q = tid - r * (PAGE / 4);
+        cp_async16(e_s + ((size_t)(pg % SLOTS) * REP + r) * PAGE + q * 4, erow0 + (size_t)r * A.s_stride + pg * PAGE + q * 4);
+      }
     }
     cp_async_commit();
   };
   float o[REP];
 #pragma unroll
   for (int r = 0; r < REP; r++) o[r] = 0.0f;
-  float ev = load_e(0);
   __syncthreads();  // bt_s, inv_s
-  store_p(0, ev);
-  ev = load_e(1);
-  issue(0);
-  issue(1);
+#pragma unroll
+  for (int k = 0; k < AHEAD; k++) issue(k);
   for (int pg = 0; pg < npages; pg++) {
-    // slot (pg + 2) % PV_SLOTS and p slot (pg + 1) % 3 are not read by any thread still on page pg - 1
-    issue(pg + 2);
-    store_p(pg + 1, ev);
-    ev = load_e(pg + 2);
-    cp_async_wait<2>();  // this thread's copies of page pg have landed
-    __syncthreads();     // everyone's have, and p of page pg is staged
-    const float* vs = v_s + (size_t)(pg % PV_SLOTS) * PAGE * HD + d;
-    const float4* pq = reinterpret_cast<const float4*>(&p_s[pg % 3][0][0]);
+    // slot (pg + AHEAD) % SLOTS is not read by any thread (AHEAD <= SLOTS - 2; every thread is past
+    // page pg - 2, and pg - 1 uses another slot)
+    issue(pg + AHEAD);
+    cp_async_wait<AHEAD>();  // this thread's copies of page pg have landed
+    __syncthreads();         // everyone's have, and everyone is done with page pg - 1
+    const int slot = pg % SLOTS;
+    for (int idx = tid; idx < PAGE * REP; idx += NT) {
+      const int r = idx / PAGE, j = idx - r * PAGE;
+      p_s[j][r] = fmul(e_s[((size_t)slot * REP + r) * PAGE + j], inv_s[r]);  // softmax p (ops.rs:124-126)
+    }
+    __syncthreads();
+    const float* vs = v_s + (size_t)slot * PAGE * NT + tid;
+    const float4* pq = reinterpret_cast<const float4*>(&p_s[0][0]);
     const int rows = min(PAGE, n - pg * PAGE);
+    auto step = [&](int r) {
+      const float4 p = pq[r];
+      const float v = vs[r * NT];
+      o[0] = fadd(o[0], fmul(p.x, v));
+      if (REP > 1) o[REP > 1 ? 1 : 0] = fadd(o[REP > 1 ? 1 : 0], fmul(p.y, v));
+      if (REP > 2) o[REP > 2 ? 2 : 0] = fadd(o[REP > 2 ? 2 : 0], fmul(p.z, v));
+      if (REP > 3) o[REP > 3 ? 3 : 0] = fadd(o[REP > 3 ? 3 : 0], fmul(p.w, v));
+    };
     if (rows == PAGE) {
 #pragma unroll
-      for (int r = 0; r < PAGE; r++) {
-        const float4 p = pq[r];
-        const float v = vs[r * HD];
-        o[0] = fadd(o[0], fmul(p.x, v));
-        if (REP > 1) o[REP > 1 ? 1 : 0] = fadd(o[REP > 1 ? 1 : 0], fmul(p.y, v));
-        if (REP > 2) o[REP > 2 ? 2 : 0] = fadd(o[REP > 2 ? 2 : 0], fmul(p.z, v));
-        if (REP > 3) o[REP > 3 ? 3 : 0] = fadd(o[REP > 3 ? 3 : 0], fmul(p.w, v));
-      }
+      for (int r = 0; r < PAGE; r++) step(r);
     } else {
-      for (int r = 0; r < rows; r++) {
-        const float4 p = pq[r];
-        const float v = vs[r * HD];
-        o[0] = fadd(o[0], fmul(p.x, v));
-        if (REP > 1) o[REP > 1 ? 1 : 0] = fadd(o[REP > 1 ? 1 : 0], fmul(p.y, v));
-        if (REP > 2) o[REP > 2 ? 2 : 0] = fadd(o[REP > 2 ? 2 : 0], fmul(p.z, v));
-        if (REP > 3) o[REP > 3 ? 3 : 0] = fadd(o[REP > 3 ? 3 : 0], fmul(p.w, v));
-      }
+      for (int r = 0; r < rows; r++) step(r);
     }
   }
   cp_async_wait<0>();  // no copy may land after the CTA exits
@@ -1127,6 +920,86 @@ __global__ void __launch_bounds__(HD) k_attn_pv(AttnArgs A) {
       A.qo[(size_t)t * qd + q8_pos(hd, nbq)] = q;
       if (lane == 0) A.so[(size_t)t * q8_ss(nbq) + (hd >> 5)] = dq;
     }
+  }
+}
+
+// Small batches: CTA = (token, kv head, 32-dim slice), one warp per q head of the group (lane =
+// output dim), all warps reading the same staged pages. A warp does one chain per lane, about four
+// instructions per position. The pages come in through registers: each thread holds its 16-byte
+// piece of the next D pages (plain 128-bit loads keep far more bytes in flight per CTA than
+// cp.async here), stores one page per step into a shared double buffer, and the warps chain over it.
+template <int HD, int REP, int D>
+__global__ void __launch_bounds__(32 * REP) k_attn_pv_hw(AttnArgs A) {
+  static_assert(HD % 32 == 0 && REP == 4, "32-dim slices, GQA group of 4 (one 16-byte V piece per thread)");
+  constexpr int NT = 32 * REP, DS = HD / 32;
+  constexpr int ESEG = REP * PAGE / 4;  // 16-byte pieces of e per page
+  extern __shared__ __align__(16) unsigned char dsm[];
+  int* bt_s = reinterpret_cast<int*>(dsm);  // page ids
+  __shared__ __align__(16) float v_s[2][PAGE][32];
+  __shared__ __align__(16) float e_s[2][REP][PAGE];
+  __shared__ __align__(16) float p_s[REP][PAGE];
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int slice = blockIdx.x % DS, tk = blockIdx.x / DS;
+  const int t = tk / A.nkv, kvh = tk - t * A.nkv, d = slice * 32 + lane, h = kvh * REP + w;
+  const int pos = A.pos[t];
+  if (pos < 0 || pos >= A.max_pos) return;  // flagged by k_attn_scores
+  const int n = pos + 1, npages = (n + PAGE - 1) / PAGE;
+  const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
+  for (int p = tid; p < npages; p += NT) bt_s[p] = bt[p];
+  const float inv = A.rinv[(size_t)t * A.nh + h];
+  // this thread's pieces: V row tid / 8, dims 4 * (tid % 8) .. + 3 of the slice; e piece tid (< ESEG)
+  const int vrow = tid >> 3, vcol = (tid & 7) * 4;
+  const float* vsrc = A.v_pool + (long long)kvh * PAGE * HD + slice * 32 + vrow * HD + vcol;
+  const int er = tid / (PAGE / 4), eq = tid - er * (PAGE / 4);
+  const float* esrc = A.S + ((size_t)t * A.nh + kvh * REP + (tid < ESEG ? er : 0)) * A.s_stride + eq * 4;
+  auto load = [&](int pg, float4& v, float4& e) {  // e rows run to s_stride >= npages * PAGE
+    if (pg < npages) {
+      v = __ldg(reinterpret_cast<const float4*>(vsrc + (long long)bt_s[pg] * A.page_stride));
+      if (tid < ESEG) e = *reinterpret_cast<const float4*>(esrc + pg * PAGE);
+    }
+  };
+  float4 rv[D], re[D];
+  float o = 0.0f;
+  __syncthreads();  // bt_s
+#pragma unroll
+  for (int k = 0; k < D; k++) load(k, rv[k], re[k]);
+  for (int pg0 = 0; pg0 < npages; pg0 += D) {
+#pragma unroll
+    for (int k = 0; k < D; k++) {
+      const int pg = pg0 + k;
+      if (pg >= npages) break;  // uniform over the CTA
+      // buffer pg & 1 was last read for page pg - 2, before the previous step's barrier
+      *reinterpret_cast<float4*>(&v_s[pg & 1][vrow][vcol]) = rv[k];
+      if (tid < ESEG) *reinterpret_cast<float4*>(&e_s[pg & 1][er][eq * 4]) = re[k];
+      load(pg + D, rv[k], re[k]);
+      __syncthreads();
+      if (lane < PAGE) p_s[w][lane] = fmul(e_s[pg & 1][w][lane], inv);  // ops.rs:124-126
+      __syncwarp();
+      const float* vs = &v_s[pg & 1][0][lane];
+      const float4* pq = reinterpret_cast<const float4*>(&p_s[w][0]);
+      const int rows = min(PAGE, n - pg * PAGE);
+      if (rows == PAGE) {
+#pragma unroll
+        for (int q = 0; q < PAGE / 4; q++) {
+          const float4 p = pq[q];
+          o = fadd(o, fmul(p.x, vs[(4 * q + 0) * 32]));
+          o = fadd(o, fmul(p.y, vs[(4 * q + 1) * 32]));
+          o = fadd(o, fmul(p.z, vs[(4 * q + 2) * 32]));
+          o = fadd(o, fmul(p.w, vs[(4 * q + 3) * 32]));
+        }
+      } else {
+        for (int r = 0; r < rows; r++) o = fadd(o, fmul(p_s[w][r], vs[r * 32]));
+      }
+    }
+  }
+  const int qd = A.nh * HD, hd = h * HD + d;
+  if (A.out) A.out[(size_t)t * qd + hd] = o;
+  if (A.qo) {  // the warp holds one 32-block of the head
+    float dq;
+    int8_t q = quant_lane(o, &dq);
+    const int nbq = qd >> 5;
+    A.qo[(size_t)t * qd + q8_pos(hd, nbq)] = q;
+    if (lane == 0) A.so[(size_t)t * q8_ss(nbq) + (hd >> 5)] = dq;
   }
 }
 
@@ -1273,32 +1146,35 @@ int attn_grid(int T, int nkv, int max_chunks) {
   return (int)(g > 0 ? g : 1);
 }
 
-// Batches whose (token, kv head) pairs fill at least this many CTAs take the split output path
-// (k_attn_softmax + k_attn_pv); smaller ones keep one CTA per (token, q head) with a V ring.
-constexpr int ATT_SPLIT_MIN_CTAS = 64;
+template <int HD, int NT>
+constexpr int pv_nt() { return NT < HD ? NT : HD; }
 
-bool attn_split(int T, int nkv) { return T * nkv >= ATT_SPLIT_MIN_CTAS; }
+// dynamic shared memory of k_attn_pv: the V and e rings, then the page ids
+constexpr size_t pv_smem(int nt, int slots, int rep, int bt_stride) {
+  return (size_t)slots * PAGE * nt * 4 + (size_t)slots * rep * PAGE * 4 + (size_t)bt_stride * 4;
+}
+
+template <int HD, int REP, int NT, int SLOTS>
+static void launch_pv(const AttnArgs& A, cudaStream_t st) {
+  k_attn_pv<HD, REP, NT, SLOTS><<<A.T * A.nkv * (HD / NT), NT, pv_smem(NT, SLOTS, REP, A.bt_stride), st>>>(A);
+}
 
 template <int HD, int REP>
 static cudaError_t launch_attn_t(const AttnArgs& A, int grid, cudaStream_t st, int which) {
   if (which & 1) k_attn_scores<HD, REP><<<grid, 256, 0, st>>>(A);
   if (which & 2) {
-    if (attn_split(A.T, A.nkv)) {
-      if (!A.rinv) return cudaErrorInvalidValue;
-      k_attn_softmax<<<A.T * A.nh, SMX_THREADS, 0, st>>>(A);
-      k_attn_pv<HD, REP><<<A.T * A.nkv, HD, (size_t)PV_SLOTS * PAGE * HD * 4 + (size_t)A.bt_stride * 4, st>>>(A);
-    } else {
-      const size_t smem = (size_t)A.stages * PAGE * HD * 4 + (size_t)A.bt_stride * 4;
-      k_attn_out<HD><<<A.T * A.nh, HD, smem, st>>>(A);
-    }
+    k_attn_softmax<<<A.T * A.nh, SMX_THREADS, 0, st>>>(A);
+    if (REP == 4 && A.T * A.nkv <= PV_SMALL_MAX_PAIRS)
+      k_attn_pv_hw<HD, 4, PV_DEPTH_SMALL><<<A.T * A.nkv * (HD / 32), 128, (size_t)A.bt_stride * 4, st>>>(A);
+    else
+      launch_pv<HD, REP, pv_nt<HD, PV_NT_LARGE>(), PV_SLOTS_LARGE>(A, st);
   }
   return cudaGetLastError();
 }
 
 static cudaError_t launch_attn_which(const AttnArgs& A, int grid, cudaStream_t st, int which) {
   int rep = A.nh / A.nkv;
-  if (A.stages < 2 || A.stages > ATT_MAX_STAGES || (A.stages & 1) || A.bt_stride > ATT_MAX_BT)
-    return cudaErrorInvalidValue;
+  if (A.bt_stride > ATT_MAX_BT || !A.rinv) return cudaErrorInvalidValue;
   if (A.hd == 128 && rep == 4) return launch_attn_t<128, 4>(A, grid, st, which);
   if (A.hd == 64 && rep == 4) return launch_attn_t<64, 4>(A, grid, st, which);
   if (A.hd == 128 && rep == 2) return launch_attn_t<128, 2>(A, grid, st, which);
@@ -1316,12 +1192,10 @@ cudaError_t launch_attn_out_only(const AttnArgs& A, cudaStream_t st) { return la
 // graph capture).
 template <int HD, int REP>
 static cudaError_t prepare_attn_t() {
-  // the rings plus up to ATT_MAX_BT page ids
-  cudaError_t e = cudaFuncSetAttribute((const void*)k_attn_out<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       ATT_MAX_STAGES * PAGE * HD * 4 + ATT_MAX_BT * 4);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute((const void*)k_attn_pv<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              PV_SLOTS * PAGE * HD * 4 + ATT_MAX_BT * 4);
+  // the V rings plus up to ATT_MAX_BT page ids
+  constexpr int NL = pv_nt<HD, PV_NT_LARGE>();
+  return cudaFuncSetAttribute((const void*)k_attn_pv<HD, REP, NL, PV_SLOTS_LARGE>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pv_smem(NL, PV_SLOTS_LARGE, REP, ATT_MAX_BT));
 }
 
 cudaError_t prepare_attn(int hd, int rep) {

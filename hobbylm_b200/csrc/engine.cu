@@ -455,7 +455,6 @@ AttnArgs make_attn_args(hg_engine* e, const DecodeBufs& B, int l) {
   A.s_stride = B.s_stride;
   A.cmax = B.cmax;
   A.rinv = B.rinv;
-  A.stages = B.T < 8 ? 24 : 8;  // few CTAs: each streams its V alone, so keep more pages in flight
   A.out = nullptr;
   A.qo = B.qo;
   A.so = B.so;
@@ -1316,7 +1315,6 @@ int hg_op_kv_attn(const hg_kv_attn_args* a, void* scratch, void* stream) {
     A.cmax = reinterpret_cast<float*>(base + s_bytes);
     A.rinv = reinterpret_cast<float*>(base + s_bytes + align256((size_t)a->n_seqs * a->n_heads * max_chunks * 8 * 4));
     A.err = nullptr;
-    A.stages = a->n_seqs < 8 ? 24 : 8;
     A.out = a->out;
     A.qo = nullptr;
     A.so = nullptr;

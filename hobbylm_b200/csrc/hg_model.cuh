@@ -102,7 +102,6 @@ struct AttnArgs {
   long long s_stride;  // >= max_pos, multiple of 16
   float* rinv;     // [T][nh] 1 / softmax denominator (split path)
   float* cmax;     // [T][nh][max_chunks][8] per-warp chunk maxima of the scores
-  int stages;      // V pages in flight per k_attn_out CTA (2..24, even)
   float* out;      // [T][nh*hd] or null
   int8_t* qo;      // [T][nh*hd] or null
   float* so;       // [T][ss(nh*hd/32)]
