@@ -44,8 +44,17 @@ __device__ inline float seq_sumsq_block(const float* xs, int n, float* red) {
   __syncthreads();
   if (threadIdx.x == 0) {
     float ss = 0.0f;
-#pragma unroll 8
-    for (int i = 0; i < n; i++) ss = fadd(ss, fmul(xs[i], xs[i]));
+    const float4* x4 = reinterpret_cast<const float4*>(xs);  // n % 4 == 0, xs 16-byte aligned
+    const int n4 = n >> 2;
+    float4 a = n4 > 0 ? x4[0] : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < n4; i++) {
+      const float4 b = i + 1 < n4 ? x4[i + 1] : a;  // next group's load issued before this group's adds
+      ss = fadd(ss, fmul(a.x, a.x));
+      ss = fadd(ss, fmul(a.y, a.y));
+      ss = fadd(ss, fmul(a.z, a.z));
+      ss = fadd(ss, fmul(a.w, a.w));
+      a = b;
+    }
     red[0] = ss;
   }
   __syncthreads();
@@ -57,7 +66,9 @@ __device__ inline float seq_sumsq_block(const float* xs, int n, float* red) {
 // mode 0: x = token embedding; 1: x += y[t][0] (dense FFN); 2: x += MoE combine (model.rs:300-323,
 // rank order then the shared expert); 3: x unchanged.
 // ------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) k_pre_norm(Dims D, DecodeBufs B, int mode, const float* __restrict__ embd,
+constexpr int PRE_NORM_THREADS = 1024;  // one element per thread up to d = 1024
+
+__global__ void __launch_bounds__(PRE_NORM_THREADS) k_pre_norm(Dims D, DecodeBufs B, int mode, const float* __restrict__ embd,
                                                   const float* __restrict__ norm_w, int8_t* q_out, float* s_out,
                                                   float* h_out, int reset_moe, int reset_amax) {
   extern __shared__ float xs[];
@@ -78,12 +89,23 @@ __global__ void __launch_bounds__(256) k_pre_norm(Dims D, DecodeBufs B, int mode
   } else if (mode == 2) {
     const float* y = B.y + (size_t)t * (D.k + 1) * d;
     float sc[MAX_TOPK];
-    for (int r = 0; r < D.k; r++) sc[r] = fmul(B.selw[t * D.k + r], D.wscale);
+#pragma unroll
+    for (int r = 0; r < MAX_TOPK; r++) sc[r] = r < D.k ? fmul(B.selw[t * D.k + r], D.wscale) : 0.0f;
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
+      float yv[MAX_TOPK + 1];  // every row's element loaded before the rank-order sum
+#pragma unroll
+      for (int r = 0; r <= MAX_TOPK; r++) yv[r] = (r < D.k || (r == D.k && D.nsh > 0)) ? y[r * d + i] : 0.0f;
+      const float xi = x[i];
       float o = 0.0f;
-      for (int r = 0; r < D.k; r++) o = fadd(o, fmul(sc[r], y[r * d + i]));
-      if (D.nsh > 0) o = fadd(o, y[D.k * d + i]);
-      xs[i] = fadd(x[i], o);
+#pragma unroll
+      for (int r = 0; r < MAX_TOPK; r++)
+        if (r < D.k) o = fadd(o, fmul(sc[r], yv[r]));
+      if (D.nsh > 0) {
+#pragma unroll
+        for (int r = 0; r <= MAX_TOPK; r++)
+          if (r == D.k) o = fadd(o, yv[r]);
+      }
+      xs[i] = fadd(xi, o);
     }
   } else {
     for (int i = threadIdx.x; i < d; i += blockDim.x) xs[i] = x[i];
@@ -250,12 +272,27 @@ __global__ void __launch_bounds__(ROWS * 8) k_mv_tokens(Dims D, DecodeBufs B, Q8
 // id), gate weights = raw scores (optionally renormalized), expert token lists.
 // ------------------------------------------------------------------------------------------
 // prenormed != 0: B.h2 already holds the normed hidden state (op-level MoE entry point).
-__global__ void __launch_bounds__(256) k_route(Dims D, DecodeBufs B, LayerDev Ld, int layer, int prenormed) {
+constexpr int ROUTE_THREADS = 1024;
+constexpr int ROUTE_ROWS = 2;  // router rows per warp held in registers (covers 64 experts)
+
+template <int NI>  // d / 32 (0: rows are read during the dot, any d)
+__global__ void __launch_bounds__(ROUTE_THREADS) k_route(Dims D, DecodeBufs B, LayerDev Ld, int layer, int prenormed) {
   extern __shared__ float hs[];  // d floats
   __shared__ float red[32];
   __shared__ float logit_s[128], score_s[128], selsc_s[128];
   __shared__ int rank_e[MAX_TOPK];
   const int t = blockIdx.x, d = D.d;
+  // this warp's router rows, loaded before the norm so their latency overlaps it
+  const int rwarp = threadIdx.x >> 5, rlane = threadIdx.x & 31;
+  float wr[ROUTE_ROWS][NI > 0 ? NI : 1];
+  if (NI > 0 && Ld.moe) {
+#pragma unroll
+    for (int rr = 0; rr < ROUTE_ROWS; rr++) {
+      const int e = rwarp + rr * (ROUTE_THREADS / 32);
+#pragma unroll
+      for (int i = 0; i < NI; i++) wr[rr][i] = e < D.ne ? Ld.router[(size_t)e * d + 32 * i + rlane] : 0.0f;
+    }
+  }
   if (prenormed) {
     for (int i = threadIdx.x; i < d; i += blockDim.x) hs[i] = B.h2[(size_t)t * d + i];
   } else {
@@ -273,7 +310,20 @@ __global__ void __launch_bounds__(256) k_route(Dims D, DecodeBufs B, LayerDev Ld
   quant_row_block(hs, d, B.qh + (size_t)t * d, B.sh + (size_t)t * q8_ss(d >> 5));
   if (!Ld.moe) return;
   const int ne = D.ne, k = D.k, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int e = warp; e < ne; e += nw) {
+  if (NI > 0) {
+#pragma unroll
+    for (int rr = 0; rr < ROUTE_ROWS; rr++) {
+      const int e = warp + rr * nw;
+      if (e < ne) {
+        float acc = 0.0f;  // ops::dot lane order, as dot_ref_warp
+#pragma unroll
+        for (int i = 0; i < NI; i++) acc = __fmaf_rn(wr[rr][i], hs[32 * i + rlane], acc);
+        const float lg = dot_ref_warp_finish(acc);
+        if (rlane == 0) logit_s[e] = lg;
+      }
+    }
+  }
+  for (int e = warp + (NI > 0 ? ROUTE_ROWS * nw : 0); e < ne; e += nw) {
     float lg = dot_ref_warp(Ld.router + (size_t)e * d, hs, d);
     if ((threadIdx.x & 31) == 0) logit_s[e] = lg;
   }
@@ -1087,12 +1137,15 @@ void launch_lmhead(const Dims& D, const DecodeBufs& B, const Q8M& W, const int8_
 
 void launch_pre_norm(const Dims& D, const DecodeBufs& B, int mode, const float* embd, const float* norm_w,
                      int8_t* q_out, float* s_out, float* h_out, int reset_moe, int reset_amax, cudaStream_t st) {
-  k_pre_norm<<<B.T, 256, D.d * sizeof(float), st>>>(D, B, mode, embd, norm_w, q_out, s_out, h_out, reset_moe,
-                                                    reset_amax);
+  k_pre_norm<<<B.T, PRE_NORM_THREADS, D.d * sizeof(float), st>>>(D, B, mode, embd, norm_w, q_out, s_out, h_out,
+                                                                 reset_moe, reset_amax);
 }
 
 void launch_route(const Dims& D, const DecodeBufs& B, const LayerDev& L, int layer, int prenormed, cudaStream_t st) {
-  k_route<<<B.T, 256, D.d * sizeof(float), st>>>(D, B, L, layer, prenormed);
+  const size_t sm = D.d * sizeof(float);
+  if (D.d == 768) k_route<24><<<B.T, ROUTE_THREADS, sm, st>>>(D, B, L, layer, prenormed);
+  else if (D.d == 512) k_route<16><<<B.T, ROUTE_THREADS, sm, st>>>(D, B, L, layer, prenormed);
+  else k_route<0><<<B.T, ROUTE_THREADS, sm, st>>>(D, B, L, layer, prenormed);
 }
 
 // MoE combine without a residual (op-level entry point): y_out[t] = rank-order combine.

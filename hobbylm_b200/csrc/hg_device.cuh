@@ -143,14 +143,18 @@ __device__ inline float q8_lane_dot_rt(const int8_t* __restrict__ wq, const floa
 // ops::dot (ops.rs:7-36) of two n-float vectors (n % 32 == 0) by one warp: thread (m = lane/8,
 // l = lane%8) is accumulator m's SIMD lane l, FMA-accumulating elements 32i + 8m + l in order i;
 // then ((a0+a1)+(a2+a3)) per lane and the 8-lane tree. Returns the dot in every lane.
+// The reduction of dot_ref_warp from each lane's accumulator: lane = 8m + l: combine m=0 with m=1
+// (xor 8), m=2 with m=3 -> (a0+a1), (a2+a3); then xor 16; then the 8-lane tree.
+__device__ __forceinline__ float dot_ref_warp_finish(float acc) {
+  acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 8));
+  acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 16));
+  return hsum8_group(acc);
+}
 __device__ __forceinline__ float dot_ref_warp(const float* __restrict__ a, const float* __restrict__ b, int n) {
   int lane = threadIdx.x & 31;
   float acc = 0.0f;
   for (int i = 0; i < n; i += 32) acc = __fmaf_rn(a[i + lane], b[i + lane], acc);
-  // lane = 8m + l: combine m=0 with m=1 (xor 8), m=2 with m=3 -> (a0+a1), (a2+a3); then xor 16.
-  acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 8));
-  acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 16));
-  return hsum8_group(acc);
+  return dot_ref_warp_finish(acc);
 }
 
 // Orderable 32-bit key of a float (larger float -> larger key).
