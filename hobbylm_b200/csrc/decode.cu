@@ -15,9 +15,34 @@
 // reference's loops (one thread per chain).
 #include <cfloat>
 
+#include <utility>
+
 #include "hg_model.cuh"
 
 namespace hg {
+
+// Steps of up to this many tokens launch their kernels with programmatic stream serialization
+// (see pdl_wait in hg_device.cuh): their kernels are short, so hiding each launch and each
+// kernel's weight-load latency behind the previous kernel pays. Larger steps run multi-wave grids,
+// where early-launched CTAs would only hold SM slots while they wait; they launch normally.
+constexpr int PDL_MAX_T = 64;
+
+// Launch (programmatic when pdl); errors are left for cudaGetLastError like a <<<>>> launch.
+template <typename... P, typename... Args>
+static inline void launch_pdl(bool pdl, void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // ------------------------------------------------------------------------------------------
 // Block reductions
@@ -75,6 +100,8 @@ __global__ void __launch_bounds__(PRE_NORM_THREADS) k_pre_norm(Dims D, DecodeBuf
   __shared__ float red[32];
   const int t = blockIdx.x, d = D.d;
   float* x = B.x + (size_t)t * d;
+  pdl_wait();
+  pdl_trigger();
   if (mode == 0) {
     int tok = B.tok[t];
     if (tok < 0 || tok >= D.vocab) {
@@ -224,9 +251,11 @@ __global__ void __launch_bounds__(ROWS * 8) k_mv_tokens(Dims D, DecodeBufs B, Q8
   const int row = blockIdx.x * ROWS + rl;
   const bool valid_row = row < W.rows;
   const int tbeg = blockIdx.y * ty, tend = min(B.T, tbeg + ty);
-  if (tbeg >= tend) return;
   RowDot<NB> rd;
-  rd.init(W.row_q(0, valid_row ? row : 0), W.row_s(0, valid_row ? row : 0), lane, nb);
+  rd.init(W.row_q(0, valid_row ? row : 0), W.row_s(0, valid_row ? row : 0), lane, nb);  // weights: before the wait
+  pdl_wait();
+  pdl_trigger();
+  if (tbeg >= tend) return;
   __shared__ unsigned long long best_s[TT > 0 ? TT : 1];
   auto emit = [&](int i, int t, float v) {
     if (EPI == EPI_STORE) {
@@ -293,6 +322,8 @@ __global__ void __launch_bounds__(ROUTE_THREADS) k_route(Dims D, DecodeBufs B, L
       for (int i = 0; i < NI; i++) wr[rr][i] = e < D.ne ? Ld.router[(size_t)e * d + 32 * i + rlane] : 0.0f;
     }
   }
+  pdl_wait();
+  pdl_trigger();
   if (prenormed) {
     for (int i = threadIdx.x; i < d; i += blockDim.x) hs[i] = B.h2[(size_t)t * d + i];
   } else {
@@ -387,32 +418,42 @@ __global__ void __launch_bounds__(PAIRS * 16) k_ffn_up(Dims D, DecodeBufs B, Lay
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ int ent_s[TT];
   const int cols = D.d, nb = cols >> 5, ss = q8_ss(nb);
-  const int grp = blockIdx.y;
+  const int grp = blockIdx.y, pair0 = blockIdx.x * PAIRS;
+  const int lane = threadIdx.x & 7, rg = threadIdx.x >> 3, pr = rg >> 1, is_up = rg & 1;
+  const int row = pair0 + pr;
+  // group 0 (shared expert or dense FFN) has fixed weights: load them before the wait; the routed
+  // groups' experts come from the router, the kernel just before this one
+  RowDot<NB> rd;
+  const bool fixed = grp == 0 && !(Ld.moe && D.nsh == 0);
+  const int fdim0 = Ld.moe ? D.f : D.df;
+  if (fixed) {
+    const Q8M M = Ld.moe ? (is_up ? Ld.sup : Ld.sgate) : (is_up ? Ld.up : Ld.gate);
+    const int r = row < fdim0 ? row : 0;
+    rd.init(M.row_q(0, r), M.row_s(0, r), lane, nb);
+  }
+  pdl_wait();
+  pdl_trigger();
   int expert = 0, nent, fdim;
   if (grp == 0) {
-    if (Ld.moe && D.nsh == 0) return;
+    if (!fixed) return;
     nent = B.T;
-    fdim = Ld.moe ? D.f : D.df;
+    fdim = fdim0;
   } else {
     if (!Ld.moe || grp - 1 >= B.ecount[D.ne]) return;
     expert = B.active[grp - 1];
     nent = B.ecount[expert];
     fdim = D.f;
   }
-  const int pair0 = blockIdx.x * PAIRS;
   if (pair0 >= fdim) return;
   int8_t* aq_s = reinterpret_cast<int8_t*>(smem);
   float* as_s = reinterpret_cast<float*>(smem + (size_t)TT * cols);
-  const int lane = threadIdx.x & 7, rg = threadIdx.x >> 3, pr = rg >> 1, is_up = rg & 1;
-  const int row = pair0 + pr;
   const bool valid_row = row < fdim;
-  const Q8M M = grp == 0 ? (Ld.moe ? (is_up ? Ld.sup : Ld.sgate) : (is_up ? Ld.up : Ld.gate))
-                         : (is_up ? Ld.up : Ld.gate);
-  const int mi = grp == 0 ? 0 : expert;
   const int ebeg = blockIdx.z * ez, eend = min(nent, ebeg + ez);
   if (ebeg >= eend) return;
-  RowDot<NB> rd;
-  rd.init(M.row_q(mi, valid_row ? row : 0), M.row_s(mi, valid_row ? row : 0), lane, nb);
+  if (!fixed) {
+    const Q8M M = is_up ? Ld.up : Ld.gate;
+    rd.init(M.row_q(expert, valid_row ? row : 0), M.row_s(expert, valid_row ? row : 0), lane, nb);
+  }
   for (int e0 = ebeg; e0 < eend; e0 += TT) {
     int n = min(TT, eend - e0);
     __syncthreads();
@@ -461,17 +502,28 @@ template <int NB, int ROWS, int TT>
 __global__ void __launch_bounds__(ROWS * 8) k_ffn_down(Dims D, DecodeBufs B, LayerDev Ld, int ez) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ int ent_s[TT];
+  // the expert tables come from the router, two kernels back (readable before the wait); the
+  // activations come from k_ffn_up, just before
   const int grp = blockIdx.y;
-  int expert = 0, nent, fdim;
+  int expert = 0, nent = 0, fdim = 0;
+  bool work = true;
   if (grp == 0) {
-    if (Ld.moe && D.nsh == 0) return;
+    work = !(Ld.moe && D.nsh == 0);
     nent = B.T;
     fdim = Ld.moe ? D.f : D.df;
   } else {
-    if (!Ld.moe || grp - 1 >= B.ecount[D.ne]) return;
-    expert = B.active[grp - 1];
-    nent = B.ecount[expert];
-    fdim = D.f;
+    work = Ld.moe && grp - 1 < B.ecount[D.ne];
+    if (work) {
+      expert = B.active[grp - 1];
+      nent = B.ecount[expert];
+      fdim = D.f;
+    }
+  }
+  const int ebeg = blockIdx.z * ez, eend = min(nent, ebeg + ez);
+  if (!work || ebeg >= eend) {
+    pdl_wait();
+    pdl_trigger();
+    return;
   }
   const Q8M W = (grp == 0 && Ld.moe) ? Ld.sdown : Ld.down;
   const int cols = fdim, nb = cols >> 5, ss = q8_ss(nb);
@@ -481,10 +533,10 @@ __global__ void __launch_bounds__(ROWS * 8) k_ffn_down(Dims D, DecodeBufs B, Lay
   const int row = blockIdx.x * ROWS + rl;
   const bool valid_row = row < D.d;
   const int mi = grp == 0 ? 0 : expert;
-  const int ebeg = blockIdx.z * ez, eend = min(nent, ebeg + ez);
-  if (ebeg >= eend) return;
   RowDot<NB> rd;
   rd.init(W.row_q(mi, valid_row ? row : 0), W.row_s(mi, valid_row ? row : 0), lane, nb);
+  pdl_wait();
+  pdl_trigger();
   for (int e0 = ebeg; e0 < eend; e0 += TT) {
     int n = min(TT, eend - e0);
     __syncthreads();
@@ -628,6 +680,8 @@ __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
   __shared__ int g_s;
   __shared__ int pg_s[1024];  // page ids of the item's chunks (ATT_CHUNK / PAGE per chunk)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_trigger();
   const int total = attn_item_prefix(A, prefix_s, &g_s);
   const int G = g_s;
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
@@ -794,6 +848,8 @@ __global__ void __launch_bounds__(SMX_THREADS) k_attn_softmax(AttnArgs A) {
   __shared__ float m_s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t = blockIdx.x / A.nh, h = blockIdx.x - t * A.nh;
+  pdl_wait();
+  pdl_trigger();
   const int pos = A.pos[t];
   if (pos < 0 || pos >= A.max_pos) return;  // flagged by k_attn_scores
   const int n = pos + 1, nch = (n + ATT_CHUNK - 1) / ATT_CHUNK;
@@ -894,12 +950,18 @@ __global__ void __launch_bounds__(NT) k_attn_pv(AttnArgs A) {
   const int tid = threadIdx.x, lane = tid & 31;
   const int slice = blockIdx.x % DS, tk = blockIdx.x / DS;
   const int t = tk / A.nkv, kvh = tk - t * A.nkv, d = slice * NT + tid;
-  const int pos = A.pos[t];
-  if (pos < 0 || pos >= A.max_pos) return;  // flagged by k_attn_scores
+  const int pos = A.pos[t];  // positions and page ids are older than the previous kernel
+  if (pos < 0 || pos >= A.max_pos) {  // flagged by k_attn_scores
+    pdl_wait();
+    pdl_trigger();
+    return;
+  }
   const int n = pos + 1, npages = (n + PAGE - 1) / PAGE;
   const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
   for (int p = tid; p < npages; p += NT) bt_s[p] = bt[p];
   const int h0 = kvh * REP;
+  pdl_wait();  // 1/sum and e come from k_attn_softmax
+  pdl_trigger();
   if (tid < REP) inv_s[tid] = A.rinv[(size_t)t * A.nh + h0 + tid];
   const float* erow0 = A.S + ((size_t)t * A.nh + h0) * A.s_stride;
   const float* vpage0 = A.v_pool + (long long)kvh * PAGE * HD + slice * NT;
@@ -991,28 +1053,40 @@ __global__ void __launch_bounds__(32 * REP) k_attn_pv_hw(AttnArgs A) {
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int slice = blockIdx.x % DS, tk = blockIdx.x / DS;
   const int t = tk / A.nkv, kvh = tk - t * A.nkv, d = slice * 32 + lane, h = kvh * REP + w;
-  const int pos = A.pos[t];
-  if (pos < 0 || pos >= A.max_pos) return;  // flagged by k_attn_scores
+  const int pos = A.pos[t];  // positions, page ids and V rows are older than the previous kernel
+  if (pos < 0 || pos >= A.max_pos) {  // flagged by k_attn_scores
+    pdl_wait();
+    pdl_trigger();
+    return;
+  }
   const int n = pos + 1, npages = (n + PAGE - 1) / PAGE;
   const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
   for (int p = tid; p < npages; p += NT) bt_s[p] = bt[p];
-  const float inv = A.rinv[(size_t)t * A.nh + h];
   // this thread's pieces: V row tid / 8, dims 4 * (tid % 8) .. + 3 of the slice; e piece tid (< ESEG)
   const int vrow = tid >> 3, vcol = (tid & 7) * 4;
   const float* vsrc = A.v_pool + (long long)kvh * PAGE * HD + slice * 32 + vrow * HD + vcol;
   const int er = tid / (PAGE / 4), eq = tid - er * (PAGE / 4);
   const float* esrc = A.S + ((size_t)t * A.nh + kvh * REP + (tid < ESEG ? er : 0)) * A.s_stride + eq * 4;
-  auto load = [&](int pg, float4& v, float4& e) {  // e rows run to s_stride >= npages * PAGE
-    if (pg < npages) {
-      v = __ldg(reinterpret_cast<const float4*>(vsrc + (long long)bt_s[pg] * A.page_stride));
-      if (tid < ESEG) e = *reinterpret_cast<const float4*>(esrc + pg * PAGE);
-    }
+  auto load_v = [&](int pg, float4& v) {
+    if (pg < npages) v = __ldg(reinterpret_cast<const float4*>(vsrc + (long long)bt_s[pg] * A.page_stride));
+  };
+  auto load_e = [&](int pg, float4& e) {  // e rows run to s_stride >= npages * PAGE
+    if (pg < npages && tid < ESEG) e = *reinterpret_cast<const float4*>(esrc + pg * PAGE);
+  };
+  auto load = [&](int pg, float4& v, float4& e) {
+    load_v(pg, v);
+    load_e(pg, e);
   };
   float4 rv[D], re[D];
   float o = 0.0f;
   __syncthreads();  // bt_s
 #pragma unroll
-  for (int k = 0; k < D; k++) load(k, rv[k], re[k]);
+  for (int k = 0; k < D; k++) load_v(k, rv[k]);
+  pdl_wait();  // 1/sum and e come from k_attn_softmax
+  pdl_trigger();
+  const float inv = A.rinv[(size_t)t * A.nh + h];
+#pragma unroll
+  for (int k = 0; k < D; k++) load_e(k, re[k]);
   for (int pg0 = 0; pg0 < npages; pg0 += D) {
 #pragma unroll
     for (int k = 0; k < D; k++) {
@@ -1060,6 +1134,8 @@ __global__ void __launch_bounds__(32 * REP) k_attn_pv_hw(AttnArgs A) {
 // ------------------------------------------------------------------------------------------
 __global__ void k_feedback(DecodeBufs B, int32_t* tok, int32_t* pos, int32_t* gen, int gen_cap, int32_t* step) {
   const int t = threadIdx.x;
+  pdl_wait();
+  pdl_trigger();
   const int s = *step;
   __syncthreads();
   if (t < B.T) {
@@ -1075,7 +1151,7 @@ __global__ void k_feedback(DecodeBufs B, int32_t* tok, int32_t* pos, int32_t* ge
 
 void launch_feedback(const DecodeBufs& B, int32_t* tok, int32_t* pos, int32_t* gen, int gen_cap, int32_t* step,
                      cudaStream_t st) {
-  k_feedback<<<1, 256, 0, st>>>(B, tok, pos, gen, gen_cap, step);
+  launch_pdl(B.T <= PDL_MAX_T, k_feedback, dim3(1), dim3(256), 0, st, B, tok, pos, gen, gen_cap, step);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -1083,6 +1159,8 @@ void launch_feedback(const DecodeBufs& B, int32_t* tok, int32_t* pos, int32_t* g
 // ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_quant_rows(const float* x, int cols, int8_t* q, float* s) {
   const int t = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
   quant_row_block(x + (size_t)t * cols, cols, q + (size_t)t * cols, s + (size_t)t * q8_ss(cols >> 5));
 }
 
@@ -1112,13 +1190,13 @@ static void launch_mv_tokens_t(const Dims& D, const DecodeBufs& B, const Q8M& W,
   if (B.T == 1) {
     constexpr int ROWS = 8, TT = 1;
     dim3 grid((W.rows + ROWS - 1) / ROWS);
-    HG_NB_SWITCH(nb, k_mv_tokens<NB, ROWS, TT, EPI><<<grid, ROWS * 8, act_smem(TT, W.cols), st>>>(D, B, W, aq, as, out, ostride, 1));
+    HG_NB_SWITCH(nb, launch_pdl(B.T <= PDL_MAX_T, k_mv_tokens<NB, ROWS, TT, EPI>, grid, dim3(ROWS * 8), act_smem(TT, W.cols), st, D, B, W, aq, as, out, ostride, 1));
   } else {
     constexpr int ROWS = 32, TT = 8;
     // token chunks of MV_TY tokens: enough CTAs for small matrices, weights re-read from L2 per chunk
     const int ty = MV_TY;
     dim3 grid((W.rows + ROWS - 1) / ROWS, (B.T + ty - 1) / ty);
-    HG_NB_SWITCH(nb, k_mv_tokens<NB, ROWS, TT, EPI><<<grid, ROWS * 8, act_smem(TT, W.cols), st>>>(D, B, W, aq, as, out, ostride, ty));
+    HG_NB_SWITCH(nb, launch_pdl(B.T <= PDL_MAX_T, k_mv_tokens<NB, ROWS, TT, EPI>, grid, dim3(ROWS * 8), act_smem(TT, W.cols), st, D, B, W, aq, as, out, ostride, ty));
   }
 }
 
@@ -1137,20 +1215,23 @@ void launch_lmhead(const Dims& D, const DecodeBufs& B, const Q8M& W, const int8_
 
 void launch_pre_norm(const Dims& D, const DecodeBufs& B, int mode, const float* embd, const float* norm_w,
                      int8_t* q_out, float* s_out, float* h_out, int reset_moe, int reset_amax, cudaStream_t st) {
-  k_pre_norm<<<B.T, PRE_NORM_THREADS, D.d * sizeof(float), st>>>(D, B, mode, embd, norm_w, q_out, s_out, h_out,
-                                                                 reset_moe, reset_amax);
+  launch_pdl(B.T <= PDL_MAX_T, k_pre_norm, dim3(B.T), dim3(PRE_NORM_THREADS), D.d * sizeof(float), st, D, B, mode, embd, norm_w, q_out,
+             s_out, h_out, reset_moe, reset_amax);
 }
 
 void launch_route(const Dims& D, const DecodeBufs& B, const LayerDev& L, int layer, int prenormed, cudaStream_t st) {
   const size_t sm = D.d * sizeof(float);
-  if (D.d == 768) k_route<24><<<B.T, ROUTE_THREADS, sm, st>>>(D, B, L, layer, prenormed);
-  else if (D.d == 512) k_route<16><<<B.T, ROUTE_THREADS, sm, st>>>(D, B, L, layer, prenormed);
-  else k_route<0><<<B.T, ROUTE_THREADS, sm, st>>>(D, B, L, layer, prenormed);
+  const dim3 g(B.T), b(ROUTE_THREADS);
+  if (D.d == 768) launch_pdl(B.T <= PDL_MAX_T, k_route<24>, g, b, sm, st, D, B, L, layer, prenormed);
+  else if (D.d == 512) launch_pdl(B.T <= PDL_MAX_T, k_route<16>, g, b, sm, st, D, B, L, layer, prenormed);
+  else launch_pdl(B.T <= PDL_MAX_T, k_route<0>, g, b, sm, st, D, B, L, layer, prenormed);
 }
 
 // MoE combine without a residual (op-level entry point): y_out[t] = rank-order combine.
 __global__ void k_moe_combine(Dims D, DecodeBufs B, float* y_out) {
   const int t = blockIdx.x, d = D.d;
+  pdl_wait();
+  pdl_trigger();
   const float* y = B.y + (size_t)t * (D.k + 1) * d;
   float sc[MAX_TOPK];
   for (int r = 0; r < D.k; r++) sc[r] = fmul(B.selw[t * D.k + r], D.wscale);
@@ -1174,22 +1255,22 @@ void launch_ffn(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaStrea
   if (B.T == 1) {
     constexpr int PAIRS = 16, TT = 1;
     dim3 grid((fdim + PAIRS - 1) / PAIRS, groups, nz);
-    HG_NB_SWITCH(nb_up, k_ffn_up<NB, PAIRS, TT><<<grid, PAIRS * 16, act_smem(TT, D.d), st>>>(D, B, L, ez));
+    HG_NB_SWITCH(nb_up, launch_pdl(B.T <= PDL_MAX_T, k_ffn_up<NB, PAIRS, TT>, grid, dim3(PAIRS * 16), act_smem(TT, D.d), st, D, B, L, ez));
   } else {
     constexpr int PAIRS = 16, TT = 8;
     dim3 grid((fdim + PAIRS - 1) / PAIRS, groups, nz);
-    HG_NB_SWITCH(nb_up, k_ffn_up<NB, PAIRS, TT><<<grid, PAIRS * 16, act_smem(TT, D.d), st>>>(D, B, L, ez));
+    HG_NB_SWITCH(nb_up, launch_pdl(B.T <= PDL_MAX_T, k_ffn_up<NB, PAIRS, TT>, grid, dim3(PAIRS * 16), act_smem(TT, D.d), st, D, B, L, ez));
   }
   // dense layers and the shared expert use the down matrix of their own width
   const int nb_dn = fdim >> 5;
   if (B.T == 1) {
     constexpr int ROWS = 8, TT = 1;
     dim3 grid((D.d + ROWS - 1) / ROWS, groups, nz);
-    HG_NB_SWITCH(nb_dn, k_ffn_down<NB, ROWS, TT><<<grid, ROWS * 8, act_smem(TT, fdim), st>>>(D, B, L, ez));
+    HG_NB_SWITCH(nb_dn, launch_pdl(B.T <= PDL_MAX_T, k_ffn_down<NB, ROWS, TT>, grid, dim3(ROWS * 8), act_smem(TT, fdim), st, D, B, L, ez));
   } else {
     constexpr int ROWS = 32, TT = 8;
     dim3 grid((D.d + ROWS - 1) / ROWS, groups, nz);
-    HG_NB_SWITCH(nb_dn, k_ffn_down<NB, ROWS, TT><<<grid, ROWS * 8, act_smem(TT, fdim), st>>>(D, B, L, ez));
+    HG_NB_SWITCH(nb_dn, launch_pdl(B.T <= PDL_MAX_T, k_ffn_down<NB, ROWS, TT>, grid, dim3(ROWS * 8), act_smem(TT, fdim), st, D, B, L, ez));
   }
 }
 
@@ -1209,16 +1290,17 @@ constexpr size_t pv_smem(int nt, int slots, int rep, int bt_stride) {
 
 template <int HD, int REP, int NT, int SLOTS>
 static void launch_pv(const AttnArgs& A, cudaStream_t st) {
-  k_attn_pv<HD, REP, NT, SLOTS><<<A.T * A.nkv * (HD / NT), NT, pv_smem(NT, SLOTS, REP, A.bt_stride), st>>>(A);
+  launch_pdl(A.T <= PDL_MAX_T, k_attn_pv<HD, REP, NT, SLOTS>, dim3(A.T * A.nkv * (HD / NT)), dim3(NT), pv_smem(NT, SLOTS, REP, A.bt_stride),
+             st, A);
 }
 
 template <int HD, int REP>
 static cudaError_t launch_attn_t(const AttnArgs& A, int grid, cudaStream_t st, int which) {
-  if (which & 1) k_attn_scores<HD, REP><<<grid, 256, 0, st>>>(A);
+  if (which & 1) launch_pdl(A.T <= PDL_MAX_T, k_attn_scores<HD, REP>, dim3(grid), dim3(256), 0, st, A);
   if (which & 2) {
-    k_attn_softmax<<<A.T * A.nh, SMX_THREADS, 0, st>>>(A);
+    launch_pdl(A.T <= PDL_MAX_T, k_attn_softmax, dim3(A.T * A.nh), dim3(SMX_THREADS), 0, st, A);
     if (REP == 4 && A.T * A.nkv <= PV_SMALL_MAX_PAIRS)
-      k_attn_pv_hw<HD, 4, PV_DEPTH_SMALL><<<A.T * A.nkv * (HD / 32), 128, (size_t)A.bt_stride * 4, st>>>(A);
+      launch_pdl(A.T <= PDL_MAX_T, k_attn_pv_hw<HD, 4, PV_DEPTH_SMALL>, dim3(A.T * A.nkv * (HD / 32)), dim3(128), (size_t)A.bt_stride * 4, st, A);
     else
       launch_pv<HD, REP, pv_nt<HD, PV_NT_LARGE>(), PV_SLOTS_LARGE>(A, st);
   }

@@ -32,6 +32,15 @@ __host__ __device__ inline int q8_pos(int k, int nb) {
 __device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
 __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
 
+// Programmatic dependent launch. A kernel launched with programmatic serialization may start while
+// the previous kernel on the stream is still running. pdl_wait() returns once that kernel has
+// completed and its writes are visible; every decode kernel calls it before reading anything the
+// previous kernel wrote, and calls pdl_trigger() after it, so a kernel starts at most one kernel
+// ahead: anything written two or more kernels earlier may be read before pdl_wait(). Without the
+// launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // f32 exp pinned to the correctly rounded value: (float)exp((double)x). The CPU oracle uses the
 // same definition, so sigmoid / silu / softmax weights match it bit for bit.
 __device__ __forceinline__ float exp_cr(float x) { return (float)exp((double)x); }
