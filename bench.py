@@ -41,6 +41,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-bs1", action="store_true", help="skip the config-4 bs1 sub-measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--bs1-only", action="store_true", help="run only the config-4 bs1 measurement (one GPU)")
     ap.add_argument("--seqs", type=int, default=N_SEQS, help=argparse.SUPPRESS)
     return ap.parse_args()
 
@@ -426,6 +427,10 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.bs1_only:
+        from hobbylm_b200 import synth
+
+        print(json.dumps(run_bs1(synth.cached_model("500M", 0, context_length=CTX), 0)), flush=True)
     else:
         run_ours(args)
 

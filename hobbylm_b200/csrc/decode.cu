@@ -919,7 +919,7 @@ __global__ void __launch_bounds__(SMX_THREADS) k_attn_softmax(AttnArgs A) {
 // head, pages staged through registers) because each CTA must stream its whole context alone.
 constexpr int PV_NT_LARGE = 64, PV_SLOTS_LARGE = 4;
 constexpr int PV_DEPTH_SMALL = 16;  // pages in flight per k_attn_pv_hw CTA (held in registers)
-constexpr int PV_SMALL_MAX_PAIRS = 64;  // (token, kv head) pairs up to which the small shape is used
+constexpr int PV_SMALL_MAX_PAIRS = 192;  // (token, kv head) pairs up to which k_attn_pv_hw is used (measured crossover)
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)

@@ -132,13 +132,14 @@ def test_moe_op_config2_bitexact(native, oracle_mod, moe_inputs, T):
     assert np.array_equal(_bits(y), _bits(y_ref)), f"max |d| {np.abs(y - y_ref).max()}"
 
 
-def test_kv_attn_config3(native, oracle_mod):
+@pytest.mark.parametrize("n_seqs,steps", [(64, 4), (72, 2)])
+def test_kv_attn_config3(native, oracle_mod, n_seqs, steps):
     """Config 3 (reduced step count): 64 sequences, ctx ~ U[512, 4096] (seed 3), 500M head shapes,
-    K/V/Q ~ N(0,1), QK-norm gains 1, RoPE base 1e4, 16-token pages placed by a random permutation."""
+    K/V/Q ~ N(0,1), QK-norm gains 1, RoPE base 1e4, 16-token pages placed by a random permutation.
+    64 sequences take the small-batch value-sum kernel (one warp per q head), 72 the large one."""
     import torch
 
     nh, nkv, hd, eps, theta = 12, 3, 128, 1e-5, 10000.0
-    n_seqs, steps = 64, 4
     rng = np.random.default_rng(3)
     ctx = rng.integers(512, 4097, n_seqs)
     max_pos = int(ctx.max()) + steps + 1
