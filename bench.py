@@ -278,7 +278,7 @@ def run_ours(args):
         "e2e": {"value": round(total_tokens / e2e_s, 1), "unit": "tok/s",
                 "h2d_bytes_per_step": int(reduce_sum(n_local * 12, world)),
                 "d2h_bytes_per_step": int(reduce_sum(n_local * 8 + 4, world))},
-        "roofline": {"bound": "hbm", "kernel": "attention (k_attn_scores + k_attn_softmax + k_attn_pv), one layer",
+        "roofline": {"bound": "hbm", "kernel": "attention (k_qk_prep + k_attn_scores + k_attn_softmax + k_attn_pv), one layer",
                      "achieved": round(att_gbs, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(att_gbs / hbm, 4), "peak_kind": peak_kind,
                      "traffic": traffic, "ms_scores": round(ms_s, 4), "ms_out": round(ms_o, 4),

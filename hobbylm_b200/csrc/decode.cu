@@ -671,11 +671,42 @@ __device__ inline int attn_item_prefix(const AttnArgs& A, int* prefix_s, int* g_
   return prefix_s[A.T];
 }
 
+// QK-norm (sequential sum, model.rs:753-763) + RoPE of every q head of a token into qn, and of
+// the token's k heads, appended with its v heads to their page slot (model.rs:199-210). One CTA
+// per token, one warp per head (q heads first, then kv heads).
+template <int HD>
+__global__ void k_qk_prep(AttnArgs A) {
+  extern __shared__ __align__(16) float prep_s[];  // one HD-float scratch per warp
+  const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_trigger();
+  const int pos = A.pos[t];
+  if (pos < 0 || pos >= A.max_pos || pos / PAGE >= A.bt_stride) return;  // flagged by k_attn_scores
+  const float* qkv = A.qkv + (size_t)t * A.qkv_stride;
+  const int qd = A.nh * HD, kvd = A.nkv * HD;
+  const float* cs = A.rope_cos + (size_t)pos * (HD / 2);
+  const float* sn = A.rope_sin + (size_t)pos * (HD / 2);
+  float* buf = prep_s + warp * HD;
+  if (warp < A.nh) {
+    norm_rope_warp<HD>(qkv + warp * HD, A.q_norm, A.eps, cs, sn, buf);
+    float* dst = A.qn + ((size_t)t * A.nh + warp) * HD;
+    for (int j = lane; j < HD; j += 32) dst[j] = buf[j];
+  } else if (warp < A.nh + A.nkv) {
+    const int kvh = warp - A.nh;
+    const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
+    const long long off = (long long)bt[pos / PAGE] * A.page_stride + ((long long)kvh * PAGE + pos % PAGE) * HD;
+    norm_rope_warp<HD>(qkv + qd + kvh * HD, A.k_norm, A.eps, cs, sn, buf);
+    for (int j = lane; j < HD; j += 32) {
+      A.k_pool[off + j] = buf[j];
+      A.v_pool[off + j] = qkv[qd + kvd + kvh * HD + j];
+    }
+  }
+}
+
 template <int HD, int REP>
 __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
   constexpr int E = HD / 32;
   __shared__ __align__(16) float q_s[REP][HD];
-  __shared__ __align__(16) float knew_s[HD];
   __shared__ int prefix_s[257];
   __shared__ int g_s;
   __shared__ int pg_s[1024];  // page ids of the item's chunks (ATT_CHUNK / PAGE per chunk)
@@ -698,25 +729,12 @@ __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
     const int nch = (n + ATT_CHUNK - 1) / ATT_CHUNK;
     const int cbeg = cg * G, cend = min(nch, cbeg + G);
     const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
-    const float* qkv = A.qkv + (size_t)t * A.qkv_stride;
-    const int qd = A.nh * HD, kvd = A.nkv * HD;
-    const float* cs = A.rope_cos + (size_t)pos * (HD / 2);
-    const float* sn = A.rope_sin + (size_t)pos * (HD / 2);
-    const bool has_new = (pos / ATT_CHUNK) >= cbeg && (pos / ATT_CHUNK) < cend;
     __syncthreads();
     const int pg0 = cbeg * (ATT_CHUNK / PAGE), npg = min((cend - cbeg) * (ATT_CHUNK / PAGE), 1024);
     for (int i = threadIdx.x; i < npg; i += blockDim.x) pg_s[i] = pg0 + i < A.bt_stride ? bt[pg0 + i] : 0;
-    if (warp < REP) norm_rope_warp<HD>(qkv + (kvh * REP + warp) * HD, A.q_norm, A.eps, cs, sn, q_s[warp]);
-    if (has_new) {
-      const long long off =
-          (long long)bt[pos / PAGE] * A.page_stride + ((long long)kvh * PAGE + pos % PAGE) * HD;
-      if (warp == REP) {
-        norm_rope_warp<HD>(qkv + qd + kvh * HD, A.k_norm, A.eps, cs, sn, knew_s);
-        for (int j = lane; j < HD; j += 32) A.k_pool[off + j] = knew_s[j];
-      } else if (warp == REP + 1) {
-        for (int j = lane; j < HD; j += 32) A.v_pool[off + j] = qkv[qd + kvd + kvh * HD + j];
-      }
-    }
+    // the group's q heads, QK-normed and roped by k_qk_prep (which also appended the new K row)
+    const float* qsrc = A.qn + ((size_t)t * A.nh + kvh * REP) * HD;
+    for (int i = threadIdx.x; i < REP * HD; i += blockDim.x) q_s[i / HD][i % HD] = qsrc[i];
     __syncthreads();
     // ops::dot lane mapping: accumulator m's SIMD lane l sums elements 32i + 8m + l (FMA, i
     // ascending); lane sums are (a0+a1)+(a2+a3), then the 8-lane tree. Here a group of 8 threads
@@ -734,7 +752,7 @@ __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
     const float* kbase = A.k_pool + (long long)kvh * PAGE * HD;
     auto prefetch_rows = [&](int c) {
       const int p = c * ATT_CHUNK + warp * 8 + (lane >> 2);
-      if (c < cend && p < n && p != pos) {
+      if (c < cend && p < n) {
         const int pgi = p / PAGE - pg0;
         const int page = pgi < 1024 ? pg_s[pgi] : bt[p / PAGE];
         const float* r = kbase + (long long)page * A.page_stride + (long long)(p % PAGE) * HD + (lane & 3) * (HD / 4);
@@ -756,9 +774,7 @@ __global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
         const int pc = p < n ? p : c0;  // positions past the end read a valid row, unused
         const int pgi = pc / PAGE - pg0;
         const int page = pgi < 1024 ? pg_s[pgi] : bt[pc / PAGE];
-        const float* kp = p == pos ? knew_s
-                                   : A.k_pool + (long long)page * A.page_stride +
-                                         ((long long)kvh * PAGE + (pc % PAGE)) * HD;
+        const float* kp = A.k_pool + (long long)page * A.page_stride + ((long long)kvh * PAGE + (pc % PAGE)) * HD;
 #pragma unroll
         for (int i = 0; i < E; i++)
 #pragma unroll
@@ -1296,7 +1312,11 @@ static void launch_pv(const AttnArgs& A, cudaStream_t st) {
 
 template <int HD, int REP>
 static cudaError_t launch_attn_t(const AttnArgs& A, int grid, cudaStream_t st, int which) {
-  if (which & 1) launch_pdl(A.T <= PDL_MAX_T, k_attn_scores<HD, REP>, dim3(grid), dim3(256), 0, st, A);
+  if (which & 1) {
+    const int nw = A.nh + A.nkv;
+    launch_pdl(A.T <= PDL_MAX_T, k_qk_prep<HD>, dim3(A.T), dim3(32 * nw), (size_t)nw * HD * 4, st, A);
+    launch_pdl(A.T <= PDL_MAX_T, k_attn_scores<HD, REP>, dim3(grid), dim3(256), 0, st, A);
+  }
   if (which & 2) {
     launch_pdl(A.T <= PDL_MAX_T, k_attn_softmax, dim3(A.T * A.nh), dim3(SMX_THREADS), 0, st, A);
     if (REP == 4 && A.T * A.nkv <= PV_SMALL_MAX_PAIRS)
@@ -1309,7 +1329,7 @@ static cudaError_t launch_attn_t(const AttnArgs& A, int grid, cudaStream_t st, i
 
 static cudaError_t launch_attn_which(const AttnArgs& A, int grid, cudaStream_t st, int which) {
   int rep = A.nh / A.nkv;
-  if (A.bt_stride > ATT_MAX_BT || !A.rinv) return cudaErrorInvalidValue;
+  if (A.bt_stride > ATT_MAX_BT || !A.rinv || !A.qn || A.nh + A.nkv > 32) return cudaErrorInvalidValue;
   if (A.hd == 128 && rep == 4) return launch_attn_t<128, 4>(A, grid, st, which);
   if (A.hd == 64 && rep == 4) return launch_attn_t<64, 4>(A, grid, st, which);
   if (A.hd == 128 && rep == 2) return launch_attn_t<128, 2>(A, grid, st, which);

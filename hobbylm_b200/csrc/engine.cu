@@ -234,6 +234,7 @@ void alloc_work(hg_engine* e) {
   B.cmax = a.take<float>((size_t)T * c.n_heads * max_chunks * 8);
   B.max_chunks = max_chunks;
   B.rinv = a.take<float>((size_t)T * c.n_heads);
+  B.qn = a.take<float>((size_t)T * D.qd);
   B.logits = a.take<float>((size_t)T * c.vocab_size);
   B.amax = a.take<unsigned long long>(T);
   B.dbg_sel = a.take<int32_t>((size_t)c.n_layers * T * k);
@@ -455,6 +456,7 @@ AttnArgs make_attn_args(hg_engine* e, const DecodeBufs& B, int l) {
   A.s_stride = B.s_stride;
   A.cmax = B.cmax;
   A.rinv = B.rinv;
+  A.qn = B.qn;
   A.out = nullptr;
   A.qo = B.qo;
   A.so = B.so;
@@ -967,7 +969,7 @@ size_t kv_scratch_bytes(const hg_kv_attn_args* a) {
   int max_chunks = (a->max_pos + ATT_CHUNK - 1) / ATT_CHUNK;
   return align256((size_t)a->n_seqs * a->n_heads * kv_s_stride(a) * 4) +
          align256((size_t)a->n_seqs * a->n_heads * max_chunks * 8 * 4) +
-         align256((size_t)a->n_seqs * a->n_heads * 4) + 256;
+         align256((size_t)a->n_seqs * a->n_heads * 4) + align256((size_t)a->n_seqs * a->n_heads * a->head_dim * 4) + 256;
 }
 
 }  // namespace
@@ -1314,6 +1316,7 @@ int hg_op_kv_attn(const hg_kv_attn_args* a, void* scratch, void* stream) {
     const size_t s_bytes = align256((size_t)a->n_seqs * a->n_heads * A.s_stride * 4);
     A.cmax = reinterpret_cast<float*>(base + s_bytes);
     A.rinv = reinterpret_cast<float*>(base + s_bytes + align256((size_t)a->n_seqs * a->n_heads * max_chunks * 8 * 4));
+    A.qn = reinterpret_cast<float*>(reinterpret_cast<char*>(A.rinv) + align256((size_t)a->n_seqs * a->n_heads * 4));
     A.err = nullptr;
     A.out = a->out;
     A.qo = nullptr;

@@ -74,6 +74,7 @@ struct DecodeBufs {
   float* S;                // [T][nh][s_stride] attention scores / exp weights
   long long s_stride;
   float* rinv;             // [T][nh] 1 / softmax denominator
+  float* qn;               // [T][nh][hd] QK-normed, roped q
   float* cmax;             // [T][nh][max_chunks][8] per-warp chunk maxima of the scores
   int max_chunks;
   float* logits;           // [T][vocab] or null
@@ -100,7 +101,8 @@ struct AttnArgs {
   long long page_stride;
   float* S;        // [T][nh][s_stride] scores, then exp(score - max)
   long long s_stride;  // >= max_pos, multiple of 16
-  float* rinv;     // [T][nh] 1 / softmax denominator (split path)
+  float* rinv;     // [T][nh] 1 / softmax denominator
+  float* qn;       // [T][nh][hd] QK-normed, roped q (k_qk_prep)
   float* cmax;     // [T][nh][max_chunks][8] per-warp chunk maxima of the scores
   float* out;      // [T][nh*hd] or null
   int8_t* qo;      // [T][nh*hd] or null
