@@ -582,15 +582,16 @@ __global__ void __launch_bounds__(ROWS * 8) k_ffn_down(Dims D, DecodeBufs B, Lay
 // ------------------------------------------------------------------------------------------
 // Attention (model.rs:199-233) over a paged f32 KV pool, in the reference's arithmetic order.
 //
-// k_attn_scores: work item = (token, kv head, chunk of ATT_CHUNK positions), 8 warps x 8
-//   positions. QK-norm (sequential sum, model.rs:753-763) + RoPE of the item's q heads, and for
-//   the chunk holding the new position the same for k, plus the k/v append to its page slot.
-//   s[t][h][j] = dot(q_h, k_j) * (1/sqrt(hd)) in the ops::dot order; the chunk maximum per head.
+// k_qk_prep: QK-norm (sequential sum, model.rs:753-763) + RoPE of each token's q heads and k
+//   heads; the k and v rows are appended to their page slot.
+// k_attn_scores: work item = (token, kv head, run of chunks of ATT_CHUNK positions), 8 warps x 8
+//   positions per chunk. s[t][h][j] = dot(q_h, k_j) * (1/sqrt(hd)) in the ops::dot order; the
+//   chunk maximum per head and warp.
 // k_attn_softmax: softmax (ops.rs:112-128) per (token, q head): global max, e_j = exp(s_j - max)
 //   (parallel), sum = sequential f32 sum over j, inv = 1/sum.
-// k_attn_pv: every (head, dim) chain accumulates o += (e_j * inv) * v_j[dim] sequentially over j
-//   (model.rs:227-232), V pages streamed into shared memory by cp.async; the result is quantized
-//   per 32-block for the output projection (quant.rs:112-123).
+// k_attn_pv / k_attn_pv_hw: every (head, dim) chain accumulates o += (e_j * inv) * v_j[dim]
+//   sequentially over j (model.rs:227-232); the result is quantized per 32-block for the output
+//   projection (quant.rs:112-123).
 // ------------------------------------------------------------------------------------------
 
 constexpr int ATT_MAX_BT = 4096;  // block-table entries staged in shared memory (contexts <= 65536)

@@ -122,7 +122,8 @@ int hg_decode_kernel_count(hg_engine* e, int n);
 
 /* Device time in ms (CUDA events on the engine stream, mean over iters) of the attention kernels
  * of one decode step of the last layer for these sequences, re-run on their current state (each
- * must have decoded at least one step; the K/V append rewrites the same row). */
+ * must have decoded at least one step; the K/V append rewrites the same row): ms_scores covers the
+ * q/k preparation and the scores, ms_out the softmax and the value sums. */
 int hg_debug_time_attention(hg_engine* e, hg_seq** seqs, int n, int iters, float* ms_scores, float* ms_out);
 
 /* Engine::generate (lib.rs:107-162) on token ids: prefill, then per step mask ids >= 50257,
