@@ -1195,7 +1195,8 @@ __global__ void __launch_bounds__(256) k_quant_rows(const float* x, int cols, in
     default: { constexpr int NB = 0; __VA_ARGS__; } break;  \
   }
 
-constexpr int MV_TY = 16;  // tokens per CTA of the batched matvec
+constexpr int MV_TY = 16;         // tokens per CTA of the batched matvec
+constexpr int MV_TY_LMHEAD = 64;  // the lm_head has rows enough for many CTAs: fewer passes over its weights
 constexpr int FFN_EZ = 16;  // (token, slot) entries per CTA of the batched expert kernels
 
 static inline size_t act_smem(int tt, int cols) { return (size_t)tt * cols + (size_t)tt * q8_ss(cols >> 5) * 4; }
@@ -1211,7 +1212,7 @@ static void launch_mv_tokens_t(const Dims& D, const DecodeBufs& B, const Q8M& W,
   } else {
     constexpr int ROWS = 32, TT = 8;
     // token chunks of MV_TY tokens: enough CTAs for small matrices, weights re-read from L2 per chunk
-    const int ty = MV_TY;
+    const int ty = EPI == EPI_LMHEAD ? MV_TY_LMHEAD : MV_TY;
     dim3 grid((W.rows + ROWS - 1) / ROWS, (B.T + ty - 1) / ty);
     HG_NB_SWITCH(nb, launch_pdl(B.T <= PDL_MAX_T, k_mv_tokens<NB, ROWS, TT, EPI>, grid, dim3(ROWS * 8), act_smem(TT, W.cols), st, D, B, W, aq, as, out, ostride, ty));
   }
