@@ -47,22 +47,6 @@ static inline void launch_pdl(bool pdl, void (*kern)(P...), dim3 grid, dim3 bloc
 // ------------------------------------------------------------------------------------------
 // Block reductions
 // ------------------------------------------------------------------------------------------
-__device__ inline float block_sum(float v, float* red) {
-  int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  v = warp_sum(v);
-  __syncthreads();
-  if (lane == 0) red[w] = v;
-  __syncthreads();
-  float s = 0.0f;
-  if (w == 0) {
-    s = lane < nw ? red[lane] : 0.0f;
-    s = warp_sum(s);
-    if (lane == 0) red[0] = s;
-  }
-  __syncthreads();
-  return red[0];
-}
-
 // Sequential f32 sum of squares of xs[0..n) (ops.rs:85-95 `ss += v * v`, no FMA) computed by one
 // thread; every thread of the block receives the result.
 __device__ inline float seq_sumsq_block(const float* xs, int n, float* red) {
