@@ -398,17 +398,21 @@ __global__ void __launch_bounds__(ROUTE_THREADS) k_route(Dims D, DecodeBufs B, L
 // same rows of up (16 lanes per pair) and writes act = silu(g) * u for every token of the group.
 // ------------------------------------------------------------------------------------------
 template <int NB, int PAIRS, int TT>
-__global__ void __launch_bounds__(PAIRS * 16) k_ffn_up(Dims D, DecodeBufs B, LayerDev Ld, int ez) {
+__global__ void __launch_bounds__(PAIRS * 16) k_ffn_up(Dims D, DecodeBufs B, LayerDev Ld, int ez, int sh) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ int ent_s[TT];
   const int cols = D.d, nb = cols >> 5, ss = q8_ss(nb);
-  const int grp = blockIdx.y, pair0 = blockIdx.x * PAIRS;
+  // y < sh: group 0 (shared expert or dense FFN, all T tokens), chunk y of its entries (z == 0
+  // only); y >= sh: routed group y - sh + 1, whose chunks are strided over the z CTAs
+  const bool g0 = blockIdx.y < (unsigned)sh;
+  const int grp = g0 ? 0 : (int)blockIdx.y - sh + 1, pair0 = blockIdx.x * PAIRS;
+  const int cstep = g0 ? sh : (int)gridDim.z;
   const int lane = threadIdx.x & 7, rg = threadIdx.x >> 3, pr = rg >> 1, is_up = rg & 1;
   const int row = pair0 + pr;
   // group 0 (shared expert or dense FFN) has fixed weights: load them before the wait; the routed
   // groups' experts come from the router, the kernel just before this one
   RowDot<NB> rd;
-  const bool fixed = grp == 0 && !(Ld.moe && D.nsh == 0);
+  const bool fixed = g0 && blockIdx.z == 0 && !(Ld.moe && D.nsh == 0);
   const int fdim0 = Ld.moe ? D.f : D.df;
   if (fixed) {
     const Q8M M = Ld.moe ? (is_up ? Ld.sup : Ld.sgate) : (is_up ? Ld.up : Ld.gate);
@@ -432,14 +436,15 @@ __global__ void __launch_bounds__(PAIRS * 16) k_ffn_up(Dims D, DecodeBufs B, Lay
   int8_t* aq_s = reinterpret_cast<int8_t*>(smem);
   float* as_s = reinterpret_cast<float*>(smem + (size_t)TT * cols);
   const bool valid_row = row < fdim;
-  const int ebeg = blockIdx.z * ez, eend = min(nent, ebeg + ez);
-  if (ebeg >= eend) return;
+  const int ebeg = (g0 ? (int)blockIdx.y : (int)blockIdx.z) * ez;
+  if (ebeg >= nent) return;
   if (!fixed) {
     const Q8M M = is_up ? Ld.up : Ld.gate;
     rd.init(M.row_q(expert, valid_row ? row : 0), M.row_s(expert, valid_row ? row : 0), lane, nb);
   }
-  for (int e0 = ebeg; e0 < eend; e0 += TT) {
-    int n = min(TT, eend - e0);
+  // this CTA's chunks of ez entries (ez % TT == 0), TT entries at a time
+  for (int e0 = ebeg; e0 < nent; e0 += (e0 + TT) % ez == 0 ? TT + (cstep - 1) * ez : TT) {
+    int n = min(TT, nent - e0);
     __syncthreads();
     if (threadIdx.x < n) {
       int code = grp == 0 ? (e0 + threadIdx.x) * 32 : B.elist[(size_t)expert * B.T + e0 + threadIdx.x];
@@ -483,16 +488,18 @@ __global__ void __launch_bounds__(PAIRS * 16) k_ffn_up(Dims D, DecodeBufs B, Lay
 // matrix; y[t][slot][row] = result.
 // ------------------------------------------------------------------------------------------
 template <int NB, int ROWS, int TT>
-__global__ void __launch_bounds__(ROWS * 8) k_ffn_down(Dims D, DecodeBufs B, LayerDev Ld, int ez) {
+__global__ void __launch_bounds__(ROWS * 8) k_ffn_down(Dims D, DecodeBufs B, LayerDev Ld, int ez, int sh) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ int ent_s[TT];
   // the expert tables come from the router, two kernels back (readable before the wait); the
   // activations come from k_ffn_up, just before
-  const int grp = blockIdx.y;
+  const bool g0 = blockIdx.y < (unsigned)sh;  // group / chunk mapping as in k_ffn_up
+  const int grp = g0 ? 0 : (int)blockIdx.y - sh + 1;
+  const int cstep = g0 ? sh : (int)gridDim.z;
   int expert = 0, nent = 0, fdim = 0;
   bool work = true;
   if (grp == 0) {
-    work = !(Ld.moe && D.nsh == 0);
+    work = blockIdx.z == 0 && !(Ld.moe && D.nsh == 0);
     nent = B.T;
     fdim = Ld.moe ? D.f : D.df;
   } else {
@@ -503,8 +510,8 @@ __global__ void __launch_bounds__(ROWS * 8) k_ffn_down(Dims D, DecodeBufs B, Lay
       fdim = D.f;
     }
   }
-  const int ebeg = blockIdx.z * ez, eend = min(nent, ebeg + ez);
-  if (!work || ebeg >= eend) {
+  const int ebeg = (g0 ? (int)blockIdx.y : (int)blockIdx.z) * ez;
+  if (!work || ebeg >= nent) {
     pdl_wait();
     pdl_trigger();
     return;
@@ -521,8 +528,9 @@ __global__ void __launch_bounds__(ROWS * 8) k_ffn_down(Dims D, DecodeBufs B, Lay
   rd.init(W.row_q(mi, valid_row ? row : 0), W.row_s(mi, valid_row ? row : 0), lane, nb);
   pdl_wait();
   pdl_trigger();
-  for (int e0 = ebeg; e0 < eend; e0 += TT) {
-    int n = min(TT, eend - e0);
+  // this CTA's chunks of ez entries (ez % TT == 0), TT entries at a time
+  for (int e0 = ebeg; e0 < nent; e0 += (e0 + TT) % ez == 0 ? TT + (cstep - 1) * ez : TT) {
+    int n = min(TT, nent - e0);
     __syncthreads();
     if (threadIdx.x < n) {
       int code = grp == 0 ? (e0 + threadIdx.x) * 32 : B.elist[(size_t)expert * B.T + e0 + threadIdx.x];
@@ -1181,7 +1189,8 @@ __global__ void __launch_bounds__(256) k_quant_rows(const float* x, int cols, in
 
 constexpr int MV_TY = 16;         // tokens per CTA of the batched matvec
 constexpr int MV_TY_LMHEAD = 64;  // the lm_head has rows enough for many CTAs: fewer passes over its weights
-constexpr int FFN_EZ = 16;  // (token, slot) entries per CTA of the batched expert kernels
+constexpr int FFN_EZ = 16;   // (token, slot) entries per chunk of the batched expert kernels
+constexpr int FFN_ZMAX = 4;  // chunk CTAs per (row tile, routed expert)
 
 static inline size_t act_smem(int tt, int cols) { return (size_t)tt * cols + (size_t)tt * q8_ss(cols >> 5) * 4; }
 
@@ -1249,30 +1258,34 @@ void launch_moe_combine(const Dims& D, const DecodeBufs& B, float* y_out, cudaSt
 }
 
 void launch_ffn(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaStream_t st) {
-  const int groups = L.moe ? 1 + (D.ne < B.T * D.k ? D.ne : B.T * D.k) : 1;
+  // group 0 (shared expert / dense FFN: T entries) over sh y-slices of one ez-entry chunk each; the
+  // routed groups (at most T entries each, usually far fewer) after them, their chunks strided
+  // over nz z-CTAs, so few routed CTAs find no work
+  const int ez = B.T == 1 ? 1 : FFN_EZ, sh = (B.T + ez - 1) / ez;
+  const int nrouted = L.moe ? (D.ne < B.T * D.k ? D.ne : B.T * D.k) : 0;
+  const int groups = sh + nrouted, nz = nrouted > 0 ? std::min(sh, FFN_ZMAX) : 1;
+  static_assert(FFN_EZ % 8 == 0, "whole TT-entry steps per chunk");
   const int fdim = L.moe ? D.f : D.df;
   const int nb_up = D.d >> 5;
-  // entry chunks on grid.z: a group holds at most T entries (each token uses an expert once)
-  const int ez = B.T == 1 ? 1 : FFN_EZ, nz = (B.T + ez - 1) / ez;
   if (B.T == 1) {
     constexpr int PAIRS = 16, TT = 1;
     dim3 grid((fdim + PAIRS - 1) / PAIRS, groups, nz);
-    HG_NB_SWITCH(nb_up, launch_pdl(B.T <= PDL_MAX_T, k_ffn_up<NB, PAIRS, TT>, grid, dim3(PAIRS * 16), act_smem(TT, D.d), st, D, B, L, ez));
+    HG_NB_SWITCH(nb_up, launch_pdl(B.T <= PDL_MAX_T, k_ffn_up<NB, PAIRS, TT>, grid, dim3(PAIRS * 16), act_smem(TT, D.d), st, D, B, L, ez, sh));
   } else {
     constexpr int PAIRS = 16, TT = 8;
     dim3 grid((fdim + PAIRS - 1) / PAIRS, groups, nz);
-    HG_NB_SWITCH(nb_up, launch_pdl(B.T <= PDL_MAX_T, k_ffn_up<NB, PAIRS, TT>, grid, dim3(PAIRS * 16), act_smem(TT, D.d), st, D, B, L, ez));
+    HG_NB_SWITCH(nb_up, launch_pdl(B.T <= PDL_MAX_T, k_ffn_up<NB, PAIRS, TT>, grid, dim3(PAIRS * 16), act_smem(TT, D.d), st, D, B, L, ez, sh));
   }
   // dense layers and the shared expert use the down matrix of their own width
   const int nb_dn = fdim >> 5;
   if (B.T == 1) {
     constexpr int ROWS = 8, TT = 1;
     dim3 grid((D.d + ROWS - 1) / ROWS, groups, nz);
-    HG_NB_SWITCH(nb_dn, launch_pdl(B.T <= PDL_MAX_T, k_ffn_down<NB, ROWS, TT>, grid, dim3(ROWS * 8), act_smem(TT, fdim), st, D, B, L, ez));
+    HG_NB_SWITCH(nb_dn, launch_pdl(B.T <= PDL_MAX_T, k_ffn_down<NB, ROWS, TT>, grid, dim3(ROWS * 8), act_smem(TT, fdim), st, D, B, L, ez, sh));
   } else {
     constexpr int ROWS = 32, TT = 8;
     dim3 grid((D.d + ROWS - 1) / ROWS, groups, nz);
-    HG_NB_SWITCH(nb_dn, launch_pdl(B.T <= PDL_MAX_T, k_ffn_down<NB, ROWS, TT>, grid, dim3(ROWS * 8), act_smem(TT, fdim), st, D, B, L, ez));
+    HG_NB_SWITCH(nb_dn, launch_pdl(B.T <= PDL_MAX_T, k_ffn_down<NB, ROWS, TT>, grid, dim3(ROWS * 8), act_smem(TT, fdim), st, D, B, L, ez, sh));
   }
 }
 
