@@ -19,7 +19,7 @@ ERRORS = {
 
 # every symbol include/hobbygpu.h declares
 EXPORTS = (
-    "hg_last_error", "hg_engine_load", "hg_engine_load_ex", "hg_engine_free", "hg_engine_config", "hg_gguf_config",
+    "hg_last_error", "hg_engine_load", "hg_engine_load_ex", "hg_engine_free", "hg_engine_config", "hg_gguf_config", "hg_gguf_tensor_f32",
     "hg_engine_weight_bytes", "hg_engine_eos", "hg_engine_device_bytes", "hg_seq_create", "hg_seq_free",
     "hg_seq_len", "hg_prefill", "hg_forward", "hg_decode_batch", "hg_generate", "hg_debug_last_routing",
     "hg_q8_pack", "hg_q8_scale_stride", "hg_q8_unpack_qs", "hg_op_q8_matvec", "hg_op_q8_matmul",
@@ -93,6 +93,7 @@ def lib():
         "hg_engine_free": (None, [vp]),
         "hg_engine_config": (i32, [vp, C.POINTER(Config)]),
         "hg_gguf_config": (i32, [C.c_char_p, C.POINTER(Config)]),
+        "hg_gguf_tensor_f32": (i32, [C.c_char_p, C.c_char_p, vp, i64]),
         "hg_engine_weight_bytes": (u64, [vp]),
         "hg_engine_eos": (u32, [vp]),
         "hg_engine_device_bytes": (u64, [vp]),

@@ -1018,6 +1018,18 @@ int hg_gguf_config(const char* gguf_path, hg_config* out) {
   })
 }
 
+int hg_gguf_tensor_f32(const char* gguf_path, const char* name, float* out, int64_t n) {
+  HG_API_TRY({
+    need(gguf_path && name && out, "null argument");
+    Gguf g(gguf_path);
+    const GgufTensor* t = g.tensor(name);
+    if (!t) throw Error(HG_ERR_MISSING, std::string("tensor `") + name + "` not found");
+    need(n == (int64_t)t->n_elems(), "element count differs from the tensor's");
+    std::vector<float> v = g.load(name);
+    std::copy(v.begin(), v.end(), out);
+  })
+}
+
 uint64_t hg_engine_weight_bytes(const hg_engine* e) { return e ? e->ref_weight_bytes : 0; }
 uint32_t hg_engine_eos(const hg_engine* e) { return e ? (uint32_t)e->cfg.eos_token : 0; }
 uint64_t hg_engine_device_bytes(const hg_engine* e) {

@@ -79,6 +79,11 @@ void hg_engine_free(hg_engine* e);
 int hg_engine_config(const hg_engine* e, hg_config* out);
 /* Config::from_gguf alone: parse a GGUF file's header + metadata (no GPU needed). */
 int hg_gguf_config(const char* gguf_path, hg_config* out);
+/* Gguf::load (gguf.rs:250-269): tensor `name` of a GGUF file as f32 on the host (F32 copied; F16,
+ * Q5_0, Q8_0, Q4_K and Q6_K dequantized as gguf.rs:329-468 does). n is the element count of out
+ * and must equal the tensor's (HG_ERR_INVALID otherwise); a missing tensor is HG_ERR_MISSING and
+ * an unsupported type HG_ERR_FORMAT. No GPU work. */
+int hg_gguf_tensor_f32(const char* gguf_path, const char* name, float* out, int64_t n);
 /* Engine::weight_bytes (lib.rs:100-102): bytes of all re-quantized matmul weights (int8 + f32 scales). */
 uint64_t hg_engine_weight_bytes(const hg_engine* e);
 /* Engine::eos (lib.rs:94-96). */

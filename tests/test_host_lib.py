@@ -166,3 +166,53 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_native, "LIB_PATH", str(tmp_path / "nope.so"))
     with pytest.raises(ImportError):
         _native.lib()
+
+
+# block layouts (bytes per block, elements per block, byte offsets of the f16 scale fields)
+_QBLOCKS = {
+    "Q8_0": (34, 32, (0,)),
+    "Q5_0": (22, 32, (0,)),
+    "Q4_K": (144, 256, (0, 2)),
+    "Q6_K": (210, 256, (208,)),
+}
+
+
+def _random_blocks(qtype, rows, cols, rng):
+    nbytes, nel, f16_at = _QBLOCKS[qtype]
+    nblk = cols // nel
+    raw = rng.integers(0, 256, (rows, nblk, nbytes), dtype=np.uint8)
+    for off in f16_at:  # finite scales
+        d = (rng.standard_normal((rows, nblk)) * 0.02).astype(np.float16)
+        raw[:, :, off:off + 2] = d.view(np.uint8).reshape(rows, nblk, 2)
+    return raw.reshape(rows, nblk * nbytes)
+
+
+@pytest.mark.parametrize("qtype", ["F16", "Q8_0", "Q5_0", "Q4_K", "Q6_K"])
+def test_gguf_tensor_dequant_matches_gguf_py(native, tmp_path, qtype):
+    """Gguf::load (gguf.rs:250-269, 329-468) on every supported quantized type: the library's host
+    dequantization equals gguf-py's, bit for bit, on random valid blocks."""
+    import gguf
+
+    rng = np.random.default_rng(7)
+    rows, cols = 6, 512
+    w = gguf.GGUFWriter(str(tmp_path / "q.gguf"), "hobbylm")
+    if qtype == "F16":
+        data = (rng.standard_normal((rows, cols)) * 0.5).astype(np.float16)
+        w.add_tensor("t", data)
+        ref = data.astype(np.float32)
+    else:
+        qt = getattr(gguf.GGMLQuantizationType, qtype)
+        data = _random_blocks(qtype, rows, cols, rng)
+        w.add_tensor("t", data, raw_dtype=qt)
+        ref = np.asarray(gguf.quants.dequantize(data, qt), dtype=np.float32).reshape(rows, cols)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    out = np.empty(rows * cols, np.float32)
+    lib = native.lib()
+    native.check(lib.hg_gguf_tensor_f32(str(tmp_path / "q.gguf").encode(), b"t", out.ctypes.data, out.size))
+    assert np.array_equal(out.view(np.uint32), ref.ravel().view(np.uint32))
+    # wrong element count and missing tensor are errors, not silent truncation
+    assert lib.hg_gguf_tensor_f32(str(tmp_path / "q.gguf").encode(), b"t", out.ctypes.data, out.size - 1) == -1
+    assert lib.hg_gguf_tensor_f32(str(tmp_path / "q.gguf").encode(), b"nope", out.ctypes.data, out.size) == -4
