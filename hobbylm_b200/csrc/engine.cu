@@ -637,16 +637,22 @@ void decode_greedy(hg_engine* e, hg_seq** seqs, int n, const uint32_t* tokens, i
 // ---------------------------------------------------------------------------------------------
 // Prefill (exact reference order), chunked
 // ---------------------------------------------------------------------------------------------
-void prefill_chunk(hg_engine* e, hg_seq* s, const uint32_t* ids, int tn) {
+// One chunk of Model::prefill (model.rs:340-439). Its inputs are token ids (embedding rows looked
+// up on the GPU) or, when embeds is given, tn caller rows of d_model floats (host memory).
+void prefill_chunk(hg_engine* e, hg_seq* s, const uint32_t* ids, const float* embeds, int tn) {
   const hg_config& c = e->cfg;
   const Dims& D = e->D;
   auto& P = e->pf;
   cudaStream_t st = e->stream;
   const int d = c.d_model, base = s->len, k = c.top_k, ne = c.n_experts, f = c.expert_ffn;
   const int32_t* bt = e->d_bt + (size_t)s->row * e->bt_stride;
-  std::vector<int32_t> h_ids(ids, ids + tn);
-  HG_CUDA(cudaMemcpyAsync(P.ids, h_ids.data(), tn * 4, cudaMemcpyHostToDevice, st));
-  launch_kp_embed(e->embd, P.ids, tn, d, c.vocab_size, P.x, e->buf.err, st);
+  if (embeds) {
+    HG_CUDA(cudaMemcpyAsync(P.x, embeds, (size_t)tn * d * 4, cudaMemcpyHostToDevice, st));
+  } else {
+    std::vector<int32_t> h_ids(ids, ids + tn);
+    HG_CUDA(cudaMemcpyAsync(P.ids, h_ids.data(), tn * 4, cudaMemcpyHostToDevice, st));
+    launch_kp_embed(e->embd, P.ids, tn, d, c.vocab_size, P.x, e->buf.err, st);
+  }
   for (int l = 0; l < c.n_layers; l++) {
     const LayerDev& Ld = e->layers[l];
     float* kb = e->kv + (long long)l * e->layer_stride;
@@ -723,16 +729,19 @@ void prefill_chunk(hg_engine* e, hg_seq* s, const uint32_t* ids, int tn) {
   s->len += tn;
 }
 
-void prefill(hg_engine* e, hg_seq* s, const uint32_t* ids, int n, float* logits, uint32_t* next) {
+// Model::prefill over n inputs: token ids, or (ids == null) n rows of d_model floats in embeds.
+void prefill(hg_engine* e, hg_seq* s, const uint32_t* ids, const float* embeds, int n, float* logits, uint32_t* next) {
   if (n <= 0) throw Error(HG_ERR_INVALID, "empty prefill");
-  for (int i = 0; i < n; i++)
-    if ((int64_t)ids[i] >= e->cfg.vocab_size) throw Error(HG_ERR_TOKEN, "token id out of range");
+  if (ids) {
+    for (int i = 0; i < n; i++)
+      if ((int64_t)ids[i] >= e->cfg.vocab_size) throw Error(HG_ERR_TOKEN, "token id out of range");
+  }
   if (s->len + n > s->max_ctx) throw Error(HG_ERR_CONTEXT, "prompt exceeds the sequence's max context");
   ensure_pages(s, s->len + n);
   int last = 0;
   for (int c0 = 0; c0 < n; c0 += e->pf_rows) {
     int tn = std::min(e->pf_rows, n - c0);
-    prefill_chunk(e, s, ids + c0, tn);
+    prefill_chunk(e, s, ids ? ids + c0 : nullptr, ids ? nullptr : embeds + (size_t)c0 * e->cfg.d_model, tn);
     last = tn;
   }
   // model.rs:365-369: exact norm of the last row, then the decode-style lm_head matvec
@@ -852,7 +861,7 @@ int generate(hg_engine* e, const uint32_t* ids, int n, const hg_gen_opts* opts, 
   std::vector<float> logits(host_path ? V : 0);
   Rng rng(o.seed);
   uint32_t gpu_next = 0;
-  prefill(e, s.get(), ids, n, host_path ? logits.data() : nullptr, &gpu_next);
+  prefill(e, s.get(), ids, nullptr, n, host_path ? logits.data() : nullptr, &gpu_next);
   int pos = n, count = 0;
   std::vector<uint32_t> out;
   for (int it = 0; it < o.max_new; it++) {
@@ -1050,7 +1059,15 @@ int hg_prefill(hg_engine* e, hg_seq* s, const uint32_t* ids, int n, float* logit
   HG_API_TRY({
     need(e && s && ids && s->e == e, "bad argument");
     DeviceGuard g(e->device);
-    prefill(e, s, ids, n, logits_or_null, nullptr);
+    prefill(e, s, ids, nullptr, n, logits_or_null, nullptr);
+  })
+}
+
+int hg_prefill_embeds(hg_engine* e, hg_seq* s, const float* embeds, int n, float* logits_or_null) {
+  HG_API_TRY({
+    need(e && s && embeds && s->e == e, "bad argument");
+    DeviceGuard g(e->device);
+    prefill(e, s, nullptr, embeds, n, logits_or_null, nullptr);
   })
 }
 

@@ -120,6 +120,16 @@ class Engine:
         check(lib().hg_prefill(self.h, cache.h, ids.ctypes.data, len(ids), out.ctypes.data))
         return out
 
+    def prefill_embeds(self, cache: KvCache, rows) -> np.ndarray:
+        """Model::prefill on caller rows (n x d_model f32, e.g. modality embeddings spliced before a
+        prompt, lib.rs:118-121); returns the last position's logits."""
+        rows = np.ascontiguousarray(rows, dtype=np.float32)
+        if rows.ndim != 2 or rows.shape[1] != self.cfg["d_model"]:
+            raise HgError(-1, f"rows must be n x {self.cfg['d_model']}")
+        out = np.empty(self.vocab, np.float32)
+        check(lib().hg_prefill_embeds(self.h, cache.h, rows.ctypes.data, rows.shape[0], out.ctypes.data))
+        return out
+
     def forward(self, cache: KvCache, token: int, pos: int | None = None, want_logits: bool = True):
         """Model::forward(token, pos, cache). pos, if given, must equal the cache length.
         Returns (logits or None, greedy next id with ids >= 50257 masked)."""

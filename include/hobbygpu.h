@@ -102,6 +102,11 @@ int hg_seq_len(const hg_seq* s);
 /* Model::prefill (model.rs:340-370) on token ids: embeds, runs all positions with the prefill
  * arithmetic, appends K/V and writes the last position's vocab logits (may be NULL). */
 int hg_prefill(hg_engine* e, hg_seq* s, const uint32_t* ids, int n, float* logits_or_null);
+/* Model::prefill (model.rs:340-370) on caller rows: n initial residual vectors of d_model floats
+ * (host memory, row-major), e.g. modality embeddings spliced before a prompt's token embeddings
+ * (lib.rs:118-121: prefill the embeddings, then the prompt ids with hg_prefill on the same
+ * sequence; chunked prefill equals one prefill over all rows). logits as for hg_prefill. */
+int hg_prefill_embeds(hg_engine* e, hg_seq* s, const float* embeds, int n, float* logits_or_null);
 
 /* Model::forward (model.rs:152-184): one decode step of `token` at position hg_seq_len(s).
  * logits_or_null receives the raw vocab logits; argmax_or_null the greedy pick with ids >= 50257

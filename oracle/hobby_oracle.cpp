@@ -1251,6 +1251,16 @@ int hor_prefill(void* ep, void* cp, const uint32_t* ids, int n, float* logits) {
   })
 }
 
+// Model::prefill (model.rs:340-370) on caller rows (n x d_model): the inputs lib.rs:118-121 builds
+// from spliced modality embeddings and token embeddings.
+int hor_prefill_embeds(void* ep, void* cp, const float* rows, int n, float* logits) {
+  HOR_TRY({
+    Engine* e = (Engine*)ep;
+    if (n <= 0) throw Error("empty prefill");
+    e->model.prefill(rows, n, *(KvCache*)cp, logits);
+  })
+}
+
 int hor_forward(void* ep, void* cp, uint32_t token, int pos, float* logits) {
   HOR_TRY({ ((Engine*)ep)->model.forward(token, pos, *(KvCache*)cp, logits); })
 }

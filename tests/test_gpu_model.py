@@ -181,6 +181,36 @@ def test_engine_freed_before_its_caches(model130):
     b.close()
 
 
+def test_prefill_embeds_splice_matches_oracle(engine130, oracle130, model130, native):
+    """Model::prefill on caller rows (model.rs:340; lib.rs:118-121 splices modality rows before the
+    prompt's token embeddings): the token-embedding rows of a prompt give its ids' logits, and three
+    spliced rows + the prompt, then greedy decode, equal the oracle bit for bit."""
+    ids = synth.prompt_ids(40, 9)
+    d, vocab = engine130.cfg["d_model"], engine130.vocab
+    emb = np.empty(vocab * d, np.float32)
+    native.check(native.lib().hg_gguf_tensor_f32(str(model130).encode(), b"token_embd.weight", emb.ctypes.data, emb.size))
+    emb = emb.reshape(vocab, d)
+    with engine130.new_cache() as a, engine130.new_cache() as b:
+        la = engine130.prefill(a, ids)
+        lb = engine130.prefill_embeds(b, emb[ids])
+        assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+    extra = (np.random.default_rng(11).standard_normal((3, d)) * 0.02).astype(np.float32)
+    oc = oracle130.new_cache()
+    ref = oracle130.prefill_embeds(oc, np.concatenate([extra, emb[ids]]))
+    with engine130.new_cache() as kv:
+        engine130.prefill_embeds(kv, extra)
+        lg = engine130.prefill(kv, ids)
+        n = kv.len
+        assert n == 3 + len(ids)
+        for i in range(8):
+            assert np.array_equal(lg.view(np.uint32), ref.view(np.uint32)), f"step {i}: rel L2 {_rel(lg, ref)}"
+            lm = lg.copy()
+            lm[50257:] = -np.inf
+            tok = int(np.argmax(lm))
+            lg, _ = engine130.forward(kv, tok)
+            ref = oracle130.forward(oc, tok, n + i)
+
+
 def test_errors(engine130, model130):
     from hobbylm_b200 import Engine
 
