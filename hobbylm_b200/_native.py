@@ -19,7 +19,7 @@ ERRORS = {
 
 # every symbol include/hobbygpu.h declares
 EXPORTS = (
-    "hg_last_error", "hg_engine_load", "hg_engine_load_ex", "hg_engine_free", "hg_engine_config", "hg_gguf_config", "hg_gguf_tensor_f32", "hg_prefill_embeds",
+    "hg_last_error", "hg_engine_load", "hg_engine_load_ex", "hg_engine_free", "hg_engine_config", "hg_gguf_config", "hg_gguf_tensor_f32", "hg_prefill_embeds", "hg_forward_x",
     "hg_engine_weight_bytes", "hg_engine_eos", "hg_engine_device_bytes", "hg_seq_create", "hg_seq_free",
     "hg_seq_len", "hg_prefill", "hg_forward", "hg_decode_batch", "hg_generate", "hg_debug_last_routing",
     "hg_q8_pack", "hg_q8_scale_stride", "hg_q8_unpack_qs", "hg_op_q8_matvec", "hg_op_q8_matmul",
@@ -103,6 +103,7 @@ def lib():
         "hg_prefill": (i32, [vp, vp, vp, i32, vp]),
         "hg_prefill_embeds": (i32, [vp, vp, vp, i32, vp]),
         "hg_forward": (i32, [vp, vp, u32, vp, vp]),
+        "hg_forward_x": (i32, [vp, vp, vp, vp, vp]),
         "hg_decode_batch": (i32, [vp, vp, i32, vp, vp, vp]),
         "hg_generate": (i32, [vp, vp, i32, C.POINTER(GenOptsC), TOKEN_CB, vp, vp]),
         "hg_debug_last_routing": (i32, [vp, i32, vp]),

@@ -88,11 +88,16 @@ __global__ void __launch_bounds__(PRE_NORM_THREADS) k_pre_norm(Dims D, DecodeBuf
   pdl_trigger();
   if (mode == 0) {
     int tok = B.tok[t];
-    if (tok < 0 || tok >= D.vocab) {
-      if (threadIdx.x == 0) atomicExch(B.err, HG_ERR_TOKEN);
-      tok = 0;
+    const float* e;
+    if (tok == -1 && B.xin) {  // Model::forward_x (model.rs:160): the caller's row instead of an embedding
+      e = B.xin + (size_t)t * d;
+    } else {
+      if (tok < 0 || tok >= D.vocab) {
+        if (threadIdx.x == 0) atomicExch(B.err, HG_ERR_TOKEN);
+        tok = 0;
+      }
+      e = embd + (size_t)tok * d;
     }
-    const float* e = embd + (size_t)tok * d;
     for (int i = threadIdx.x; i < d; i += blockDim.x) xs[i] = e[i];
   } else if (mode == 1) {
     const float* y = B.y + (size_t)t * (D.k + 1) * d;

@@ -213,6 +213,7 @@ void alloc_work(hg_engine* e) {
   B.bt = e->d_bt;
   B.bt_stride = e->bt_stride;
   B.x = a.take<float>((size_t)T * d);
+  B.xin = a.take<float>((size_t)T * d);
   B.qa = a.take<int8_t>((size_t)T * d);
   B.sa = a.take<float>((size_t)T * ss_d);
   B.qkv = a.take<float>((size_t)T * qkvd);
@@ -561,6 +562,24 @@ void seq_check_step(hg_seq* s, uint32_t token) {
 void forward(hg_engine* e, hg_seq* s, uint32_t token, float* logits, uint32_t* next) {
   seq_check_step(s, token);
   e->h_meta[0] = (int32_t)token;
+  e->h_meta[1] = s->len;
+  e->h_meta[2] = s->row;
+  decode_step(e, 1);
+  if (logits)
+    HG_CUDA(cudaMemcpyAsync(logits, e->buf.logits, (size_t)e->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, e->stream));
+  finish_step(e);
+  s->len += 1;
+  if (next) *next = amax_index(e->h_amax[0]);
+}
+
+// Model::forward_x (model.rs:160-184): one decode step from a caller row (d_model floats, host)
+// instead of a token embedding; the step graph reads token -1 as "take row t of xin".
+void forward_x(hg_engine* e, hg_seq* s, const float* row, float* logits, uint32_t* next) {
+  if (s->len >= s->max_ctx) throw Error(HG_ERR_CONTEXT, "sequence is at its max context");
+  ensure_pages(s, s->len + 1);
+  HG_CUDA(cudaMemcpyAsync(const_cast<float*>(e->buf.xin), row, (size_t)e->cfg.d_model * 4, cudaMemcpyHostToDevice,
+                          e->stream));
+  e->h_meta[0] = -1;
   e->h_meta[1] = s->len;
   e->h_meta[2] = s->row;
   decode_step(e, 1);
@@ -1076,6 +1095,14 @@ int hg_forward(hg_engine* e, hg_seq* s, uint32_t token, float* logits_or_null, u
     need(e && s && s->e == e, "bad argument");
     DeviceGuard g(e->device);
     forward(e, s, token, logits_or_null, argmax_or_null);
+  })
+}
+
+int hg_forward_x(hg_engine* e, hg_seq* s, const float* row, float* logits_or_null, uint32_t* argmax_or_null) {
+  HG_API_TRY({
+    need(e && s && row && s->e == e, "bad argument");
+    DeviceGuard g(e->device);
+    forward_x(e, s, row, logits_or_null, argmax_or_null);
   })
 }
 

@@ -55,6 +55,7 @@ struct DecodeBufs {
   const int32_t* bt_row;   // [T] row of each token's sequence in bt
   int bt_stride;
   float* x;                // [T][d] residual stream
+  const float* xin;        // [T][d] caller rows: a token given as -1 starts from its row (forward_x)
   int8_t* qa;              // [T][d] quantized normed activations (attention / lm_head input)
   float* sa;               // [T][ss(d)]
   float* qkv;              // [T][qkvd]

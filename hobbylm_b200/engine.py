@@ -130,6 +130,18 @@ class Engine:
         check(lib().hg_prefill_embeds(self.h, cache.h, rows.ctypes.data, rows.shape[0], out.ctypes.data))
         return out
 
+    def forward_x(self, cache: KvCache, row, want_logits: bool = True):
+        """Model::forward_x (model.rs:160): one decode step from a d_model-float row instead of a
+        token embedding. Returns (logits or None, greedy next id with ids >= 50257 masked)."""
+        row = np.ascontiguousarray(row, dtype=np.float32)
+        if row.shape != (self.cfg["d_model"],):
+            raise HgError(-1, f"row must have {self.cfg['d_model']} floats")
+        out = np.empty(self.vocab, np.float32) if want_logits else None
+        nxt = C.c_uint32()
+        check(lib().hg_forward_x(self.h, cache.h, row.ctypes.data, out.ctypes.data if want_logits else None,
+                                 C.byref(nxt)))
+        return out, int(nxt.value)
+
     def forward(self, cache: KvCache, token: int, pos: int | None = None, want_logits: bool = True):
         """Model::forward(token, pos, cache). pos, if given, must equal the cache length.
         Returns (logits or None, greedy next id with ids >= 50257 masked)."""

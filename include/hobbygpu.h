@@ -112,6 +112,10 @@ int hg_prefill_embeds(hg_engine* e, hg_seq* s, const float* embeds, int n, float
  * logits_or_null receives the raw vocab logits; argmax_or_null the greedy pick with ids >= 50257
  * masked (lib.rs:127-134, sample.rs:53-64). */
 int hg_forward(hg_engine* e, hg_seq* s, uint32_t token, float* logits_or_null, uint32_t* argmax_or_null);
+/* Model::forward_x (model.rs:160-184): one decode step from a caller row of d_model floats (host
+ * memory) in place of a token embedding, e.g. a modality vector fed during decode. logits and
+ * argmax as for hg_forward. */
+int hg_forward_x(hg_engine* e, hg_seq* s, const float* row, float* logits_or_null, uint32_t* argmax_or_null);
 
 /* One batched decode step: seqs[i] consumes tokens[i]; next_ids[i] gets its greedy pick.
  * Per sequence the result equals hg_forward. n <= max_batch. */

@@ -67,6 +67,7 @@ def lib():
         "hor_cache_fill": (i, [vp, vp, f32p, f32p, i]),
         "hor_prefill": (i, [vp, vp, u32p, i, f32p]),
         "hor_prefill_embeds": (i, [vp, vp, f32p, i, f32p]),
+        "hor_forward_x": (i, [vp, vp, f32p, i, f32p]),
         "hor_forward": (i, [vp, vp, C.c_uint32, i, f32p]),
         "hor_last_routing": (i, [vp, i32p, f32p]),
         "hor_generate": (i, [vp, u32p, i, i, f, f, C.c_uint64, f, u32p, vp, C.POINTER(i), C.POINTER(d),
@@ -165,6 +166,12 @@ class Engine:
         rows = np.ascontiguousarray(rows, dtype=np.float32)
         out = np.zeros(self.vocab, np.float32)
         _check(lib().hor_prefill_embeds(self.h, cache.h, rows, rows.shape[0], out))
+        return out
+
+    def forward_x(self, cache: "Cache", row, pos: int) -> np.ndarray:
+        row = np.ascontiguousarray(row, dtype=np.float32)
+        out = np.zeros(self.vocab, np.float32)
+        _check(lib().hor_forward_x(self.h, cache.h, row, int(pos), out))
         return out
 
     def forward(self, cache: "Cache", token: int, pos: int) -> np.ndarray:

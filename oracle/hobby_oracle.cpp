@@ -1261,6 +1261,14 @@ int hor_prefill_embeds(void* ep, void* cp, const float* rows, int n, float* logi
   })
 }
 
+// Model::forward_x (model.rs:160-184) from a caller row of d_model floats.
+int hor_forward_x(void* ep, void* cp, const float* row, int pos, float* logits) {
+  HOR_TRY({
+    Engine* e = (Engine*)ep;
+    e->model.forward_x(std::vector<float>(row, row + e->cfg.d_model), pos, *(KvCache*)cp, logits);
+  })
+}
+
 int hor_forward(void* ep, void* cp, uint32_t token, int pos, float* logits) {
   HOR_TRY({ ((Engine*)ep)->model.forward(token, pos, *(KvCache*)cp, logits); })
 }

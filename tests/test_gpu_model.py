@@ -211,6 +211,37 @@ def test_prefill_embeds_splice_matches_oracle(engine130, oracle130, model130, na
             ref = oracle130.forward(oc, tok, n + i)
 
 
+def test_forward_x_matches_forward_and_oracle(engine130, oracle130, model130, native):
+    """Model::forward_x (model.rs:160): a decode step from a token's own embedding row equals the step
+    from its id, and steps from arbitrary rows between token steps equal the oracle bit for bit."""
+    ids = synth.prompt_ids(30, 13)
+    d, vocab = engine130.cfg["d_model"], engine130.vocab
+    emb = np.empty(vocab * d, np.float32)
+    native.check(native.lib().hg_gguf_tensor_f32(str(model130).encode(), b"token_embd.weight", emb.ctypes.data, emb.size))
+    emb = emb.reshape(vocab, d)
+    rows = (np.random.default_rng(17).standard_normal((2, d)) * 0.02).astype(np.float32)
+    oc = oracle130.new_cache()
+    oracle130.prefill(oc, ids)
+    with engine130.new_cache() as a, engine130.new_cache() as b:
+        engine130.prefill(a, ids)
+        engine130.prefill(b, ids)
+        la, na = engine130.forward(a, 1234)
+        lb, nb = engine130.forward_x(b, emb[1234])
+        assert na == nb and np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+        ref = oracle130.forward(oc, 1234, len(ids))
+        assert np.array_equal(lb.view(np.uint32), ref.view(np.uint32))
+        pos, tok = len(ids) + 1, nb
+        for step in range(6):
+            if step in (1, 4):
+                lg, nxt = engine130.forward_x(b, rows[0 if step == 1 else 1])
+                ref = oracle130.forward_x(oc, rows[0 if step == 1 else 1], pos)
+            else:
+                lg, nxt = engine130.forward(b, tok)
+                ref = oracle130.forward(oc, tok, pos)
+            assert np.array_equal(lg.view(np.uint32), ref.view(np.uint32)), f"step {step}: rel L2 {_rel(lg, ref)}"
+            pos, tok = pos + 1, nxt
+
+
 def test_errors(engine130, model130):
     from hobbylm_b200 import Engine
 
