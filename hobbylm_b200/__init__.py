@@ -7,5 +7,5 @@
 The compute runs in libhobbygpu.so (hand-written CUDA for sm_100a behind the C ABI in
 include/hobbygpu.h); this package is the host-side mirror of hobby-rs's Engine / KvCache API.
 """
-from .engine import GPT2_VALID, Engine, GenOpts, KvCache  # noqa: F401
+from .engine import GPT2_VALID, DiffOpts, Engine, GenOpts, KvCache  # noqa: F401
 from ._native import HgError  # noqa: F401

@@ -19,7 +19,8 @@ ERRORS = {
 
 # every symbol include/hobbygpu.h declares
 EXPORTS = (
-    "hg_last_error", "hg_engine_load", "hg_engine_load_ex", "hg_engine_free", "hg_engine_config", "hg_gguf_config", "hg_gguf_tensor_f32", "hg_prefill_embeds", "hg_forward_x",
+    "hg_last_error", "hg_engine_load", "hg_engine_load_ex", "hg_engine_free", "hg_engine_config", "hg_gguf_config",
+    "hg_gguf_tensor_f32", "hg_prefill_embeds", "hg_forward_x", "hg_run_block", "hg_generate_diffusion",
     "hg_engine_weight_bytes", "hg_engine_eos", "hg_engine_device_bytes", "hg_seq_create", "hg_seq_free",
     "hg_seq_len", "hg_prefill", "hg_forward", "hg_decode_batch", "hg_generate", "hg_debug_last_routing",
     "hg_q8_pack", "hg_q8_scale_stride", "hg_q8_unpack_qs", "hg_op_q8_matvec", "hg_op_q8_matmul",
@@ -41,7 +42,8 @@ class Config(C.Structure):
         "d_model", "n_layers", "n_dense", "n_heads", "n_kv_heads", "head_dim", "dense_ffn", "expert_ffn",
         "n_experts", "top_k", "n_shared", "vocab_size", "context_length", "expert_weights_norm",
         "gating_sigmoid", "eos_token")] + [("rms_eps", C.c_float), ("rope_theta", C.c_float),
-                                           ("expert_weights_scale", C.c_float)]
+                                           ("expert_weights_scale", C.c_float)] + [
+        (n, C.c_int32) for n in ("diffusion", "mask_token_id", "block_size")]
 
     def as_dict(self) -> dict:
         return {n: getattr(self, n) for n, _ in self._fields_}
@@ -55,6 +57,12 @@ class EngineOpts(C.Structure):
 class GenOptsC(C.Structure):
     _fields_ = [("max_new", C.c_int32), ("temp", C.c_float), ("top_p", C.c_float), ("seed", C.c_uint64),
                 ("rep_penalty", C.c_float)]
+
+
+class DiffOptsC(C.Structure):
+    _fields_ = [("gen_len", C.c_int32), ("block", C.c_int32), ("steps", C.c_int32), ("temp", C.c_float),
+                ("rep_penalty", C.c_float), ("remask_steps", C.c_int32), ("remask_frac", C.c_float),
+                ("seed", C.c_uint64), ("cached", C.c_int32), ("threshold", C.c_float)]
 
 
 class MoeWeights(C.Structure):
@@ -73,6 +81,7 @@ class KvAttnArgs(C.Structure):
 
 
 TOKEN_CB = C.CFUNCTYPE(C.c_int, C.c_uint32, C.c_void_p)
+BLOCK_CB = C.CFUNCTYPE(C.c_int, C.POINTER(C.c_uint32), C.c_int, C.c_void_p)
 
 _lib = None
 
@@ -106,6 +115,8 @@ def lib():
         "hg_forward_x": (i32, [vp, vp, vp, vp, vp]),
         "hg_decode_batch": (i32, [vp, vp, i32, vp, vp, vp]),
         "hg_generate": (i32, [vp, vp, i32, C.POINTER(GenOptsC), TOKEN_CB, vp, vp]),
+        "hg_run_block": (i32, [vp, vp, vp, i32, i32, i32, vp]),
+        "hg_generate_diffusion": (i32, [vp, vp, i32, C.POINTER(DiffOptsC), BLOCK_CB, vp, vp]),
         "hg_debug_last_routing": (i32, [vp, i32, vp]),
         "hg_q8_pack": (i32, [vp, i64, i64, vp, vp]),
         "hg_q8_scale_stride": (i32, [i64]),

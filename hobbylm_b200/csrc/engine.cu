@@ -107,6 +107,8 @@ struct hg_engine {
     int32_t *ids, *sel, *ecount, *elist, *a_idx, *o_idx, *gm, *go, *gc;
   } pf{};
   int pf_tq = 1024;
+  float* blk_logits = nullptr;  // [blk_logits_rows][vocab] logits of diffusion block rows
+  int blk_logits_rows = 0;
   std::vector<int32_t> last_sel;  // [n_layers][max_batch][k] from the last decode step
   int last_T = 0;
   size_t device_bytes() const { return weights.cap + work.cap; }
@@ -403,6 +405,7 @@ void free_engine(hg_engine* e) {
   e->work.release();
   if (e->kv) cudaFree(e->kv);
   if (e->d_bt) cudaFree(e->d_bt);
+  if (e->blk_logits) cudaFree(e->blk_logits);
   if (e->h_meta) cudaFreeHost(e->h_meta);
   if (e->h_amax) cudaFreeHost(e->h_amax);
   if (e->h_err) cudaFreeHost(e->h_err);
@@ -658,7 +661,9 @@ void decode_greedy(hg_engine* e, hg_seq** seqs, int n, const uint32_t* tokens, i
 // ---------------------------------------------------------------------------------------------
 // One chunk of Model::prefill (model.rs:340-439). Its inputs are token ids (embedding rows looked
 // up on the GPU) or, when embeds is given, tn caller rows of d_model floats (host memory).
-void prefill_chunk(hg_engine* e, hg_seq* s, const uint32_t* ids, const float* embeds, int tn) {
+// bidir: the rows form one diffusion block (Model::run_block, model.rs:472-587): each attends to
+// the prefix and to all tn rows, and the sequence length is left unchanged.
+void prefill_chunk(hg_engine* e, hg_seq* s, const uint32_t* ids, const float* embeds, int tn, bool bidir) {
   const hg_config& c = e->cfg;
   const Dims& D = e->D;
   auto& P = e->pf;
@@ -682,7 +687,8 @@ void prefill_chunk(hg_engine* e, hg_seq* s, const uint32_t* ids, const float* em
                              e->rope_cos, e->rope_sin, bt, kb, vb, e->page_stride, P.q, st);
     for (int t0 = 0; t0 < tn; t0 += e->pf_tq) {
       int tq = std::min(e->pf_tq, tn - t0);
-      launch_kp_attention(P.q, D.qd, t0, tq, base, c.n_heads, c.n_kv_heads, c.head_dim, bt, kb, vb, e->page_stride,
+      launch_kp_attention(P.q, D.qd, t0, tq, base, bidir ? base + tn : 0, c.n_heads, c.n_kv_heads, c.head_dim, bt, kb,
+                          vb, e->page_stride,
                           P.S, P.inv, P.o, st);
     }
     launch_kp_quant_rows(P.o, tn, D.qd, P.qa, P.sa, st);
@@ -745,7 +751,7 @@ void prefill_chunk(hg_engine* e, hg_seq* s, const uint32_t* ids, const float* em
     }
     launch_kp_combine(P.x, P.y, P.sel, P.selw, tn, d, k, 1, c.n_shared, st);
   }
-  s->len += tn;
+  if (!bidir) s->len += tn;
 }
 
 // Model::prefill over n inputs: token ids, or (ids == null) n rows of d_model floats in embeds.
@@ -760,7 +766,7 @@ void prefill(hg_engine* e, hg_seq* s, const uint32_t* ids, const float* embeds, 
   int last = 0;
   for (int c0 = 0; c0 < n; c0 += e->pf_rows) {
     int tn = std::min(e->pf_rows, n - c0);
-    prefill_chunk(e, s, ids ? ids + c0 : nullptr, ids ? nullptr : embeds + (size_t)c0 * e->cfg.d_model, tn);
+    prefill_chunk(e, s, ids ? ids + c0 : nullptr, ids ? nullptr : embeds + (size_t)c0 * e->cfg.d_model, tn, false);
     last = tn;
   }
   // model.rs:365-369: exact norm of the last row, then the decode-style lm_head matvec
@@ -778,6 +784,43 @@ void prefill(hg_engine* e, hg_seq* s, const uint32_t* ids, const float* embeds, 
   if (logits) HG_CUDA(cudaMemcpyAsync(logits, B.logits, (size_t)D.vocab * 4, cudaMemcpyDeviceToHost, st));
   finish_step(e);
   if (next) *next = amax_index(e->h_amax[0]);
+}
+
+// Model::run_block (model.rs:472-510) of n token ids at positions len..len+n: each row attends to
+// the sequence's prefix and to every row of the block, with the prefill arithmetic. The block's
+// K/V rows go to its pages past len; commit makes them part of the prefix (lib.rs:386-391),
+// otherwise the next call at the same position overwrites them. logits (host, may be null):
+// [n_logits][vocab] of the last n_logits rows through output.matmul (model.rs:505-508).
+void run_block(hg_engine* e, hg_seq* s, const uint32_t* ids, int n, int n_logits, bool commit, float* logits) {
+  const hg_config& c = e->cfg;
+  if (n <= 0 || n > e->pf_rows) throw Error(HG_ERR_INVALID, "block rows out of range (1..1024 per bidirectional pass)");
+  if (n_logits < 0 || n_logits > n) throw Error(HG_ERR_INVALID, "n_logits out of range");
+  for (int i = 0; i < n; i++)
+    if ((int64_t)ids[i] >= c.vocab_size) throw Error(HG_ERR_TOKEN, "token id out of range");
+  if (s->len + n > s->max_ctx) throw Error(HG_ERR_CONTEXT, "block exceeds the sequence's max context");
+  ensure_pages(s, s->len + n);
+  prefill_chunk(e, s, ids, nullptr, n, true);
+  cudaStream_t st = e->stream;
+  if (n_logits > 0) {
+    const Dims& D = e->D;
+    auto& P = e->pf;
+    if (e->blk_logits_rows < n_logits) {
+      HG_CUDA(cudaStreamSynchronize(st));
+      if (e->blk_logits) HG_CUDA(cudaFree(e->blk_logits));
+      e->blk_logits = nullptr;
+      e->blk_logits_rows = 0;
+      HG_CUDA(cudaMalloc(&e->blk_logits, (size_t)n_logits * D.vocab * 4));
+      e->blk_logits_rows = n_logits;
+    }
+    const int r0 = n - n_logits;
+    launch_kp_norm(P.x + (size_t)r0 * D.d, nullptr, n_logits, D.d, e->out_norm, c.rms_eps, nullptr, P.qa, P.sa, st);
+    launch_kp_matmul(mm_args(e->lm, P.qa, P.sa, n_logits, e->blk_logits, D.vocab, 0), n_logits, 1, st);
+    if (logits)
+      HG_CUDA(cudaMemcpyAsync(logits, e->blk_logits, (size_t)n_logits * D.vocab * 4, cudaMemcpyDeviceToHost, st));
+  }
+  HG_CUDA(cudaMemcpyAsync(e->h_err, e->buf.err, 4, cudaMemcpyDeviceToHost, st));
+  finish_step(e);
+  if (commit) s->len += n;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -906,6 +949,236 @@ int generate(hg_engine* e, const uint32_t* ids, int n, const hg_gen_opts* opts, 
     pos += 1;
   }
   return count;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Diffusion decode (lib.rs:164-495): blocks of [MASK] ids filled over denoising passes of
+// run_block on the GPU; each pass's block logits are scored on the host.
+// ---------------------------------------------------------------------------------------------
+float log_pinned(float x) { return (float)std::log((double)x); }
+
+// sample.rs:29-47: Gumbel-max over the finite logits; temp <= 0 is the plain argmax.
+uint32_t gumbel_argmax(const float* l, int n, float temp, Rng& rng) {
+  if (temp <= 0.0f) return host_argmax(l, n);
+  int best = 0;
+  float bv = -INFINITY;
+  for (int i = 0; i < n; i++) {
+    if (!std::isfinite(l[i])) continue;
+    float u = std::clamp(rng.next_f32(), 1e-9f, 1.0f - 1e-9f);
+    float val = l[i] / temp + -log_pinned(-log_pinned(u));
+    if (val > bv) {
+      bv = val;
+      best = i;
+    }
+  }
+  return (uint32_t)best;
+}
+
+// lib.rs:66-73: n unmask events spread over `steps` (sums to n).
+std::vector<int> num_transfer(int n, int steps) {
+  const int base = n / steps;
+  std::vector<int> out(steps, base);
+  for (int i = 0; i < n - base * steps; i++) out[i] += 1;
+  return out;
+}
+
+// lib.rs:221-263 (score_block): per block row, ids >= valid banned, the presence penalty over the
+// committed ids and the block's own non-mask ids, a Gumbel / greedy pick, and the softmax
+// probabilities (ops.rs:112-128) of the pick (pconf) and of the row's current id (cconf). Rows are
+// independent except for the Gumbel draws, which take one RNG stream row after row.
+void score_block(const float* all, int V, const uint32_t* blk, int blk_len, const uint32_t* committed,
+                 int n_committed, int valid, uint32_t mask, float rep_penalty, float temp, Rng& rng, uint32_t* pred,
+                 float* pconf, float* cconf, std::vector<float>& rows) {
+  std::vector<char> present(valid, 0);
+  if (rep_penalty != 1.0f)
+    for (int i = 0; i < n_committed + blk_len; i++) {
+      uint32_t id = i < n_committed ? committed[i] : blk[i - n_committed];
+      if (id != mask && (int64_t)id < valid) present[id] = 1;
+    }
+  rows.resize((size_t)blk_len * V);
+#pragma omp parallel for schedule(static)
+  for (int i = 0; i < blk_len; i++) {
+    float* row = rows.data() + (size_t)i * V;
+    memcpy(row, all + (size_t)i * V, (size_t)V * 4);
+    for (int l = valid; l < V; l++) row[l] = -INFINITY;
+    if (rep_penalty != 1.0f)
+      for (int t = 0; t < valid; t++)
+        if (present[t]) {
+          float l = row[t];
+          row[t] = l > 0.0f ? l / rep_penalty : l * rep_penalty;
+        }
+    if (temp <= 0.0f) pred[i] = host_argmax(row, V);
+  }
+  if (temp > 0.0f)
+    for (int i = 0; i < blk_len; i++) pred[i] = gumbel_argmax(rows.data() + (size_t)i * V, V, temp, rng);
+#pragma omp parallel for schedule(static)
+  for (int i = 0; i < blk_len; i++) {
+    const float* row = rows.data() + (size_t)i * V;
+    float m = -INFINITY;
+    for (int k = 0; k < V; k++)
+      if (row[k] > m) m = row[k];
+    float sum = 0.0f;
+    for (int k = 0; k < V; k++) sum += exp_pinned(row[k] - m);
+    const float inv = 1.0f / sum;
+    pconf[i] = exp_pinned(row[pred[i]] - m) * inv;
+    cconf[i] = exp_pinned(row[blk[i]] - m) * inv;
+  }
+}
+
+// The unmasking passes shared by both paths for one block (lib.rs:304-384 / 425-471): `ids` are
+// the block's current ids, `step` runs one scored pass over them.
+template <class Step>
+void fill_block(uint32_t* ids, int blk_len, int gen_len, uint32_t mask, const hg_diff_opts& o, bool threshold_mode,
+                const uint32_t* pred, const float* pconf, const float* cconf, Step step) {
+  auto any_masked = [&]() { return std::find(ids, ids + blk_len, mask) != ids + blk_len; };
+  if (threshold_mode) {
+    // Fast-dLLM confidence threshold (lib.rs:304-327): commit every masked row at or above it,
+    // or else the most confident one (Iterator::max_by keeps the last of equal maxima).
+    for (int it = 0; it < std::max(blk_len, 1); it++) {
+      if (!any_masked()) break;
+      step();
+      int best = -1;
+      for (int i = 0; i < blk_len; i++)
+        if (ids[i] == mask && (best < 0 || !(pconf[i] < pconf[best]))) best = i;
+      bool any = false;
+      for (int i = 0; i < blk_len; i++)
+        if (ids[i] == mask && pconf[i] >= o.threshold) {
+          ids[i] = pred[i];
+          any = true;
+        }
+      if (!any) ids[best] = pred[best];
+    }
+  } else {
+    // fixed num_transfer schedule (lib.rs:328-354): the k most confident masked rows per pass
+    const int sb = std::max((int)std::round((float)(o.steps * blk_len) / (float)gen_len), 1);
+    for (int k_step : num_transfer(blk_len, sb)) {
+      step();
+      std::vector<std::pair<int, float>> cand;
+      for (int i = 0; i < blk_len; i++)
+        if (ids[i] == mask) cand.push_back({i, pconf[i]});
+      if (cand.empty()) break;
+      std::stable_sort(cand.begin(), cand.end(), [](const auto& a, const auto& b) { return a.second > b.second; });
+      for (int r = 0; r < std::min(k_step, (int)cand.size()); r++) ids[cand[r].first] = pred[cand[r].first];
+    }
+    if (any_masked()) {
+      step();
+      for (int i = 0; i < blk_len; i++)
+        if (ids[i] == mask) ids[i] = pred[i];
+    }
+  }
+  // low-confidence remasking (lib.rs:356-375)
+  for (int it = 0; it < o.remask_steps; it++) {
+    step();
+    const int r = std::max((int)((float)blk_len * o.remask_frac), 1);
+    std::vector<std::pair<int, float>> idx(blk_len);
+    for (int i = 0; i < blk_len; i++) idx[i] = {i, cconf[i]};
+    std::stable_sort(idx.begin(), idx.end(), [](const auto& a, const auto& b) { return a.second < b.second; });
+    for (int q = 0; q < std::min(r, blk_len); q++) ids[idx[q].first] = mask;
+    step();
+    for (int i = 0; i < blk_len; i++)
+      if (ids[i] == mask) ids[i] = pred[i];
+  }
+}
+
+// Streams the generated ids up to the first eos (lib.rs:393-405 / 473-491, one call per block);
+// returns false to stop, with *count set to the generated length.
+bool stream_block(const std::vector<uint32_t>& ids, int p, int upto, uint32_t eos, int& emitted, hg_block_cb cb,
+                  void* user, uint32_t* out_ids, int* count) {
+  int endpos = upto;
+  bool hit = false;
+  for (int i = p; i < upto; i++)
+    if (ids[i] == eos) {
+      endpos = i;
+      hit = true;
+      break;
+    }
+  const int n_new = endpos - p - emitted;
+  if (out_ids && n_new > 0) std::copy(ids.begin() + p + emitted, ids.begin() + endpos, out_ids + emitted);
+  const int cont = cb ? cb(ids.data() + p + emitted, n_new, user) : 1;
+  emitted = endpos - p;
+  *count = endpos - p;
+  return !(hit || !cont);
+}
+
+// lib.rs:265-407 (generate_diffusion_cached): the prompt is encoded bidirectionally into the
+// sequence, then each block's passes run only the block against that frozen prefix.
+int diffusion_cached(hg_engine* e, const uint32_t* prompt, int p, const hg_diff_opts& o, hg_block_cb cb, void* user,
+                     uint32_t* out_ids) {
+  const hg_config& c = e->cfg;
+  const int V = c.vocab_size, valid = std::min(50257, V);
+  const uint32_t mask = (uint32_t)c.mask_token_id;
+  Rng rng(o.seed);
+  if (p == 0) return 0;
+  const int gen_len = std::min(o.gen_len, std::max(c.context_length - (p + o.block), 1));
+  std::unique_ptr<hg_seq, void (*)(hg_seq*)> s(seq_create(e, c.context_length), seq_free);
+  run_block(e, s.get(), prompt, p, 0, true, nullptr);
+  std::vector<uint32_t> committed(prompt, prompt + p);
+  std::vector<float> all, rows;
+  int emitted = 0, count = 0;
+  for (int b0 = p; b0 < p + gen_len;) {
+    const int b1 = std::min(b0 + o.block, p + gen_len), blk_len = b1 - b0;
+    std::vector<uint32_t> blk(blk_len, mask), pred(blk_len);
+    std::vector<float> pconf(blk_len), cconf(blk_len);
+    all.resize((size_t)blk_len * V);
+    auto step = [&]() {
+      run_block(e, s.get(), blk.data(), blk_len, blk_len, false, all.data());
+      score_block(all.data(), V, blk.data(), blk_len, committed.data(), (int)committed.size(), valid, mask,
+                  o.rep_penalty, o.temp, rng, pred.data(), pconf.data(), cconf.data(), rows);
+    };
+    fill_block(blk.data(), blk_len, gen_len, mask, o, o.threshold > 0.0f, pred.data(), pconf.data(), cconf.data(),
+               step);
+    run_block(e, s.get(), blk.data(), blk_len, 0, true, nullptr);  // finalize: the block joins the prefix
+    committed.insert(committed.end(), blk.begin(), blk.end());
+    if (!stream_block(committed, p, (int)committed.size(), (uint32_t)c.eos_token, emitted, cb, user, out_ids, &count))
+      return count;
+    b0 = b1;
+  }
+  return gen_len;
+}
+
+// lib.rs:409-495 (generate_diffusion_uncached): every pass re-runs the canvas x[0..b1] as one
+// bidirectional block from position 0 (Model::forward_bidir, model.rs:441-470, is run_block on an
+// empty prefix) and scores the active block's rows (diffusion_block, lib.rs:164-209).
+int diffusion_uncached(hg_engine* e, const uint32_t* prompt, int p, const hg_diff_opts& o, hg_block_cb cb,
+                       void* user, uint32_t* out_ids) {
+  const hg_config& c = e->cfg;
+  const int V = c.vocab_size, valid = std::min(50257, V);
+  const uint32_t mask = (uint32_t)c.mask_token_id;
+  Rng rng(o.seed);
+  const int gen_len = std::min(o.gen_len, std::max(c.context_length - p, 1));
+  std::vector<uint32_t> x(prompt, prompt + p);
+  x.resize((size_t)p + std::max(gen_len, 0), mask);
+  std::unique_ptr<hg_seq, void (*)(hg_seq*)> s(seq_create(e, c.context_length), seq_free);
+  std::vector<float> all, rows;
+  int emitted = 0, count = 0;
+  for (int b0 = p; b0 < p + gen_len;) {
+    const int b1 = std::min(b0 + o.block, p + gen_len), blk_len = b1 - b0;
+    std::vector<uint32_t> pred(blk_len);
+    std::vector<float> pconf(blk_len), cconf(blk_len);
+    all.resize((size_t)blk_len * V);
+    auto step = [&]() {
+      run_block(e, s.get(), x.data(), b1, blk_len, false, all.data());
+      score_block(all.data(), V, x.data() + b0, blk_len, x.data(), b0, valid, mask, o.rep_penalty, o.temp, rng,
+                  pred.data(), pconf.data(), cconf.data(), rows);
+    };
+    fill_block(x.data() + b0, blk_len, gen_len, mask, o, false, pred.data(), pconf.data(), cconf.data(), step);
+    if (!stream_block(x, p, b1, (uint32_t)c.eos_token, emitted, cb, user, out_ids, &count)) return count;
+    b0 = b1;
+  }
+  return gen_len;
+}
+
+// Engine::generate_diffusion (lib.rs:211-220).
+int generate_diffusion(hg_engine* e, const uint32_t* ids, int n, const hg_diff_opts* opts, hg_block_cb cb, void* user,
+                       uint32_t* out_ids) {
+  hg_diff_opts o = opts ? *opts : hg_diff_opts{128, 32, 32, 0.0f, 1.4f, 0, 0.3f, 1234, 1, 0.0f};
+  if (o.block <= 0) o.block = std::max(e->cfg.block_size, 1);
+  if (n < 0 || o.gen_len < 0) throw Error(HG_ERR_INVALID, "negative prompt or generation length");
+  for (int i = 0; i < n; i++)
+    if ((int64_t)ids[i] >= e->cfg.vocab_size) throw Error(HG_ERR_TOKEN, "token id out of range");
+  if ((int64_t)e->cfg.mask_token_id >= e->cfg.vocab_size) throw Error(HG_ERR_TOKEN, "mask token id out of range");
+  return o.cached ? diffusion_cached(e, ids, n, o, cb, user, out_ids)
+                  : diffusion_uncached(e, ids, n, o, cb, user, out_ids);
 }
 
 }  // namespace
@@ -1121,6 +1394,30 @@ int hg_generate(hg_engine* e, const uint32_t* ids, int n, const hg_gen_opts* opt
     need(e && (ids || n == 0), "null argument");
     DeviceGuard g(e->device);
     return generate(e, ids, n, opts, cb, user, out_ids);
+  } catch (const ::hg::Error& ex) {
+    set_last_error(ex.what());
+    return ex.code;
+  } catch (const std::exception& ex) {
+    set_last_error(ex.what());
+    return HG_ERR_INVALID;
+  }
+}
+
+int hg_run_block(hg_engine* e, hg_seq* s, const uint32_t* ids, int n, int n_logits, int commit,
+                 float* logits_or_null) {
+  HG_API_TRY({
+    need(e && s && ids && s->e == e, "bad argument");
+    DeviceGuard g(e->device);
+    run_block(e, s, ids, n, n_logits, commit != 0, logits_or_null);
+  })
+}
+
+int hg_generate_diffusion(hg_engine* e, const uint32_t* ids, int n, const hg_diff_opts* opts, hg_block_cb cb,
+                          void* user, uint32_t* out_ids) {
+  try {
+    need(e && (ids || n == 0), "null argument");
+    DeviceGuard g(e->device);
+    return generate_diffusion(e, ids, n, opts, cb, user, out_ids);
   } catch (const ::hg::Error& ex) {
     set_last_error(ex.what());
     return ex.code;

@@ -370,6 +370,9 @@ hg_config config_from_gguf(const Gguf& g) {  // config.rs:35-98
   c.expert_weights_norm = g.get_bool(key("expert_weights_norm"), &b) ? (int32_t)b : 0;
   c.eos_token = 50256;
   if (g.get_u32("tokenizer.ggml.eos_token_id", &v)) c.eos_token = (int32_t)v;
+  c.diffusion = g.get_bool("diffusion.enabled", &b) ? (int32_t)b : 0;
+  c.mask_token_id = g.get_u32("diffusion.mask_token_id", &v) ? (int32_t)v : 50257;
+  c.block_size = g.get_u32("diffusion.block_size", &v) ? (int32_t)v : 32;
   return c;
 }
 

@@ -35,9 +35,10 @@ void launch_kp_qk_rope_append(const float* qkv, int rows, int base, int nh, int 
                               const float* q_norm, const float* k_norm, const float* rcos, const float* rsin,
                               const int32_t* bt, float* k_pool, float* v_pool, long long page_stride, float* qo,
                               cudaStream_t st);
-void launch_kp_attention(const float* q, int qd, int t0, int tq, int base, int nh, int nkv, int hd, const int32_t* bt,
-                         const float* k_pool, const float* v_pool, long long page_stride, float* S, float* inv,
-                         float* o, cudaStream_t st);
+// nfix = 0: causal rows (query t sees keys 0..base+t); nfix > 0: every row sees keys 0..nfix-1.
+void launch_kp_attention(const float* q, int qd, int t0, int tq, int base, int nfix, int nh, int nkv, int hd,
+                         const int32_t* bt, const float* k_pool, const float* v_pool, long long page_stride, float* S,
+                         float* inv, float* o, cudaStream_t st);
 void launch_kp_route(const float* h, int tn, int d, const float* router, const float* bias, int ne, int k, int gsig,
                      int wnorm, float wscale, int32_t* sel, float* selw, int32_t* ecount, int32_t* elist, int list_cap,
                      cudaStream_t st);

@@ -211,17 +211,19 @@ __global__ void __launch_bounds__(128) kp_qk_rope_append(const float* qkv, int r
 
 // ------------------------------------------------------------------------------------------
 // Attention scores for a tile of query rows. R = (t_local, head-in-group) flattened for one kv
-// head g: R = t_local * rep + hr. S[j][R] = dot(q, k_j) * scale for j < base + t + 1.
-// One thread per (R, j) with the ops::dot order computed per SIMD lane.
+// head g: R = t_local * rep + hr. S[j][R] = dot(q, k_j) * scale for j < base + t + 1 (causal), or
+// for j < nfix when nfix > 0: every row attends to the same nfix keys, the diffusion block's
+// prefix plus the whole block (model.rs:556-565). One thread per (R, j) with the ops::dot order
+// computed per SIMD lane.
 // ------------------------------------------------------------------------------------------
 template <int HD>
 __global__ void __launch_bounds__(256) kp_scores(const float* q, int qd, int t0, int tq, int base, int rep, int kvh,
                                                  const int32_t* bt, const float* k_pool, long long page_stride,
-                                                 float* S, int nR) {
+                                                 float* S, int nR, int nfix) {
   __shared__ float qs[32][HD + 1];
   __shared__ float ks[32][HD + 1];
   const int R0 = blockIdx.x * 32, j0 = blockIdx.y * 32;
-  const int nmax = base + t0 + tq;  // longest row in the tile set
+  const int nmax = nfix > 0 ? nfix : base + t0 + tq;  // longest row in the tile set
   if (j0 >= nmax) return;
   // rows of this R tile: token t_local = R / rep, head = kvh*rep + R%rep
   for (int i = threadIdx.x; i < 32 * HD; i += 256) {
@@ -245,7 +247,7 @@ __global__ void __launch_bounds__(256) kp_scores(const float* q, int qd, int t0,
     int R = R0 + rr, j = j0 + jj;
     if (R >= nR) continue;
     int tl = R / rep;
-    if (j >= base + t0 + tl + 1) continue;
+    if (j >= (nfix > 0 ? nfix : base + t0 + tl + 1)) continue;
     const float* a = qs[rr];
     const float* b = ks[jj];
     float t8[8];
@@ -269,17 +271,18 @@ __global__ void __launch_bounds__(256) kp_scores(const float* q, int qd, int t0,
 // Softmax of 32 score rows (ops.rs:112-128) per CTA of 1024 threads: the row maxima in parallel
 // (order does not matter for a max), then in chunks of 256 positions e = exp(s - max) is written
 // back in place and staged in shared memory, where lane r of warp 0 adds row r's values in
-// position order (the reference's sequential sum). inv[R] = 1 / sum.
-__global__ void __launch_bounds__(1024) kp_softmax_rows(float* S, int nR, int rep, int base, int t0, float* inv) {
+// position order (the reference's sequential sum). inv[R] = 1 / sum. Row lengths as kp_scores.
+__global__ void __launch_bounds__(1024) kp_softmax_rows(float* S, int nR, int rep, int base, int t0, int nfix,
+                                                        float* inv) {
   __shared__ float ch[256][33];
   __shared__ float mred[32][33];
   __shared__ float m_s[32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int R = blockIdx.x * 32 + lane;
   const bool valid = R < nR;
-  const int n = valid ? base + t0 + R / rep + 1 : 0;
+  const int n = valid ? (nfix > 0 ? nfix : base + t0 + R / rep + 1) : 0;
   const int Rl = min(blockIdx.x * 32 + 31, nR - 1);
-  const int nmax = base + t0 + Rl / rep + 1;
+  const int nmax = nfix > 0 ? nfix : base + t0 + Rl / rep + 1;
   float m = -INFINITY;
   for (int j = warp; j < nmax; j += 32)
     if (j < n) {
@@ -316,11 +319,12 @@ __global__ void __launch_bounds__(1024) kp_softmax_rows(float* S, int nR, int re
   if (warp == 0 && valid) inv[R] = __fdiv_rn(1.0f, sum);
 }
 
-// O[t][h][dd] = sum_j (e_j * inv) * v_j[dd], sequential in j (model.rs:426-432). Tile: 32 R x HD.
+// O[t][h][dd] = sum_j (e_j * inv) * v_j[dd], sequential in j (model.rs:426-432; 573-584 for a
+// diffusion block, whose prefix-then-block order is position order). Tile: 32 R x HD.
 template <int HD>
 __global__ void __launch_bounds__(256) kp_pv(const float* S, const float* inv, int nR, int rep, int base, int t0,
-                                             int kvh, const int32_t* bt, const float* v_pool, long long page_stride,
-                                             float* o, int qd) {
+                                             int nfix, int kvh, const int32_t* bt, const float* v_pool,
+                                             long long page_stride, float* o, int qd) {
   constexpr int PD = HD / 32;  // dims per thread (threads: 8 R-groups x 32 dims)
   __shared__ float ps[32][33];
   __shared__ float vs[32][HD];
@@ -336,11 +340,11 @@ __global__ void __launch_bounds__(256) kp_pv(const float* S, const float* inv, i
 #pragma unroll
   for (int i = 0; i < 4; i++) {
     int R = R0 + rg * 4 + i;
-    lim[i] = R < nR ? base + t0 + R / rep + 1 : 0;
+    lim[i] = R < nR ? (nfix > 0 ? nfix : base + t0 + R / rep + 1) : 0;
     iv[i] = R < nR ? inv[R] : 0.0f;
   }
   int Rlast = min(R0 + 31, nR - 1);
-  const int nmax = base + t0 + Rlast / rep + 1;
+  const int nmax = nfix > 0 ? nfix : base + t0 + Rlast / rep + 1;
   for (int j0 = 0; j0 < nmax; j0 += 32) {
     __syncthreads();
     for (int i = threadIdx.x; i < 32 * 32; i += 256) {
@@ -556,20 +560,22 @@ void launch_kp_qk_rope_append(const float* qkv, int rows, int base, int nh, int 
   kp_qk_rope_append<<<(items + 3) / 4, 128, 4 * hd * sizeof(float), st>>>(
       qkv, rows, base, nh, nkv, hd, eps, q_norm, k_norm, rcos, rsin, bt, k_pool, v_pool, page_stride, qo);
 }
-void launch_kp_attention(const float* q, int qd, int t0, int tq, int base, int nh, int nkv, int hd, const int32_t* bt,
-                         const float* k_pool, const float* v_pool, long long page_stride, float* S, float* inv,
-                         float* o, cudaStream_t st) {
+void launch_kp_attention(const float* q, int qd, int t0, int tq, int base, int nfix, int nh, int nkv, int hd,
+                         const int32_t* bt, const float* k_pool, const float* v_pool, long long page_stride, float* S,
+                         float* inv, float* o, cudaStream_t st) {
   const int rep = nh / nkv;
   const int nR = tq * rep;
-  const int nmax = base + t0 + tq;
+  const int nmax = nfix > 0 ? nfix : base + t0 + tq;
   for (int g = 0; g < nkv; g++) {
     dim3 gs((nR + 31) / 32, (nmax + 31) / 32);
-    if (hd == 128) kp_scores<128><<<gs, 256, 0, st>>>(q, qd, t0, tq, base, rep, g, bt, k_pool, page_stride, S, nR);
-    else kp_scores<64><<<gs, 256, 0, st>>>(q, qd, t0, tq, base, rep, g, bt, k_pool, page_stride, S, nR);
-    kp_softmax_rows<<<(nR + 31) / 32, 1024, 0, st>>>(S, nR, rep, base, t0, inv);
+    if (hd == 128)
+      kp_scores<128><<<gs, 256, 0, st>>>(q, qd, t0, tq, base, rep, g, bt, k_pool, page_stride, S, nR, nfix);
+    else kp_scores<64><<<gs, 256, 0, st>>>(q, qd, t0, tq, base, rep, g, bt, k_pool, page_stride, S, nR, nfix);
+    kp_softmax_rows<<<(nR + 31) / 32, 1024, 0, st>>>(S, nR, rep, base, t0, nfix, inv);
     dim3 gp((nR + 31) / 32);
-    if (hd == 128) kp_pv<128><<<gp, 256, 0, st>>>(S, inv, nR, rep, base, t0, g, bt, v_pool, page_stride, o, qd);
-    else kp_pv<64><<<gp, 256, 0, st>>>(S, inv, nR, rep, base, t0, g, bt, v_pool, page_stride, o, qd);
+    if (hd == 128)
+      kp_pv<128><<<gp, 256, 0, st>>>(S, inv, nR, rep, base, t0, nfix, g, bt, v_pool, page_stride, o, qd);
+    else kp_pv<64><<<gp, 256, 0, st>>>(S, inv, nR, rep, base, t0, nfix, g, bt, v_pool, page_stride, o, qd);
   }
 }
 void launch_kp_route(const float* h, int tn, int d, const float* router, const float* bias, int ne, int k, int gsig,

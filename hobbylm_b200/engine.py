@@ -13,7 +13,7 @@ from typing import Callable, Iterable, Sequence
 
 import numpy as np
 
-from ._native import Config, EngineOpts, GenOptsC, HgError, TOKEN_CB, check, lib
+from ._native import BLOCK_CB, Config, DiffOptsC, EngineOpts, GenOptsC, HgError, TOKEN_CB, check, lib
 
 GPT2_VALID = 50257  # lib.rs:26
 
@@ -29,6 +29,25 @@ class GenOpts:
 
     def c(self) -> GenOptsC:
         return GenOptsC(self.max_new, self.temp, self.top_p, self.seed, self.rep_penalty)
+
+
+@dataclass
+class DiffOpts:
+    """DiffOpts (lib.rs:43-63, same defaults). block 0 takes the model's diffusion.block_size."""
+    gen_len: int = 128
+    block: int = 32
+    steps: int = 32
+    temp: float = 0.0
+    rep_penalty: float = 1.4
+    remask_steps: int = 0
+    remask_frac: float = 0.3
+    seed: int = 1234
+    cached: bool = True
+    threshold: float = 0.0
+
+    def c(self) -> DiffOptsC:
+        return DiffOptsC(self.gen_len, self.block, self.steps, self.temp, self.rep_penalty, self.remask_steps,
+                         self.remask_frac, self.seed, 1 if self.cached else 0, self.threshold)
 
 
 def _u32(ids) -> np.ndarray:
@@ -190,6 +209,43 @@ class Engine:
         sel = np.empty((self.cfg["n_layers"], self.cfg["top_k"]), np.int32)
         check(lib().hg_debug_last_routing(self.h, slot, sel.ctypes.data))
         return sel
+
+    def run_block(self, cache: KvCache, ids, n_logits: int | None = None, commit: bool = False):
+        """Model::run_block (model.rs:472-510) at position cache.len: the rows attend to the prefix and
+        to each other. Returns the logits [n_logits][vocab] of the last n_logits rows (default all, 0
+        for none); commit appends the block's K/V to the sequence (lib.rs:386-391)."""
+        ids = _u32(list(ids))
+        nl = len(ids) if n_logits is None else int(n_logits)
+        out = np.empty((nl, self.vocab), np.float32) if nl > 0 else None
+        check(lib().hg_run_block(self.h, cache.h, ids.ctypes.data, len(ids), nl, 1 if commit else 0,
+                                 out.ctypes.data if out is not None else None))
+        return out
+
+    def generate_diffusion(self, prompt_ids: Iterable[int], opts: DiffOpts | None = None,
+                           on_block: Callable[[list[int]], bool] | None = None) -> list[int]:
+        """Engine::generate_diffusion (lib.rs:211-495) on token ids. on_block(ids) receives each
+        finished block's new ids (up to the first eos) and returns False to stop."""
+        opts = opts or DiffOpts()
+        ids = _u32(list(prompt_ids))
+        out = np.empty(max(opts.gen_len, 1), np.uint32)
+        err: list[BaseException] = []
+
+        def cb(p, n, _user):
+            if on_block is None:
+                return 1
+            try:
+                return 1 if on_block([int(p[i]) for i in range(n)]) else 0
+            except BaseException as ex:  # stop generation and re-raise after the call returns
+                err.append(ex)
+                return 0
+
+        cfun = BLOCK_CB(cb)
+        o = opts.c()
+        n = check(lib().hg_generate_diffusion(self.h, ids.ctypes.data if len(ids) else None, len(ids), C.byref(o),
+                                              cfun, None, out.ctypes.data))
+        if err:
+            raise err[0]
+        return [int(t) for t in out[:n]]
 
     def generate(self, prompt_ids: Iterable[int], opts: GenOpts | None = None,
                  on_token: Callable[[int], bool] | None = None) -> list[int]:

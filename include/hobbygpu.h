@@ -47,6 +47,9 @@ typedef struct {
   int32_t n_experts, top_k, n_shared, vocab_size, context_length;
   int32_t expert_weights_norm, gating_sigmoid, eos_token;
   float rms_eps, rope_theta, expert_weights_scale;
+  /* diffusion.enabled (default 0), diffusion.mask_token_id (50257), diffusion.block_size (32):
+   * config.rs:92-94, keys without the architecture prefix */
+  int32_t diffusion, mask_token_id, block_size;
 } hg_config;
 
 /* Engine options (zero-initialised = defaults). */
@@ -67,6 +70,23 @@ typedef struct {
 
 /* Streaming callback: receives each generated token id; return 0 to stop (lib.rs:152). */
 typedef int (*hg_token_cb)(uint32_t token, void* user);
+
+/* Diffusion decode options, DiffOpts (lib.rs:43-63); NULL = DiffOpts::default(). block <= 0 takes
+ * the model's diffusion.block_size (main.rs:174). threshold > 0 selects the confidence-threshold
+ * schedule of the cached path; otherwise `steps` passes spread over gen_len (lib.rs:304-354). */
+typedef struct {
+  int32_t gen_len, block, steps;
+  float temp, rep_penalty;
+  int32_t remask_steps;
+  float remask_frac;
+  uint64_t seed;
+  int32_t cached;
+  float threshold;
+} hg_diff_opts;
+
+/* Diffusion streaming callback, called once per finished block with the ids it adds before the
+ * first eos (lib.rs:393-405, in ids instead of text; n may be 0); return 0 to stop. */
+typedef int (*hg_block_cb)(const uint32_t* ids, int n, void* user);
 
 const char* hg_last_error(void);
 
@@ -145,6 +165,25 @@ int hg_debug_time_attention(hg_engine* e, hg_seq** seqs, int n, int iters, float
  * out_ids (may be NULL) receives up to opts->max_new ids. Returns the count (>= 0) or an error. */
 int hg_generate(hg_engine* e, const uint32_t* ids, int n, const hg_gen_opts* opts, hg_token_cb cb, void* user,
                 uint32_t* out_ids);
+
+/* Model::run_block (model.rs:472-510): n token ids at positions hg_seq_len(s).. attend to the
+ * sequence's prefix and to every one of the n rows (bidirectional within the block), with the
+ * prefill arithmetic. The block's K/V rows are written past the sequence's length; commit != 0
+ * appends them to it (lib.rs:386-391), otherwise the length is unchanged and the next call at the
+ * same position overwrites them. logits_or_null: [n_logits][vocab] of the last n_logits rows
+ * (0 <= n_logits <= n) through the lm_head matmul (model.rs:505-508). On a sequence of length 0
+ * the logits are those of Model::forward_bidir (model.rs:441-470). n <= 1024 per call. */
+int hg_run_block(hg_engine* e, hg_seq* s, const uint32_t* ids, int n, int n_logits, int commit,
+                 float* logits_or_null);
+
+/* Engine::generate_diffusion (lib.rs:211-495) on token ids: the prefix-cached path (the prompt
+ * encoded bidirectionally, each denoising pass re-running only the active block) or, with
+ * cached = 0, the uncached path (every pass re-runs the canvas). The [MASK] id is the model's
+ * diffusion.mask_token_id; ids >= 50257 are never emitted. out_ids (may be NULL) receives up to
+ * gen_len ids. Returns the generated count (>= 0) or an error. The prompt (cached) or the canvas
+ * (uncached) holds at most 1024 positions. */
+int hg_generate_diffusion(hg_engine* e, const uint32_t* ids, int n, const hg_diff_opts* opts, hg_block_cb cb,
+                          void* user, uint32_t* out_ids);
 
 /* Debug: expert ids selected at every MoE layer by the last decode step of sequence slot `slot`
  * of the last hg_forward / hg_decode_batch ([n_layers][top_k], -1 for dense layers). */

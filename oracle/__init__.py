@@ -68,6 +68,9 @@ def lib():
         "hor_prefill": (i, [vp, vp, u32p, i, f32p]),
         "hor_prefill_embeds": (i, [vp, vp, f32p, i, f32p]),
         "hor_forward_x": (i, [vp, vp, f32p, i, f32p]),
+        "hor_run_block": (i, [vp, vp, u32p, i, i, vp]),
+        "hor_forward_bidir": (i, [vp, u32p, i, f32p]),
+        "hor_generate_diffusion": (i, [vp, u32p, i, i, i, i, f, f, i, f, C.c_uint64, i, f, u32p, C.POINTER(i)]),
         "hor_forward": (i, [vp, vp, C.c_uint32, i, f32p]),
         "hor_last_routing": (i, [vp, i32p, f32p]),
         "hor_generate": (i, [vp, u32p, i, i, f, f, C.c_uint64, f, u32p, vp, C.POINTER(i), C.POINTER(d),
@@ -114,7 +117,7 @@ def _ptr(a):
 
 CONFIG_INTS = ("d_model", "n_layers", "n_dense", "n_heads", "n_kv_heads", "head_dim", "dense_ffn", "expert_ffn",
                "n_experts", "top_k", "n_shared", "vocab_size", "context_length", "expert_weights_norm",
-               "gating_sigmoid", "eos")
+               "gating_sigmoid", "eos", "diffusion", "mask_token_id", "block_size")
 CONFIG_FLOATS = ("rms_eps", "rope_theta", "expert_weights_scale")
 
 
@@ -133,7 +136,7 @@ class Engine:
         h = C.c_void_p()
         _check(lib().hor_engine_load(path.encode(), 1 if quant else 0, C.byref(h)))
         self.h = h
-        ints = np.zeros(16, np.int32)
+        ints = np.zeros(len(CONFIG_INTS), np.int32)
         fl = np.zeros(3, np.float32)
         _check(lib().hor_engine_config(self.h, ints, fl))
         self.cfg = {k: int(v) for k, v in zip(CONFIG_INTS, ints)}
@@ -178,6 +181,33 @@ class Engine:
         out = np.zeros(self.vocab, np.float32)
         _check(lib().hor_forward(self.h, cache.h, int(token), int(pos), out))
         return out
+
+    def run_block(self, cache: "Cache", ids, commit: bool = False, want_logits: bool = True):
+        """Model::run_block (model.rs:472-510) at base = len(cache): logits [n][vocab] (or None);
+        commit appends the block's K/V to the cache (lib.rs:386-391)."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        out = np.zeros((len(ids), self.vocab), np.float32) if want_logits else None
+        _check(lib().hor_run_block(self.h, cache.h, ids, len(ids), 1 if commit else 0, _ptr(out)))
+        return out
+
+    def forward_bidir(self, ids) -> np.ndarray:
+        """Model::forward_bidir (model.rs:441-470): logits [n][vocab] of every position."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        out = np.zeros((len(ids), self.vocab), np.float32)
+        _check(lib().hor_forward_bidir(self.h, ids, len(ids), out))
+        return out
+
+    def generate_diffusion(self, ids, gen_len: int = 128, block: int = 32, steps: int = 32, temp: float = 0.0,
+                           rep_penalty: float = 1.4, remask_steps: int = 0, remask_frac: float = 0.3,
+                           seed: int = 1234, cached: bool = True, threshold: float = 0.0) -> np.ndarray:
+        """Engine::generate_diffusion (lib.rs:211-220) on token ids; DiffOpts defaults (lib.rs:59-63)."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        out = np.zeros(max(gen_len, 1), np.uint32)
+        n = C.c_int()
+        _check(lib().hor_generate_diffusion(self.h, ids, len(ids), gen_len, block, steps, temp, rep_penalty,
+                                            remask_steps, remask_frac, seed, 1 if cached else 0, threshold, out,
+                                            C.byref(n)))
+        return out[:n.value].copy()
 
     def last_routing(self):
         n = self.cfg["n_layers"] * self.cfg["top_k"]

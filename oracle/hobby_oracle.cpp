@@ -14,12 +14,17 @@
 //   ops.rs    dot (wide f32x8, 4 accumulators, 7-36), rmsnorm (85-95), softmax (112-128),
 //             sigmoid/silu (75-82), Rope in f64 (139-166)
 //   model.rs  Model::load (79-131), forward/forward_x (152-184), attention (186-238), ffn (240-327),
-//             prefill (340-370), attn_prefill (372-439), ffn_prefill (653-750), norm_head (753-763)
-//   lib.rs    Engine::generate (107-162); sample.rs argmax (53-64), sample (66-112), Rng (3-22)
+//             prefill (340-370), attn_prefill (372-439), ffn_prefill (653-750), norm_head (753-763),
+//             diffusion forward_bidir (441-470), run_block (472-510), attn_block_cached (512-587),
+//             attn_bidir (589-640)
+//   lib.rs    Engine::generate (107-162); diffusion: num_transfer (66-73), diffusion_block (164-209),
+//             score_block (221-263), generate_diffusion_cached (265-407) / _uncached (409-495);
+//             sample.rs argmax (53-64), sample (66-112), gumbel_argmax (29-47), Rng (3-22)
 //
 // Arithmetic pins (built with -ffp-contract=off so only the explicit fmaf/_mm256_fmadd_ps fuse,
 // matching Rust, which never contracts):
-//   * f32::exp is platform-defined in Rust. The oracle pins it to (float)exp((double)x), the
+//   * f32::exp and f32::ln are platform-defined in Rust. The oracle pins them to (float)exp((double)x)
+//     and (float)log((double)x) (ln appears only in the diffusion Gumbel sampler), the
 //     correctly rounded value with overwhelming probability. glibc 2.39 expf agrees with it on
 //     99.992% of finite inputs in [-104, 89]; `hor_set_exp_mode(1)` switches to libm expf so the
 //     difference can be measured.
@@ -63,6 +68,11 @@ struct Error : std::runtime_error {
 static inline float fexp(float x) {
   if (g_exp_mode == 1) return expf(x);
   return (float)exp((double)x);
+}
+// f32::ln (the diffusion Gumbel sampler, sample.rs:36-46), pinned like fexp.
+static inline float flog(float x) {
+  if (g_exp_mode == 1) return logf(x);
+  return (float)log((double)x);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -395,6 +405,8 @@ struct Config {
   int n_experts, top_k, n_shared, vocab_size, context_length;
   float rms_eps, rope_theta, expert_weights_scale;
   bool expert_weights_norm, gating_sigmoid;
+  bool diffusion;  // config.rs:92-94 (keys without the architecture prefix)
+  int mask_token_id, block_size;
   int q_dim() const { return n_heads * head_dim; }
   int kv_dim() const { return n_kv_heads * head_dim; }
   bool is_moe(int l) const { return l >= n_dense; }
@@ -446,6 +458,9 @@ static Config config_from_gguf(const Gguf& g) {  // config.rs:35-98
   c.expert_weights_scale = g.get_f32(k("expert_weights_scale"), &f) ? f : 1.0f;
   bool b;
   c.expert_weights_norm = g.get_bool(k("expert_weights_norm"), &b) ? b : false;
+  c.diffusion = g.get_bool("diffusion.enabled", &b) ? b : false;
+  c.mask_token_id = g.get_u32("diffusion.mask_token_id", &v) ? (int)v : 50257;
+  c.block_size = g.get_u32("diffusion.block_size", &v) ? (int)v : 32;
   return c;
 }
 
@@ -1073,6 +1088,159 @@ struct Model {
     rmsnorm(&x[(size_t)(tn - 1) * d], output_norm.data(), c.rms_eps, hl.data(), d);
     output.matvec(hl.data(), logits);
   }
+
+  // QK-norm + RoPE of the q and k heads of tn qkv rows at positions base + t (model.rs:529-542).
+  void qk_norm_rope_rows(const Layer& L, float* qkv, int tn, int base) const {
+    const Config& c = cfg;
+    int hd = c.head_dim, qd = c.q_dim(), kvd = c.kv_dim(), qw = qd + 2 * kvd;
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < tn; t++) {
+      float* row = qkv + (size_t)t * qw;
+      for (int hq = 0; hq < c.n_heads; hq++) {
+        norm_head(row + hq * hd, L.attn_q_norm.data(), c.rms_eps, hd);
+        rope.apply(row + hq * hd, base + t);
+      }
+      for (int hk = 0; hk < c.n_kv_heads; hk++) {
+        norm_head(row + qd + hk * hd, L.attn_k_norm.data(), c.rms_eps, hd);
+        rope.apply(row + qd + hk * hd, base + t);
+      }
+    }
+  }
+
+  // model.rs:512-587 (attn_block_cached): the b block queries attend to the cached prefix keys
+  // (0..base) and then to every block key (bidirectional). bk / bv receive the block's K / V rows.
+  void attn_block_cached(const Layer& L, const float* h, int li, const KvCache& cache, int base, int b, float* proj,
+                         float* bk, float* bv) const {
+    const Config& c = cfg;
+    int hd = c.head_dim, qd = c.q_dim(), kvd = c.kv_dim(), qw = qd + 2 * kvd, rep = c.n_heads / c.n_kv_heads;
+    float scale = 1.0f / sqrtf((float)hd);
+    std::vector<float> qkv((size_t)b * qw);
+    L.attn_qkv.matmul(h, qkv.data(), b);
+    qk_norm_rope_rows(L, qkv.data(), b, base);
+    for (int t = 0; t < b; t++) {
+      const float* row = qkv.data() + (size_t)t * qw;
+      memcpy(bk + (size_t)t * kvd, row + qd, kvd * 4);
+      memcpy(bv + (size_t)t * kvd, row + qd + kvd, kvd * 4);
+    }
+    const float* pk = cache.k[li].data();
+    const float* pv = cache.v[li].data();
+    const int n = base + b;
+    std::vector<float> o((size_t)b * qd, 0.0f);
+#pragma omp parallel for schedule(dynamic, 2)
+    for (int t = 0; t < b; t++) {
+      const float* qrow = qkv.data() + (size_t)t * qw;
+      std::vector<float> scores(n);
+      float* orow = o.data() + (size_t)t * qd;
+      for (int hq = 0; hq < c.n_heads; hq++) {
+        int kvh = hq / rep;
+        const float* qh = qrow + hq * hd;
+        for (int j = 0; j < base; j++) scores[j] = dot(qh, pk + (size_t)j * kvd + kvh * hd, hd) * scale;
+        for (int j = 0; j < b; j++) scores[base + j] = dot(qh, bk + (size_t)j * kvd + kvh * hd, hd) * scale;
+        softmax(scores.data(), n);
+        float* oh = orow + hq * hd;
+        for (int j = 0; j < base; j++) {
+          const float* vt = pv + (size_t)j * kvd + kvh * hd;
+          float p = scores[j];
+          for (int di = 0; di < hd; di++) oh[di] += p * vt[di];
+        }
+        for (int j = 0; j < b; j++) {
+          const float* vt = bv + (size_t)j * kvd + kvh * hd;
+          float p = scores[base + j];
+          for (int di = 0; di < hd; di++) oh[di] += p * vt[di];
+        }
+      }
+    }
+    L.attn_output.matmul(o.data(), proj, b);
+  }
+
+  // model.rs:472-510 (run_block): b residual rows at positions base.. against the frozen prefix of
+  // `cache` (which is not modified). logits (may be null): [b][vocab] through output.matmul.
+  // bk / bv: [n_layers][b * kv_dim] block K / V, appended by the caller when the block is final.
+  void run_block(const float* inputs, int b, const KvCache& cache, int base, float* logits,
+                 std::vector<std::vector<float>>& bk, std::vector<std::vector<float>>& bv) const {
+    const Config& c = cfg;
+    int d = c.d_model, kvd = c.kv_dim();
+    if (cache.len < base) throw Error("run_block base beyond the cached prefix");
+    std::vector<float> x(inputs, inputs + (size_t)b * d), h((size_t)b * d), tmp((size_t)b * d);
+    bk.assign(c.n_layers, std::vector<float>((size_t)b * kvd));
+    bv.assign(c.n_layers, std::vector<float>((size_t)b * kvd));
+    for (int li = 0; li < c.n_layers; li++) {
+      const Layer& L = layers[li];
+#pragma omp parallel for schedule(static)
+      for (int t = 0; t < b; t++)
+        rmsnorm(&x[(size_t)t * d], L.attn_norm.data(), c.rms_eps, &h[(size_t)t * d], d);
+      attn_block_cached(L, h.data(), li, cache, base, b, tmp.data(), bk[li].data(), bv[li].data());
+      for (size_t i = 0; i < (size_t)b * d; i++) x[i] += tmp[i];
+#pragma omp parallel for schedule(static)
+      for (int t = 0; t < b; t++)
+        rmsnorm(&x[(size_t)t * d], L.ffn_norm.data(), c.rms_eps, &h[(size_t)t * d], d);
+      ffn_prefill(L, h.data(), b, tmp.data());
+      for (size_t i = 0; i < (size_t)b * d; i++) x[i] += tmp[i];
+    }
+    if (!logits) return;
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < b; t++) rmsnorm(&x[(size_t)t * d], output_norm.data(), c.rms_eps, &h[(size_t)t * d], d);
+    output.matmul(h.data(), logits, b);
+  }
+
+  // model.rs:589-640 (attn_bidir): every query attends to every key, RoPE at position t, no cache.
+  void attn_bidir(const Layer& L, const float* h, int tn, float* proj) const {
+    const Config& c = cfg;
+    int hd = c.head_dim, qd = c.q_dim(), kvd = c.kv_dim(), qw = qd + 2 * kvd, rep = c.n_heads / c.n_kv_heads;
+    float scale = 1.0f / sqrtf((float)hd);
+    std::vector<float> qkv((size_t)tn * qw);
+    L.attn_qkv.matmul(h, qkv.data(), tn);
+    qk_norm_rope_rows(L, qkv.data(), tn, 0);
+    std::vector<float> kbuf((size_t)tn * kvd), vbuf((size_t)tn * kvd);
+    for (int t = 0; t < tn; t++) {
+      const float* row = qkv.data() + (size_t)t * qw;
+      memcpy(&kbuf[(size_t)t * kvd], row + qd, kvd * 4);
+      memcpy(&vbuf[(size_t)t * kvd], row + qd + kvd, kvd * 4);
+    }
+    std::vector<float> o((size_t)tn * qd, 0.0f);
+#pragma omp parallel for schedule(dynamic, 2)
+    for (int t = 0; t < tn; t++) {
+      const float* qrow = qkv.data() + (size_t)t * qw;
+      std::vector<float> scores(tn);
+      float* orow = o.data() + (size_t)t * qd;
+      for (int hq = 0; hq < c.n_heads; hq++) {
+        int kvh = hq / rep;
+        const float* qh = qrow + hq * hd;
+        for (int j = 0; j < tn; j++) scores[j] = dot(qh, &kbuf[(size_t)j * kvd + kvh * hd], hd) * scale;
+        softmax(scores.data(), tn);
+        float* oh = orow + hq * hd;
+        for (int j = 0; j < tn; j++) {
+          const float* vt = &vbuf[(size_t)j * kvd + kvh * hd];
+          float p = scores[j];
+          for (int di = 0; di < hd; di++) oh[di] += p * vt[di];
+        }
+      }
+    }
+    L.attn_output.matmul(o.data(), proj, tn);
+  }
+
+  // model.rs:441-470 (forward_bidir): logits [tn][vocab] of every position of a bidirectional pass.
+  void forward_bidir(const float* inputs, int tn, float* logits) const {
+    const Config& c = cfg;
+    int d = c.d_model;
+    std::vector<float> x(inputs, inputs + (size_t)tn * d), h((size_t)tn * d), tmp((size_t)tn * d);
+    for (int li = 0; li < c.n_layers; li++) {
+      const Layer& L = layers[li];
+#pragma omp parallel for schedule(static)
+      for (int t = 0; t < tn; t++)
+        rmsnorm(&x[(size_t)t * d], L.attn_norm.data(), c.rms_eps, &h[(size_t)t * d], d);
+      attn_bidir(L, h.data(), tn, tmp.data());
+      for (size_t i = 0; i < (size_t)tn * d; i++) x[i] += tmp[i];
+#pragma omp parallel for schedule(static)
+      for (int t = 0; t < tn; t++)
+        rmsnorm(&x[(size_t)t * d], L.ffn_norm.data(), c.rms_eps, &h[(size_t)t * d], d);
+      ffn_prefill(L, h.data(), tn, tmp.data());
+      for (size_t i = 0; i < (size_t)tn * d; i++) x[i] += tmp[i];
+    }
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < tn; t++) rmsnorm(&x[(size_t)t * d], output_norm.data(), c.rms_eps, &h[(size_t)t * d], d);
+    output.matmul(h.data(), logits, tn);
+  }
 };
 
 // sample.rs
@@ -1144,6 +1312,254 @@ struct Engine {
   uint32_t eos = 50256;
 };
 
+// sample.rs:29-47: Gumbel-max over the finite logits; temp <= 0 is the plain argmax.
+static uint32_t gumbel_argmax(const float* logits, int n, float temp, Rng& rng) {
+  if (temp <= 0.0f) return argmax(logits, n);
+  int best = 0;
+  float bv = -INFINITY;
+  for (int i = 0; i < n; i++) {
+    float l = logits[i];
+    if (!std::isfinite(l)) continue;
+    float u = std::clamp(rng.next_f32(), 1e-9f, 1.0f - 1e-9f);
+    float val = l / temp + -flog(-flog(u));
+    if (val > bv) {
+      bv = val;
+      best = i;
+    }
+  }
+  return (uint32_t)best;
+}
+
+// lib.rs:66-73: n unmask events spread over `steps` (sums to n).
+static std::vector<int> num_transfer(int n, int steps) {
+  int base = n / steps;
+  std::vector<int> out(steps, base);
+  for (int i = 0; i < n - base * steps; i++) out[i] += 1;
+  return out;
+}
+
+// DiffOpts (lib.rs:43-63).
+struct DiffOpts {
+  int gen_len = 128, block = 32, steps = 32;
+  float temp = 0.0f, rep_penalty = 1.4f;
+  int remask_steps = 0;
+  float remask_frac = 0.3f;
+  uint64_t seed = 1234;
+  bool cached = true;
+  float threshold = 0.0f;
+};
+
+// lib.rs:221-263 (score_block): per block row, ids >= valid banned, the presence penalty over the
+// committed ids and the block's own non-mask ids, a Gumbel / greedy pick, and the softmax
+// probabilities of the pick (pconf) and of the row's current id (cconf).
+static void score_block(const float* all, int V, const uint32_t* blk, int blk_len, const uint32_t* committed,
+                        int n_committed, int valid, uint32_t mask, float rep_penalty, float temp, Rng& rng,
+                        uint32_t* pred, float* pconf, float* cconf) {
+  std::vector<char> present(valid, 0);
+  if (rep_penalty != 1.0f) {
+    for (int i = 0; i < n_committed + blk_len; i++) {
+      uint32_t id = i < n_committed ? committed[i] : blk[i - n_committed];
+      if (id != mask && (int64_t)id < valid) present[id] = 1;
+    }
+  }
+  std::vector<float> row(V);
+  for (int i = 0; i < blk_len; i++) {
+    memcpy(row.data(), all + (size_t)i * V, (size_t)V * 4);
+    for (int l = valid; l < V; l++) row[l] = -INFINITY;
+    if (rep_penalty != 1.0f)
+      for (int t = 0; t < valid; t++)
+        if (present[t]) {
+          float l = row[t];
+          row[t] = l > 0.0f ? l / rep_penalty : l * rep_penalty;
+        }
+    uint32_t p = gumbel_argmax(row.data(), V, temp, rng);
+    softmax(row.data(), V);
+    pred[i] = p;
+    pconf[i] = row[p];
+    cconf[i] = row[blk[i]];
+  }
+}
+
+static void embed_rows(const Engine& e, const uint32_t* ids, int n, std::vector<float>& out) {
+  const int d = e.cfg.d_model;
+  out.resize((size_t)n * d);
+  for (int t = 0; t < n; t++) {
+    if ((int64_t)ids[t] >= e.cfg.vocab_size) throw Error("token id out of range");
+    memcpy(&out[(size_t)t * d], &e.model.token_embd[(size_t)ids[t] * d], d * 4);
+  }
+}
+
+// lib.rs:265-407 (generate_diffusion_cached) over token ids; the per-block text stream becomes
+// the committed ids up to the first eos. Returns the generated count; out receives the ids.
+static int diffusion_cached(Engine& e, const uint32_t* prompt, int p, const DiffOpts& o, std::vector<uint32_t>& out) {
+  const Config& c = e.cfg;
+  const int V = c.vocab_size, valid = std::min(50257, V);
+  const uint32_t mask = (uint32_t)c.mask_token_id;
+  Rng rng(o.seed);
+  out.clear();
+  if (p == 0) return 0;
+  const int gen_len = std::min(o.gen_len, std::max(c.context_length - (p + o.block), 1));
+  KvCache cache;
+  e.model.new_cache(cache);
+  std::vector<float> rows;
+  std::vector<std::vector<float>> bk, bv;
+  embed_rows(e, prompt, p, rows);
+  e.model.run_block(rows.data(), p, cache, 0, nullptr, bk, bv);
+  for (int li = 0; li < c.n_layers; li++) {
+    cache.k[li].insert(cache.k[li].end(), bk[li].begin(), bk[li].end());
+    cache.v[li].insert(cache.v[li].end(), bv[li].begin(), bv[li].end());
+  }
+  cache.len = p;
+  std::vector<uint32_t> committed(prompt, prompt + p);
+  int b0 = p;
+  while (b0 < p + gen_len) {
+    const int b1 = std::min(b0 + o.block, p + gen_len), blk_len = b1 - b0, base = b0;
+    std::vector<uint32_t> blk(blk_len, mask), pred(blk_len);
+    std::vector<float> all((size_t)blk_len * V), pconf(blk_len), cconf(blk_len);
+    auto step = [&]() {
+      embed_rows(e, blk.data(), blk_len, rows);
+      e.model.run_block(rows.data(), blk_len, cache, base, all.data(), bk, bv);
+      score_block(all.data(), V, blk.data(), blk_len, committed.data(), (int)committed.size(), valid, mask,
+                  o.rep_penalty, o.temp, rng, pred.data(), pconf.data(), cconf.data());
+    };
+    auto any_masked = [&]() { return std::find(blk.begin(), blk.end(), mask) != blk.end(); };
+    if (o.threshold > 0.0f) {
+      for (int it = 0; it < std::max(blk_len, 1); it++) {
+        if (!any_masked()) break;
+        step();
+        bool any = false;
+        int best = -1;
+        for (int i = 0; i < blk_len; i++) {
+          if (blk[i] != mask) continue;
+          if (best < 0 || !(pconf[i] < pconf[best])) best = i;  // Iterator::max_by keeps the last maximum
+        }
+        for (int i = 0; i < blk_len; i++)
+          if (blk[i] == mask && pconf[i] >= o.threshold) {
+            blk[i] = pred[i];
+            any = true;
+          }
+        if (!any) blk[best] = pred[best];
+      }
+    } else {
+      const int sb = std::max((int)roundf((float)(o.steps * blk_len) / (float)gen_len), 1);
+      for (int k_step : num_transfer(blk_len, sb)) {
+        step();
+        std::vector<std::pair<int, float>> cand;
+        for (int i = 0; i < blk_len; i++)
+          if (blk[i] == mask) cand.push_back({i, pconf[i]});
+        if (cand.empty()) break;
+        std::stable_sort(cand.begin(), cand.end(), [](const auto& a, const auto& b) { return a.second > b.second; });
+        for (int r = 0; r < std::min(k_step, (int)cand.size()); r++) blk[cand[r].first] = pred[cand[r].first];
+      }
+      if (any_masked()) {
+        step();
+        for (int i = 0; i < blk_len; i++)
+          if (blk[i] == mask) blk[i] = pred[i];
+      }
+    }
+    for (int it = 0; it < o.remask_steps; it++) {
+      step();
+      const int r = std::max((int)((float)blk_len * o.remask_frac), 1);
+      std::vector<std::pair<int, float>> idx(blk_len);
+      for (int i = 0; i < blk_len; i++) idx[i] = {i, cconf[i]};
+      std::stable_sort(idx.begin(), idx.end(), [](const auto& a, const auto& b) { return a.second < b.second; });
+      for (int q = 0; q < std::min(r, blk_len); q++) blk[idx[q].first] = mask;
+      step();
+      for (int i = 0; i < blk_len; i++)
+        if (blk[i] == mask) blk[i] = pred[i];
+    }
+    // finalize: the block's K / V join the cache
+    embed_rows(e, blk.data(), blk_len, rows);
+    e.model.run_block(rows.data(), blk_len, cache, base, nullptr, bk, bv);
+    for (int li = 0; li < c.n_layers; li++) {
+      cache.k[li].insert(cache.k[li].end(), bk[li].begin(), bk[li].end());
+      cache.v[li].insert(cache.v[li].end(), bv[li].begin(), bv[li].end());
+    }
+    cache.len = b1;
+    committed.insert(committed.end(), blk.begin(), blk.end());
+    int endpos = (int)committed.size();
+    bool hit = false;
+    for (int i = p; i < (int)committed.size(); i++)
+      if (committed[i] == e.eos) {
+        endpos = i;
+        hit = true;
+        break;
+      }
+    out.assign(committed.begin() + p, committed.begin() + endpos);
+    if (hit) return endpos - p;
+    b0 = b1;
+  }
+  return gen_len;
+}
+
+// lib.rs:409-495 (generate_diffusion_uncached): every step re-runs the canvas x[0..b1]
+// bidirectionally (diffusion_block, lib.rs:164-209).
+static int diffusion_uncached(Engine& e, const uint32_t* prompt, int p, const DiffOpts& o,
+                              std::vector<uint32_t>& out) {
+  const Config& c = e.cfg;
+  const int V = c.vocab_size, valid = std::min(50257, V);
+  const uint32_t mask = (uint32_t)c.mask_token_id;
+  Rng rng(o.seed);
+  out.clear();
+  const int gen_len = std::min(o.gen_len, std::max(c.context_length - p, 1));
+  std::vector<uint32_t> x(prompt, prompt + p);
+  x.resize((size_t)p + gen_len, mask);
+  std::vector<float> rows, all;
+  int b0 = p;
+  while (b0 < p + gen_len) {
+    const int b1 = std::min(b0 + o.block, p + gen_len), blk_len = b1 - b0;
+    std::vector<uint32_t> pred(blk_len);
+    std::vector<float> pconf(blk_len), cconf(blk_len);
+    auto step = [&]() {
+      embed_rows(e, x.data(), b1, rows);
+      all.resize((size_t)b1 * V);
+      e.model.forward_bidir(rows.data(), b1, all.data());
+      score_block(all.data() + (size_t)b0 * V, V, x.data() + b0, blk_len, x.data(), b0, valid, mask, o.rep_penalty,
+                  o.temp, rng, pred.data(), pconf.data(), cconf.data());
+    };
+    const int sb = std::max((int)roundf((float)(o.steps * blk_len) / (float)gen_len), 1);
+    for (int k_step : num_transfer(blk_len, sb)) {
+      step();
+      std::vector<std::pair<int, float>> cand;
+      for (int i = 0; i < blk_len; i++)
+        if (x[b0 + i] == mask) cand.push_back({i, pconf[i]});
+      if (cand.empty()) break;
+      std::stable_sort(cand.begin(), cand.end(), [](const auto& a, const auto& b) { return a.second > b.second; });
+      for (int r = 0; r < std::min(k_step, (int)cand.size()); r++) x[b0 + cand[r].first] = pred[cand[r].first];
+    }
+    bool any = false;
+    for (int i = 0; i < blk_len; i++) any = any || x[b0 + i] == mask;
+    if (any) {
+      step();
+      for (int i = 0; i < blk_len; i++)
+        if (x[b0 + i] == mask) x[b0 + i] = pred[i];
+    }
+    for (int it = 0; it < o.remask_steps; it++) {
+      step();
+      const int r = std::max((int)((float)blk_len * o.remask_frac), 1);
+      std::vector<std::pair<int, float>> idx(blk_len);
+      for (int i = 0; i < blk_len; i++) idx[i] = {i, cconf[i]};
+      std::stable_sort(idx.begin(), idx.end(), [](const auto& a, const auto& b) { return a.second < b.second; });
+      for (int q = 0; q < std::min(r, blk_len); q++) x[b0 + idx[q].first] = mask;
+      step();
+      for (int i = 0; i < blk_len; i++)
+        if (x[b0 + i] == mask) x[b0 + i] = pred[i];
+    }
+    int endpos = b1;
+    bool hit = false;
+    for (int i = p; i < b1; i++)
+      if (x[i] == e.eos) {
+        endpos = i;
+        hit = true;
+        break;
+      }
+    out.assign(x.begin() + p, x.begin() + endpos);
+    if (hit) return endpos - p;
+    b0 = b1;
+  }
+  return gen_len;
+}
+
 }  // namespace hor
 
 using namespace hor;
@@ -1199,15 +1615,16 @@ int hor_engine_load(const char* path, int quant, void** out) {
 void hor_engine_free(void* e) { delete (Engine*)e; }
 
 // int fields: d_model n_layers n_dense n_heads n_kv_heads head_dim dense_ffn expert_ffn n_experts
-// top_k n_shared vocab_size context_length expert_weights_norm gating_sigmoid eos ; floats: rms_eps
-// rope_theta expert_weights_scale
+// top_k n_shared vocab_size context_length expert_weights_norm gating_sigmoid eos diffusion
+// mask_token_id block_size ; floats: rms_eps rope_theta expert_weights_scale
 int hor_engine_config(void* ep, int32_t* ints, float* floats) {
   HOR_TRY({
     Engine* e = (Engine*)ep;
     const Config& c = e->cfg;
-    int32_t v[16] = {c.d_model, c.n_layers, c.n_dense, c.n_heads, c.n_kv_heads, c.head_dim,
+    int32_t v[19] = {c.d_model, c.n_layers, c.n_dense, c.n_heads, c.n_kv_heads, c.head_dim,
                      c.dense_ffn, c.expert_ffn, c.n_experts, c.top_k, c.n_shared, c.vocab_size,
-                     c.context_length, (int)c.expert_weights_norm, (int)c.gating_sigmoid, (int)e->eos};
+                     c.context_length, (int)c.expert_weights_norm, (int)c.gating_sigmoid, (int)e->eos,
+                     (int)c.diffusion, c.mask_token_id, c.block_size};
     memcpy(ints, v, sizeof(v));
     floats[0] = c.rms_eps;
     floats[1] = c.rope_theta;
@@ -1274,6 +1691,61 @@ int hor_forward(void* ep, void* cp, uint32_t token, int pos, float* logits) {
 }
 
 // Routing of the last forward(): [n_layers][top_k] ids (-1 for dense layers) and gate weights.
+// Model::run_block (model.rs:472-510) of n token ids at base = cache length: logits (may be null)
+// [n][vocab]; commit != 0 appends the block's K / V to the cache as lib.rs:386-391 does.
+int hor_run_block(void* ep, void* cp, const uint32_t* ids, int n, int commit, float* logits) {
+  HOR_TRY({
+    Engine* e = (Engine*)ep;
+    KvCache& cache = *(KvCache*)cp;
+    std::vector<float> rows;
+    std::vector<std::vector<float>> bk, bv;
+    embed_rows(*e, ids, n, rows);
+    e->model.run_block(rows.data(), n, cache, cache.len, logits, bk, bv);
+    if (commit) {
+      for (int li = 0; li < e->cfg.n_layers; li++) {
+        cache.k[li].insert(cache.k[li].end(), bk[li].begin(), bk[li].end());
+        cache.v[li].insert(cache.v[li].end(), bv[li].begin(), bv[li].end());
+      }
+      cache.len += n;
+    }
+  })
+}
+
+// Model::forward_bidir (model.rs:441-470) of n token ids: logits [n][vocab].
+int hor_forward_bidir(void* ep, const uint32_t* ids, int n, float* logits) {
+  HOR_TRY({
+    Engine* e = (Engine*)ep;
+    std::vector<float> rows;
+    embed_rows(*e, ids, n, rows);
+    e->model.forward_bidir(rows.data(), n, logits);
+  })
+}
+
+// Engine::generate_diffusion (lib.rs:211-220) on token ids. out_ids: room for gen_len ids; the
+// generated count is written to *n_out.
+int hor_generate_diffusion(void* ep, const uint32_t* ids, int n, int gen_len, int block, int steps, float temp,
+                           float rep_penalty, int remask_steps, float remask_frac, uint64_t seed, int cached,
+                           float threshold, uint32_t* out_ids, int* n_out) {
+  HOR_TRY({
+    Engine* e = (Engine*)ep;
+    DiffOpts o;
+    o.gen_len = gen_len;
+    o.block = block > 0 ? block : std::max(e->cfg.block_size, 1);
+    o.steps = steps;
+    o.temp = temp;
+    o.rep_penalty = rep_penalty;
+    o.remask_steps = remask_steps;
+    o.remask_frac = remask_frac;
+    o.seed = seed;
+    o.cached = cached != 0;
+    o.threshold = threshold;
+    std::vector<uint32_t> out;
+    int cnt = o.cached ? diffusion_cached(*e, ids, n, o, out) : diffusion_uncached(*e, ids, n, o, out);
+    std::copy(out.begin(), out.end(), out_ids);
+    *n_out = cnt;
+  })
+}
+
 int hor_last_routing(void* ep, int32_t* sel, float* w) {
   HOR_TRY({
     Engine* e = (Engine*)ep;

@@ -128,6 +128,35 @@ def test_config_defaults_follow_config_rs(native, tmp_path):
     assert c["gating_sigmoid"] == 1 and c["expert_weights_norm"] == 0 and c["eos_token"] == 50256
 
 
+def test_diffusion_keys_follow_config_rs(native, tmp_path):
+    """diffusion.enabled / mask_token_id / block_size (config.rs:92-94) carry no architecture prefix;
+    absent they default to false / 50257 / 32."""
+    import gguf
+
+    meta = {"embedding_length": 64, "block_count": 2, "attention.head_count": 2, "attention.head_count_kv": 1,
+            "feed_forward_length": 64, "expert_feed_forward_length": 32, "expert_count": 4, "expert_used_count": 2}
+    p = tmp_path / "d.gguf"
+    w = gguf.GGUFWriter(str(p), "hobbylm")
+    for k, v in meta.items():
+        w.add_uint32(f"hobbylm.{k}", v)
+    w.add_bool("diffusion.enabled", True)
+    w.add_uint32("diffusion.mask_token_id", 100)
+    w.add_uint32("diffusion.block_size", 16)
+    w.add_tensor("token_embd.weight", np.zeros((123, 64), np.float32))
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    rc, cfg = _config(native, p)
+    assert rc == 0
+    c = cfg.as_dict()
+    assert (c["diffusion"], c["mask_token_id"], c["block_size"]) == (1, 100, 16)
+    q = tmp_path / "e.gguf"
+    _write_gguf(q, meta, {"token_embd.weight": np.zeros((123, 64), np.float32)})
+    rc, cfg = _config(native, q)
+    assert rc == 0 and (cfg.diffusion, cfg.mask_token_id, cfg.block_size) == (0, 50257, 32)
+
+
 def test_gguf_errors(native, tmp_path):
     lib = native.lib()
     h = C.c_void_p()
