@@ -42,6 +42,8 @@ def parse():
     ap.add_argument("--no-bs1", action="store_true", help="skip the config-4 bs1 sub-measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--bs1-only", action="store_true", help="run only the config-4 bs1 measurement (one GPU)")
+    ap.add_argument("--diffusion", action="store_true",
+                    help="measure diffusion decode (Engine::generate_diffusion) instead of the headline (one GPU)")
     ap.add_argument("--seqs", type=int, default=N_SEQS, help=argparse.SUPPRESS)
     return ap.parse_args()
 
@@ -374,6 +376,75 @@ def cpu_sample(path: str, prompts_all, steps: int = 4, n_sample: int = 2) -> dic
                       f"500M Q8_0, sequential like hobby-rs"}
 
 
+DIFF_PROMPT = 64
+
+
+def diffusion_cpu_sample(path: str, prompt) -> tuple[dict, list]:
+    """The oracle's generate_diffusion on one block: 32 ids, 8 denoising passes (the per-block
+    schedule of the defaults, round(32 * 32 / 128) = 8) after the bidirectional prompt encode."""
+    import oracle
+
+    ora = oracle.Engine(path, quant=True)
+    t = time.perf_counter()
+    ids = ora.generate_diffusion(prompt, gen_len=32, block=32, steps=8)
+    s = time.perf_counter() - t
+    ora.close()
+    return ({"value": round(len(ids) / s, 2), "unit": "tok/s", "cores": oracle.num_threads(), "kind": "port",
+             "sample": f"one 32-id block (8 passes + finalize) after a {len(prompt)}-id prompt encode, 500M Q8_0"},
+            [int(i) for i in ids])
+
+
+def run_diffusion(args):
+    """Diffusion decode on one GPU: Engine::generate_diffusion (lib.rs:211-495) with DiffOpts
+    defaults (gen_len 128, block 32, 32 steps, greedy, presence penalty 1.4, prefix-cached) after a
+    64-id prompt, wall clock per call (the block scoring runs on the host between GPU passes)."""
+    import torch
+
+    from hobbylm_b200 import DiffOpts, Engine, synth
+
+    path = synth.cached_model("500M", 0, context_length=CTX)
+    prompt = synth.prompt_ids(DIFF_PROMPT, 6)
+    eng = Engine.load(path, device=0, max_batch=1, kv_pool_tokens=4096)
+    first = eng.generate_diffusion(prompt, DiffOpts(gen_len=32, block=32, steps=8))
+    for _ in range(args.warmup):
+        eng.generate_diffusion(prompt, DiffOpts())
+    res = {}
+    for name, o in (("cached", DiffOpts()), ("uncached", DiffOpts(cached=False))):
+        times, n = [], 0
+        for _ in range(args.steps):
+            torch.cuda.synchronize()
+            t = time.perf_counter()
+            n = len(eng.generate_diffusion(prompt, o))
+            times.append(time.perf_counter() - t)
+        res[name] = (n, statistics.median(times))
+    # one denoising pass of the cached path: a 32-row block after the prompt, logits to the host
+    with eng.new_cache() as kv:
+        eng.run_block(kv, prompt, n_logits=0, commit=True)
+        blk = [eng.cfg["mask_token_id"]] * 32
+        for _ in range(3):
+            eng.run_block(kv, blk)
+        t = time.perf_counter()
+        for _ in range(20):
+            eng.run_block(kv, blk)
+        pass_ms = (time.perf_counter() - t) / 20 * 1e3
+    eng.close()
+    cpu = None if args.no_cpu else diffusion_cpu_sample(path, prompt)
+    n, s = res["cached"]
+    line = {"metric": "diffusion decode tok/s (500M Q8_0, DiffOpts defaults, prefix-cached)", "value": round(n / s, 1),
+            "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(s * 1e3, 2), "higher_is_better": True, "scaling": "replicas only",
+            "vs_baseline": None, "dtype": "int8 dot / f32", "data": "synthetic",
+            "config": {"workload": f"500M Q8_0 seed 0, {DIFF_PROMPT}-id prompt (seed 6), gen_len 128, block 32, "
+                                   "32 steps, temp 0, rep_penalty 1.4; a step = one generate_diffusion call"},
+            "generated": n, "pass_ms_32_rows": round(pass_ms, 3),
+            "uncached": {"value": round(res["uncached"][0] / res["uncached"][1], 1), "unit": "tok/s",
+                         "ms_per_call": round(res["uncached"][1] * 1e3, 2)}}
+    if cpu is not None:
+        line["cpu_baseline"] = cpu[0]
+        line["first_block_equals_oracle"] = cpu[1] == first
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args):
     """The reference arm: the CPU oracle on the host cores, rank 0 only."""
     rank, world, local = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), 0
@@ -427,6 +498,8 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.diffusion:
+        run_diffusion(args)
     elif args.bs1_only:
         from hobbylm_b200 import synth
 

@@ -57,3 +57,12 @@ def test_sequence_shards_partition_the_batch(n, world):
     parts = [bench.shard(n, r, world) for r in range(world)]
     assert sorted(i for p in parts for i in p) == list(range(n))
     assert max(map(len, parts)) - min(map(len, parts)) <= 1
+
+
+def test_diffusion_cpu_sample_reports_the_oracle(model130):
+    """bench.py --diffusion's CPU leg: one 32-id block of the oracle's generate_diffusion."""
+    from hobbylm_b200 import synth
+
+    base, ids = bench.diffusion_cpu_sample(model130, synth.prompt_ids(16, 6))
+    assert base["kind"] == "port" and base["unit"] == "tok/s" and base["value"] > 0 and base["cores"] >= 1
+    assert len(ids) == 32 and all(t < bench.VALID for t in ids)
