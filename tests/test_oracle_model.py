@@ -1,0 +1,76 @@
+"""CPU self-consistency of the oracle's model paths (hobby-rs model.rs:152-184, 340-439), the
+properties the GPU parity tests also assert of the CUDA path."""
+import numpy as np
+import pytest
+
+from hobbylm_b200 import synth
+
+
+@pytest.fixture(scope="module")
+def eng(oracle_mod):
+    return oracle_mod.Engine(synth.cached_model("130M", 0), quant=True)
+
+
+@pytest.fixture(scope="module")
+def emb(native, eng):
+    path = synth.cached_model("130M", 0)
+    d, vocab = eng.cfg["d_model"], eng.vocab
+    out = np.empty(vocab * d, np.float32)
+    native.check(native.lib().hg_gguf_tensor_f32(path.encode(), b"token_embd.weight", out.ctypes.data, out.size))
+    return out.reshape(vocab, d)
+
+
+def _bits(a):
+    return np.ascontiguousarray(a).view(np.uint32)
+
+
+def test_forward_x_of_the_embedding_row_is_forward(eng, emb):
+    """Model::forward is forward_x of the token's embedding row (model.rs:152-160)."""
+    ids = synth.prompt_ids(20, 21)
+    a, b = eng.new_cache(), eng.new_cache()
+    eng.prefill(a, ids)
+    eng.prefill(b, ids)
+    for i, tok in enumerate([5, 777, 50000]):
+        la = eng.forward(a, tok, 20 + i)
+        lb = eng.forward_x(b, emb[tok], 20 + i)
+        assert np.array_equal(_bits(la), _bits(lb))
+
+
+def test_prefill_of_embedding_rows_is_prefill_of_ids(eng, emb):
+    """Engine::generate feeds prefill the token embeddings (lib.rs:118-126)."""
+    ids = synth.prompt_ids(33, 22)
+    a, b = eng.new_cache(), eng.new_cache()
+    assert np.array_equal(_bits(eng.prefill(a, ids)), _bits(eng.prefill_embeds(b, emb[ids])))
+
+
+def test_chunked_prefill_equals_one_prefill(eng):
+    """Rows are independent in the prefill matmuls and each row's attention reads keys 0..pos, so
+    prefilling in two calls gives the same logits and cache as one call."""
+    ids = synth.prompt_ids(40, 23)
+    a, b = eng.new_cache(), eng.new_cache()
+    la = eng.prefill(a, ids)
+    eng.prefill(b, ids[:17])
+    lb = eng.prefill(b, ids[17:])
+    assert np.array_equal(_bits(la), _bits(lb))
+    for li in (0, eng.cfg["n_layers"] - 1):
+        ka, va = a.layer(li)
+        kb, vb = b.layer(li)
+        assert np.array_equal(_bits(ka), _bits(kb)) and np.array_equal(_bits(va), _bits(vb))
+
+
+def test_generate_is_prefill_then_greedy_forward(eng):
+    """Engine::generate at temp 0 (lib.rs:107-162): masked argmax of the prefill logits, then of
+    each forward step, stopping on eos."""
+    ids = synth.prompt_ids(16, 24)
+    toks, _, _, _ = eng.generate(ids, 6)
+    c = eng.new_cache()
+    lg = eng.prefill(c, ids)
+    out = []
+    for i in range(6):
+        lg[50257:] = -np.inf
+        t = int(np.argmax(lg))
+        if t == eng.cfg["eos"]:
+            break
+        out.append(t)
+        lg = eng.forward(c, t, 16 + i)
+    assert list(toks) == out
