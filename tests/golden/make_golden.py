@@ -17,6 +17,11 @@ It imports the reference's own Python code and writes, under tests/golden/:
   ``torch.Generator().manual_seed(1)``): the full last-position row plus per-position top-8 ids,
   values and logsumexp. hobby-rs reads rms_eps from GGUF metadata while the PyTorch RMSNorm uses
   1e-6, so the oracle is compared on a file written with rms_eps=1e-6.
+* torch_bidir_logits_130M.npz — the same model with ``cfg.diffusion = True``, whose attention is
+  bidirectional (hobbylm/model.py:225-226; the flag changes nothing else at inference), on an
+  18-position canvas: 12 prompt ids (seed 1) then 6 [MASK] ids (50257, hobbylm/config.py:48):
+  per-position top-8 ids, values and logsumexp, and the full rows of positions 0, 12 and 17.
+  This is the reference for Model::forward_bidir (hobby-rs model.rs:441-470).
 """
 from __future__ import annotations
 
@@ -110,12 +115,48 @@ def reference_torch_logits(ref: str) -> dict:
             "lse": lse.astype(np.float32)}
 
 
+BIDIR_ROWS = (0, 12, 17)
+
+
+def reference_torch_bidir_logits(ref: str) -> dict:
+    import torch
+
+    sys.path.insert(0, ref)
+    from hobbylm.config import get_config
+    from hobbylm.model import MoETransformer
+    from hobbylm_b200.synth import prompt_ids
+
+    cfg = get_config("130M")
+    cfg.expert_backend = "bmm"
+    cfg.diffusion = True
+    torch.manual_seed(0)
+    model = MoETransformer(cfg).eval()
+    canvas = np.concatenate([prompt_ids(12, 1).astype(np.int64), np.full(6, cfg.mask_token_id, np.int64)])
+    ids = torch.from_numpy(canvas).view(1, -1)
+    with torch.no_grad():
+        logits, _ = model(ids)
+    lg = logits[0].float().numpy()
+    top_ids = np.argsort(-lg, axis=1)[:, :8]
+    top_vals = np.take_along_axis(lg, top_ids, axis=1)
+    lse = np.log(np.exp(lg - lg.max(1, keepdims=True)).sum(1)) + lg.max(1)
+    return {"ids": canvas.astype(np.uint32), "rows": np.array(BIDIR_ROWS, np.int32),
+            "full": lg[list(BIDIR_ROWS)].astype(np.float32), "top_ids": top_ids.astype(np.int32),
+            "top_vals": top_vals.astype(np.float32), "lse": lse.astype(np.float32)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("HOBBYLM_REFERENCE", ""))
+    ap.add_argument("--only", choices=("all", "bidir"), default="all",
+                    help="bidir: write only torch_bidir_logits_130M.npz")
     a = ap.parse_args()
     if not a.reference or not os.path.isdir(a.reference):
         raise SystemExit("--reference must point at the HobbyLM checkout")
+    bl = reference_torch_bidir_logits(a.reference)
+    np.savez(os.path.join(HERE, "torch_bidir_logits_130M.npz"), **bl)
+    print("bidir logits", bl["top_ids"].shape)
+    if a.only == "bidir":
+        return
     for preset in ("130M", "500M"):
         d = reference_gguf_digests(a.reference, preset)
         with open(os.path.join(HERE, f"synth_digests_{preset}.json"), "w") as f:

@@ -54,6 +54,27 @@ def test_oracle_f32_matches_reference_torch(oracle_mod):
     assert rel < 1e-5, rel
 
 
+def test_oracle_forward_bidir_matches_reference_torch(oracle_mod):
+    """Model::forward_bidir (model.rs:441-470), the pass the diffusion decode is built on, against
+    the reference PyTorch model in its diffusion mode (bidirectional attention,
+    hobbylm/model.py:225-226) on a canvas of 12 prompt ids and 6 [MASK] ids."""
+    g = np.load(os.path.join(GOLDEN, "torch_bidir_logits_130M.npz"))
+    path = synth.cached_model("130M", 0, quant="f32", rms_eps=1e-6)
+    eng = oracle_mod.Engine(path, quant=False)
+    lg = eng.forward_bidir(g["ids"])
+    for r, full in zip(g["rows"], g["full"]):
+        rel = np.linalg.norm(lg[r] - full) / np.linalg.norm(full)
+        assert rel < 1e-5, (int(r), rel)
+    for pos in range(len(g["ids"])):
+        assert np.array_equal(np.argsort(-lg[pos])[:8], g["top_ids"][pos]), pos
+        lse = np.log(np.exp(lg[pos] - lg[pos].max()).sum()) + lg[pos].max()
+        assert abs(lse - g["lse"][pos]) < 1e-4, pos
+    # a causal pass over the same canvas differs at the prompt positions, which now see the masks
+    c = eng.new_cache()
+    causal_first = eng.prefill(c, g["ids"][:1])
+    assert np.linalg.norm(causal_first - g["full"][0]) / np.linalg.norm(g["full"][0]) > 1e-3
+
+
 def test_q8_0_fixture_dequant_matches_gguf_py(oracle_mod):
     """The oracle's Q8_0 dequant (gguf.rs:365-375) equals gguf-py's on a synthetic file's tensor."""
     import gguf
