@@ -22,6 +22,11 @@ It imports the reference's own Python code and writes, under tests/golden/:
   18-position canvas: 12 prompt ids (seed 1) then 6 [MASK] ids (50257, hobbylm/config.py:48):
   per-position top-8 ids, values and logsumexp, and the full rows of positions 0, 12 and 17.
   This is the reference for Model::forward_bidir (hobby-rs model.rs:441-470).
+* torch_diffusion_generate_130M.json — the reference's own greedy denoising sampler
+  (hobbylm/diffusion.py:92-176: num_transfer schedule, presence penalty, confidence-ordered
+  commits, low-confidence remasking, each pass over the canvas prefix x[:b1]) on that model after
+  the 12-id prompt, for three option sets. hobby-rs's uncached path (lib.rs:409-495) runs the same
+  loop; at temperature 0 no random draws are involved, so its ids must equal these.
 """
 from __future__ import annotations
 
@@ -144,17 +149,48 @@ def reference_torch_bidir_logits(ref: str) -> dict:
             "top_vals": top_vals.astype(np.float32), "lse": lse.astype(np.float32)}
 
 
+DIFF_CASES = (dict(gen_len=24, block=8, steps=8, rep_penalty=1.4),
+              dict(gen_len=24, block=8, steps=12, rep_penalty=1.4, remask_steps=1),
+              dict(gen_len=20, block=8, steps=5, rep_penalty=1.0))
+
+
+def reference_diffusion_generate(ref: str) -> dict:
+    import torch
+
+    sys.path.insert(0, ref)
+    from hobbylm import diffusion
+    from hobbylm.config import get_config
+    from hobbylm.model import MoETransformer
+    from hobbylm_b200.synth import prompt_ids
+
+    cfg = get_config("130M")
+    cfg.expert_backend = "bmm"
+    cfg.diffusion = True
+    torch.manual_seed(0)
+    model = MoETransformer(cfg).eval()
+    prompt = prompt_ids(12, 1).astype(np.int64)
+    cases = []
+    for kw in DIFF_CASES:
+        out = diffusion.generate(model, torch.from_numpy(prompt).view(1, -1), temperature=0.0, **kw)
+        cases.append({"opts": kw, "ids": [int(t) for t in out[0]]})
+    return {"prompt": [int(t) for t in prompt], "cases": cases}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("HOBBYLM_REFERENCE", ""))
     ap.add_argument("--only", choices=("all", "bidir"), default="all",
-                    help="bidir: write only torch_bidir_logits_130M.npz")
+                    help="bidir: write only the diffusion fixtures (bidirectional logits, greedy sampler ids)")
     a = ap.parse_args()
     if not a.reference or not os.path.isdir(a.reference):
         raise SystemExit("--reference must point at the HobbyLM checkout")
     bl = reference_torch_bidir_logits(a.reference)
     np.savez(os.path.join(HERE, "torch_bidir_logits_130M.npz"), **bl)
     print("bidir logits", bl["top_ids"].shape)
+    dg = reference_diffusion_generate(a.reference)
+    with open(os.path.join(HERE, "torch_diffusion_generate_130M.json"), "w") as f:
+        json.dump(dg, f)
+    print("diffusion cases", len(dg["cases"]))
     if a.only == "bidir":
         return
     for preset in ("130M", "500M"):

@@ -75,6 +75,20 @@ def test_oracle_forward_bidir_matches_reference_torch(oracle_mod):
     assert np.linalg.norm(causal_first - g["full"][0]) / np.linalg.norm(g["full"][0]) > 1e-3
 
 
+def test_oracle_diffusion_loop_matches_reference_sampler(oracle_mod):
+    """The uncached denoising loop (hobby-rs lib.rs:409-495) at temperature 0 against the
+    reference's own greedy sampler (hobbylm/diffusion.py:92-176) on the F32 model: same ids for
+    three schedules, with and without the presence penalty and a remasking pass."""
+    with open(os.path.join(GOLDEN, "torch_diffusion_generate_130M.json")) as f:
+        g = json.load(f)
+    path = synth.cached_model("130M", 0, quant="f32", rms_eps=1e-6)
+    eng = oracle_mod.Engine(path, quant=False)
+    prompt = np.array(g["prompt"], np.uint32)
+    for case in g["cases"]:
+        got = eng.generate_diffusion(prompt, cached=False, temp=0.0, **case["opts"])
+        assert [int(t) for t in got] == case["ids"], case["opts"]
+
+
 def test_q8_0_fixture_dequant_matches_gguf_py(oracle_mod):
     """The oracle's Q8_0 dequant (gguf.rs:365-375) equals gguf-py's on a synthetic file's tensor."""
     import gguf
