@@ -27,6 +27,10 @@ It imports the reference's own Python code and writes, under tests/golden/:
   commits, low-confidence remasking, each pass over the canvas prefix x[:b1]) on that model after
   the 12-id prompt, for three option sets. hobby-rs's uncached path (lib.rs:409-495) runs the same
   loop; at temperature 0 no random draws are involved, so its ids must equal these.
+* torch_embeds_logits_130M.npz — the causal model on caller rows (``inputs_embeds``,
+  hobbylm/model.py:325-333): 4 rows ~ N(0, 0.02^2) (numpy seed 7) spliced before the embeddings of
+  an 8-id prompt (seed 1), as lib.rs:118-121 splices modality rows; the full last row plus
+  per-position top-8 ids, values and logsumexp. The reference for Model::prefill / forward_x on rows.
 """
 from __future__ import annotations
 
@@ -176,14 +180,46 @@ def reference_diffusion_generate(ref: str) -> dict:
     return {"prompt": [int(t) for t in prompt], "cases": cases}
 
 
+def reference_torch_embeds_logits(ref: str) -> dict:
+    import torch
+
+    sys.path.insert(0, ref)
+    from hobbylm.config import get_config
+    from hobbylm.model import MoETransformer
+    from hobbylm_b200.synth import prompt_ids
+
+    cfg = get_config("130M")
+    cfg.expert_backend = "bmm"
+    torch.manual_seed(0)
+    model = MoETransformer(cfg).eval()
+    extra = (np.random.default_rng(7).standard_normal((4, cfg.d_model)) * 0.02).astype(np.float32)
+    ids = torch.from_numpy(prompt_ids(8, 1).astype(np.int64))
+    with torch.no_grad():
+        rows = torch.cat([torch.from_numpy(extra), model.embed(ids)], 0)
+        logits, _ = model(inputs_embeds=rows.unsqueeze(0))
+    lg = logits[0].float().numpy()
+    top_ids = np.argsort(-lg, axis=1)[:, :8]
+    top_vals = np.take_along_axis(lg, top_ids, axis=1)
+    lse = np.log(np.exp(lg - lg.max(1, keepdims=True)).sum(1)) + lg.max(1)
+    return {"rows": rows.numpy().astype(np.float32), "last": lg[-1].astype(np.float32),
+            "top_ids": top_ids.astype(np.int32), "top_vals": top_vals.astype(np.float32),
+            "lse": lse.astype(np.float32)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("HOBBYLM_REFERENCE", ""))
-    ap.add_argument("--only", choices=("all", "bidir"), default="all",
-                    help="bidir: write only the diffusion fixtures (bidirectional logits, greedy sampler ids)")
+    ap.add_argument("--only", choices=("all", "bidir", "embeds"), default="all",
+                    help="bidir: only the diffusion fixtures; embeds: only the inputs_embeds fixture")
     a = ap.parse_args()
     if not a.reference or not os.path.isdir(a.reference):
         raise SystemExit("--reference must point at the HobbyLM checkout")
+    if a.only in ("all", "embeds"):
+        el = reference_torch_embeds_logits(a.reference)
+        np.savez(os.path.join(HERE, "torch_embeds_logits_130M.npz"), **el)
+        print("embeds logits", el["top_ids"].shape)
+        if a.only == "embeds":
+            return
     bl = reference_torch_bidir_logits(a.reference)
     np.savez(os.path.join(HERE, "torch_bidir_logits_130M.npz"), **bl)
     print("bidir logits", bl["top_ids"].shape)

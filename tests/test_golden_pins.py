@@ -89,6 +89,27 @@ def test_oracle_diffusion_loop_matches_reference_sampler(oracle_mod):
         assert [int(t) for t in got] == case["ids"], case["opts"]
 
 
+def test_oracle_rows_match_reference_inputs_embeds(oracle_mod):
+    """Model::prefill and forward_x on caller rows (model.rs:160, 340) against the reference model's
+    inputs_embeds forward (hobbylm/model.py:325-333): 4 rows spliced before 8 token embeddings."""
+    g = np.load(os.path.join(GOLDEN, "torch_embeds_logits_130M.npz"))
+    path = synth.cached_model("130M", 0, quant="f32", rms_eps=1e-6)
+    eng = oracle_mod.Engine(path, quant=False)
+    rows = g["rows"]
+    last = eng.prefill_embeds(eng.new_cache(), rows)
+    rel = np.linalg.norm(last - g["last"]) / np.linalg.norm(g["last"])
+    assert rel < 1e-5, rel
+    c = eng.new_cache()
+    lg = eng.prefill_embeds(c, rows[:1])
+    for pos in range(1, len(rows)):
+        assert np.array_equal(np.argsort(-lg)[:8], g["top_ids"][pos - 1]), pos
+        lse = np.log(np.exp(lg - lg.max()).sum()) + lg.max()
+        assert abs(lse - g["lse"][pos - 1]) < 1e-4, pos
+        lg = eng.forward_x(c, rows[pos], pos)
+    rel = np.linalg.norm(lg - g["last"]) / np.linalg.norm(g["last"])
+    assert rel < 1e-5, rel
+
+
 def test_q8_0_fixture_dequant_matches_gguf_py(oracle_mod):
     """The oracle's Q8_0 dequant (gguf.rs:365-375) equals gguf-py's on a synthetic file's tensor."""
     import gguf
