@@ -7,7 +7,10 @@ The oracle restates hobby-rs (harishsg993010/HobbyLM, hobby-rs/src/{gguf,config,
 lib,sample}.rs); see the header of hobby_oracle.cpp for the per-function citations and arithmetic
 pins. Parity pins: the synthetic-model producer is pinned bit-exactly to the reference's own
 PyTorch init + exporter (tests/golden/synth_digests_*.json) and the oracle's F32 mode is pinned to
-the reference's PyTorch forward (tests/golden/torch_logits_130M.npz). The Q8 path has no reference
+the reference's PyTorch forward: causal (tests/golden/torch_logits_130M.npz), on caller rows
+(torch_embeds_logits_130M.npz) and bidirectional (torch_bidir_logits_130M.npz), and its greedy
+uncached diffusion loop to the reference's own sampler (torch_diffusion_generate_130M.json). The
+Q8 path has no reference
 output to pin against (hobby-rs cannot be built here and has no tests or fixtures for this path):
 its Q8 arithmetic is a restatement of quant.rs and is therefore "parity unpinned" for Q8.
 """
