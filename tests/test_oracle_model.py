@@ -74,3 +74,20 @@ def test_generate_is_prefill_then_greedy_forward(eng):
         out.append(t)
         lg = eng.forward(c, t, 16 + i)
     assert list(toks) == out
+
+
+def test_config2_router_margins_are_logged(oracle_mod, record_property):
+    """The top-k cut of config 2's router (model.rs:270-293): the gap between the 6th and 7th
+    selection scores of every token is recorded (a GPU/oracle selection flip on a near-tie can be
+    told apart from a real fault) and is never an exact tie, where sort order would decide."""
+    inp = synth.moe_op_inputs(seed=2, T=256)
+    moe = oracle_mod.Moe(inp["router"], inp["bias"], inp["gate_exps"], inp["up_exps"], inp["down_exps"],
+                         inp["gate_sh"], inp["up_sh"], inp["down_sh"], top_k=6)
+    margins = []
+    for x in inp["x"]:
+        s = np.sort(moe.sel_scores(x))[::-1]
+        margins.append(float(s[5] - s[6]))
+    record_property("min_top6_top7_margin", min(margins))
+    record_property("median_top6_top7_margin", float(np.median(margins)))
+    print(f"config 2 router: min top-6/7 margin {min(margins):.3e}, median {np.median(margins):.3e}")
+    assert min(margins) > 0.0
