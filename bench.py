@@ -6,9 +6,10 @@
 
 Workload (the headline): the 500M preset, random-init seed 0, Q8_0 GGUF
 (context_length 16384 so prompt + decode fits), 256 sequences with prompt lengths ~ U[1024, 8192]
-of random ids (torch.Generator seed 5). Sequences are sharded round-robin over the ranks with
-replicated weights and no collective on the decode path (strong scaling: the 256 are fixed). A step
-is one batched greedy decode step of every sequence; value = tokens of all ranks / max-over-ranks
+of random ids (torch.Generator seed 5). Sequences are sharded over the ranks with replicated
+weights and no collective on the decode path (strong scaling: the 256 are fixed). A step
+is one batched greedy decode step of every sequence (sequences are placed on ranks balanced by
+prompt length); value = tokens of all ranks / max-over-ranks
 device time. At N=1 the line also carries config 4 (bs1: 2048-token prompt seed 4, 512 greedy
 steps) under "bs1". The reference arm (--impl reference) times the CPU oracle (a C++ restatement
 of hobby-rs, which cannot be built here) on a bounded sample of the same workload.
@@ -58,9 +59,17 @@ def workload(n_seqs: int = N_SEQS, seed: int = 5):
     return prompts
 
 
-def shard(n: int, rank: int, world: int) -> list[int]:
-    """Round-robin assignment of sequence indices to ranks (no collective on the decode path)."""
-    return list(range(rank, n, world))
+def shard(lengths, rank: int, world: int) -> list[int]:
+    """Sequence indices of `rank`: sequences sorted by prompt length (longest first, ties by index)
+    are dealt in snake order (0..w-1, w-1..0, ...), so every rank holds n/world sequences with
+    nearly the same total context, i.e. the same KV bytes per step. No collective on the decode path."""
+    order = sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i))
+    mine = []
+    for j, i in enumerate(order):
+        blk, pos = divmod(j, world)
+        if (pos if blk % 2 == 0 else world - 1 - pos) == rank:
+            mine.append(i)
+    return mine
 
 
 def peaks():
@@ -203,7 +212,7 @@ def run_ours(args):
     torch.cuda.set_device(local)
     path = model_path(rank, world)
     prompts_all = workload(args.seqs)
-    mine = shard(len(prompts_all), rank, world)
+    mine = shard([len(p) for p in prompts_all], rank, world)
     prompts = [prompts_all[i] for i in mine]
     n_local = len(prompts)
     total_steps = args.warmup + 2 * args.steps + 2

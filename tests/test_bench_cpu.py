@@ -52,9 +52,10 @@ def test_reference_arm_other_ranks_exit_without_output():
     assert not [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
 
 
-@pytest.mark.parametrize("n,world", [(256, 1), (256, 2), (256, 8), (5, 3)])
+@pytest.mark.parametrize("n,world", [(256, 1), (256, 2), (256, 8), (5, 3), (0, 2)])
 def test_sequence_shards_partition_the_batch(n, world):
-    parts = [bench.shard(n, r, world) for r in range(world)]
+    lengths = [(i * 7919) % 1000 + 1 for i in range(n)]
+    parts = [bench.shard(lengths, r, world) for r in range(world)]
     assert sorted(i for p in parts for i in p) == list(range(n))
     assert max(map(len, parts)) - min(map(len, parts)) <= 1
 

@@ -26,7 +26,7 @@ def _worker(rank, world, port, q):
 
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
     try:
-        mine = bench.shard(256, rank, world)
+        mine = bench.shard([len(p) for p in bench.workload(256)], rank, world)
         elapsed = 1.0 + rank  # rank 1 is the slowest
         mx = bench.reduce_max(elapsed, world)
         tot = bench.reduce_sum(len(mine) * 32, world)
@@ -59,11 +59,12 @@ def test_two_rank_shard_and_timing_reduction():
 def test_shard_balance(world):
     import bench
 
-    prompts = bench.workload(256)
+    lengths = [len(p) for p in bench.workload(256)]
     loads = []
     for r in range(world):
-        idx = bench.shard(256, r, world)
+        idx = bench.shard(lengths, r, world)
         assert len(idx) == 256 // world
-        loads.append(sum(len(prompts[i]) for i in idx))
-    # round-robin keeps the per-rank KV (and so the step time) within a few percent
-    assert max(loads) / (sum(loads) / world) < 1.1
+        loads.append(sum(lengths[i] for i in idx))
+    # length-sorted snake dealing keeps the per-rank KV (and so the step time) within 0.2%
+    # (round-robin by index left the heaviest of 8 ranks 9.5% above the mean)
+    assert max(loads) / (sum(loads) / world) < 1.002
