@@ -823,74 +823,6 @@ void run_block(hg_engine* e, hg_seq* s, const uint32_t* ids, int n, int n_logits
   if (commit) s->len += n;
 }
 
-// ---------------------------------------------------------------------------------------------
-// Sampling on the host (sample.rs:3-112) for temp > 0 or a repetition penalty.
-// ---------------------------------------------------------------------------------------------
-struct Rng {
-  uint64_t s;
-  explicit Rng(uint64_t seed) : s(seed < 1 ? 1 : seed) {}
-  uint64_t next_u64() {
-    uint64_t x = s;
-    x ^= x >> 12;
-    x ^= x << 25;
-    x ^= x >> 27;
-    s = x;
-    return x * 0x2545F4914F6CDD1Dull;
-  }
-  float next_f32() { return (float)(next_u64() >> 40) / (float)(1ull << 24); }
-};
-
-float exp_pinned(float x) { return (float)std::exp((double)x); }
-
-uint32_t host_argmax(const float* v, int n) {
-  int best = 0;
-  float bv = -INFINITY;
-  for (int i = 0; i < n; i++)
-    if (v[i] > bv) {
-      bv = v[i];
-      best = i;
-    }
-  return (uint32_t)best;
-}
-
-uint32_t host_sample(const float* logits, int n, float temp, float top_p, Rng& rng) {
-  if (temp <= 0.0f) return host_argmax(logits, n);
-  std::vector<std::pair<int, float>> pr(n);
-  float m = -INFINITY;
-  for (int i = 0; i < n; i++) {
-    pr[i] = {i, logits[i] / temp};
-    m = std::fmax(m, pr[i].second);
-  }
-  float sum = 0.0f;
-  for (auto& p : pr) {
-    p.second = exp_pinned(p.second - m);
-    sum += p.second;
-  }
-  for (auto& p : pr) p.second /= sum;
-  if (top_p > 0.0f && top_p < 1.0f) {
-    std::stable_sort(pr.begin(), pr.end(), [](const auto& a, const auto& b) { return a.second > b.second; });
-    float cum = 0.0f;
-    size_t cut = pr.size();
-    for (size_t i = 0; i < pr.size(); i++) {
-      cum += pr[i].second;
-      if (cum >= top_p) {
-        cut = i + 1;
-        break;
-      }
-    }
-    pr.resize(cut);
-    float s = -0.0f;
-    for (auto& p : pr) s = s + p.second;
-    for (auto& p : pr) p.second /= s;
-  }
-  float r = rng.next_f32(), cum = 0.0f;
-  for (auto& p : pr) {
-    cum += p.second;
-    if (r < cum) return (uint32_t)p.first;
-  }
-  return pr.empty() ? 0 : (uint32_t)pr.back().first;
-}
-
 hg_seq* seq_create(hg_engine* e, int max_ctx) {
   if (max_ctx <= 0 || max_ctx > e->cfg.context_length) max_ctx = e->cfg.context_length;
   if (e->free_rows.empty()) throw Error(HG_ERR_POOL_EXHAUSTED, "too many live sequences");
@@ -955,76 +887,6 @@ int generate(hg_engine* e, const uint32_t* ids, int n, const hg_gen_opts* opts, 
 // Diffusion decode (lib.rs:164-495): blocks of [MASK] ids filled over denoising passes of
 // run_block on the GPU; each pass's block logits are scored on the host.
 // ---------------------------------------------------------------------------------------------
-float log_pinned(float x) { return (float)std::log((double)x); }
-
-// sample.rs:29-47: Gumbel-max over the finite logits; temp <= 0 is the plain argmax.
-uint32_t gumbel_argmax(const float* l, int n, float temp, Rng& rng) {
-  if (temp <= 0.0f) return host_argmax(l, n);
-  int best = 0;
-  float bv = -INFINITY;
-  for (int i = 0; i < n; i++) {
-    if (!std::isfinite(l[i])) continue;
-    float u = std::clamp(rng.next_f32(), 1e-9f, 1.0f - 1e-9f);
-    float val = l[i] / temp + -log_pinned(-log_pinned(u));
-    if (val > bv) {
-      bv = val;
-      best = i;
-    }
-  }
-  return (uint32_t)best;
-}
-
-// lib.rs:66-73: n unmask events spread over `steps` (sums to n).
-std::vector<int> num_transfer(int n, int steps) {
-  const int base = n / steps;
-  std::vector<int> out(steps, base);
-  for (int i = 0; i < n - base * steps; i++) out[i] += 1;
-  return out;
-}
-
-// lib.rs:221-263 (score_block): per block row, ids >= valid banned, the presence penalty over the
-// committed ids and the block's own non-mask ids, a Gumbel / greedy pick, and the softmax
-// probabilities (ops.rs:112-128) of the pick (pconf) and of the row's current id (cconf). Rows are
-// independent except for the Gumbel draws, which take one RNG stream row after row.
-void score_block(const float* all, int V, const uint32_t* blk, int blk_len, const uint32_t* committed,
-                 int n_committed, int valid, uint32_t mask, float rep_penalty, float temp, Rng& rng, uint32_t* pred,
-                 float* pconf, float* cconf, std::vector<float>& rows) {
-  std::vector<char> present(valid, 0);
-  if (rep_penalty != 1.0f)
-    for (int i = 0; i < n_committed + blk_len; i++) {
-      uint32_t id = i < n_committed ? committed[i] : blk[i - n_committed];
-      if (id != mask && (int64_t)id < valid) present[id] = 1;
-    }
-  rows.resize((size_t)blk_len * V);
-#pragma omp parallel for schedule(static)
-  for (int i = 0; i < blk_len; i++) {
-    float* row = rows.data() + (size_t)i * V;
-    memcpy(row, all + (size_t)i * V, (size_t)V * 4);
-    for (int l = valid; l < V; l++) row[l] = -INFINITY;
-    if (rep_penalty != 1.0f)
-      for (int t = 0; t < valid; t++)
-        if (present[t]) {
-          float l = row[t];
-          row[t] = l > 0.0f ? l / rep_penalty : l * rep_penalty;
-        }
-    if (temp <= 0.0f) pred[i] = host_argmax(row, V);
-  }
-  if (temp > 0.0f)
-    for (int i = 0; i < blk_len; i++) pred[i] = gumbel_argmax(rows.data() + (size_t)i * V, V, temp, rng);
-#pragma omp parallel for schedule(static)
-  for (int i = 0; i < blk_len; i++) {
-    const float* row = rows.data() + (size_t)i * V;
-    float m = -INFINITY;
-    for (int k = 0; k < V; k++)
-      if (row[k] > m) m = row[k];
-    float sum = 0.0f;
-    for (int k = 0; k < V; k++) sum += exp_pinned(row[k] - m);
-    const float inv = 1.0f / sum;
-    pconf[i] = exp_pinned(row[pred[i]] - m) * inv;
-    cconf[i] = exp_pinned(row[blk[i]] - m) * inv;
-  }
-}
-
 // The unmasking passes shared by both paths for one block (lib.rs:304-384 / 425-471): `ids` are
 // the block's current ids, `step` runs one scored pass over them.
 template <class Step>

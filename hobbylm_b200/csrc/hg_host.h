@@ -77,4 +77,30 @@ int host_q8_ss(int64_t cols);
 // RoPE cos/sin tables in f64 (ops.rs:139-154).
 void rope_tables(int head_dim, int max_pos, float theta, float* cos_out, float* sin_out);
 
+// ---- host-side token selection (sampler.cpp) ----
+// xorshift64* (sample.rs:3-22); Rng::new(seed) keeps seed.max(1).
+struct Rng {
+  uint64_t s;
+  explicit Rng(uint64_t seed) : s(seed < 1 ? 1 : seed) {}
+  uint64_t next_u64() {
+    uint64_t x = s;
+    x ^= x >> 12;
+    x ^= x << 25;
+    x ^= x >> 27;
+    s = x;
+    return x * 0x2545F4914F6CDD1Dull;
+  }
+  float next_f32() { return (float)(next_u64() >> 40) / (float)(1ull << 24); }
+};
+// f32::exp / f32::ln pinned to the correctly rounded double results.
+float exp_pinned(float x);
+float log_pinned(float x);
+uint32_t host_argmax(const float* v, int n);
+uint32_t host_sample(const float* logits, int n, float temp, float top_p, Rng& rng);
+uint32_t gumbel_argmax(const float* l, int n, float temp, Rng& rng);
+std::vector<int> num_transfer(int n, int steps);
+void score_block(const float* all, int V, const uint32_t* blk, int blk_len, const uint32_t* committed,
+                 int n_committed, int valid, uint32_t mask, float rep_penalty, float temp, Rng& rng, uint32_t* pred,
+                 float* pconf, float* cconf, std::vector<float>& rows);
+
 }  // namespace hg

@@ -199,6 +199,20 @@ int hg_q8_scale_stride(int64_t cols);
 /* Inverse of the lane-chunked byte permutation (for tests): packed row bytes -> reference order. */
 int hg_q8_unpack_qs(const int8_t* packed, int64_t rows, int64_t cols, int8_t* qs_out);
 
+/* ---- host-side token selection over logits in host memory (no GPU work) ---- */
+
+/* sample.rs:66-112 over n logits (temp <= 0: the first-max argmax, sample.rs:53-64): softmax of
+ * logits / temp, the top-p prefix (probabilities descending, ties by id) when 0 < top_p < 1, one
+ * draw. *rng_state is the xorshift64* state (sample.rs:3-22; start it at the seed) and is advanced. */
+int hg_host_sample(const float* logits, int n, float temp, float top_p, uint64_t* rng_state, uint32_t* out);
+/* The diffusion block scoring of lib.rs:221-263 over blk_len rows of vocab logits: ids >= 50257
+ * banned, the presence penalty over the committed ids and the block's non-mask ids, the pick
+ * (Gumbel-max at temp > 0, sample.rs:29-47, drawing from *rng_state row after row) and the
+ * softmax probabilities of the pick (pconf) and of the row's current id (cconf). */
+int hg_host_score_block(const float* logits, int vocab, const uint32_t* blk, int blk_len, const uint32_t* committed,
+                        int n_committed, uint32_t mask, float rep_penalty, float temp, uint64_t* rng_state,
+                        uint32_t* pred, float* pconf, float* cconf);
+
 /* ---- kernel-level ops (device pointers) ---- */
 
 /* Q8Tensor::matvec (quant.rs:106-136) for ntok activation rows: y[t][r] = row r of the packed

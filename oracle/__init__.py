@@ -72,6 +72,8 @@ def lib():
         "hor_prefill_embeds": (i, [vp, vp, f32p, i, f32p]),
         "hor_forward_x": (i, [vp, vp, f32p, i, f32p]),
         "hor_run_block": (i, [vp, vp, u32p, i, i, vp]),
+        "hor_sample": (i, [f32p, i, f, f, C.POINTER(C.c_uint64), C.POINTER(C.c_uint32)]),
+        "hor_score_block": (i, [f32p, i, u32p, i, vp, i, C.c_uint32, f, f, C.POINTER(C.c_uint64), u32p, f32p, f32p]),
         "hor_forward_bidir": (i, [vp, u32p, i, f32p]),
         "hor_generate_diffusion": (i, [vp, u32p, i, i, i, i, f, f, i, f, C.c_uint64, i, f, u32p, C.POINTER(i)]),
         "hor_forward": (i, [vp, vp, C.c_uint32, i, f32p]),
@@ -318,6 +320,27 @@ def rmsnorm(x, w, eps) -> np.ndarray:
 
 def expf(x: float) -> float:
     return float(lib().hor_expf(x))
+
+
+def sample(logits, temp: float, top_p: float, state: int) -> tuple[int, int]:
+    """sample.rs:66-112; returns (id, advanced xorshift64* state)."""
+    st, out = C.c_uint64(state), C.c_uint32()
+    _check(lib().hor_sample(np.ascontiguousarray(logits, np.float32), len(logits), temp, top_p, C.byref(st),
+                            C.byref(out)))
+    return int(out.value), int(st.value)
+
+
+def score_block(logits, blk, committed, mask: int, rep_penalty: float, temp: float, state: int):
+    """lib.rs:221-263 over rows of logits [blk_len][vocab]; returns (pred, pconf, cconf, state)."""
+    logits = np.ascontiguousarray(logits, np.float32)
+    blk = np.ascontiguousarray(blk, np.uint32)
+    committed = np.ascontiguousarray(committed, np.uint32)
+    n = len(blk)
+    pred, pconf, cconf = np.zeros(n, np.uint32), np.zeros(n, np.float32), np.zeros(n, np.float32)
+    st = C.c_uint64(state)
+    _check(lib().hor_score_block(logits, logits.shape[1], blk, n, committed.ctypes.data if len(committed) else None,
+                                 len(committed), mask, rep_penalty, temp, C.byref(st), pred, pconf, cconf))
+    return pred, pconf, cconf, int(st.value)
 
 
 class Moe:

@@ -1746,6 +1746,27 @@ int hor_generate_diffusion(void* ep, const uint32_t* ids, int n, int gen_len, in
   })
 }
 
+// sample.rs:66-112 over n logits with the xorshift64* state in *state (advanced).
+int hor_sample(const float* logits, int n, float temp, float top_p, uint64_t* state, uint32_t* out) {
+  HOR_TRY({
+    Rng rng(*state);
+    *out = sample(logits, n, temp, top_p, rng);
+    *state = rng.s;
+  })
+}
+
+// lib.rs:221-263 (score_block) over blk_len rows of vocab logits, valid = min(50257, vocab).
+int hor_score_block(const float* logits, int vocab, const uint32_t* blk, int blk_len, const uint32_t* committed,
+                    int n_committed, uint32_t mask, float rep_penalty, float temp, uint64_t* state, uint32_t* pred,
+                    float* pconf, float* cconf) {
+  HOR_TRY({
+    Rng rng(*state);
+    score_block(logits, vocab, blk, blk_len, committed, n_committed, std::min(50257, vocab), mask, rep_penalty, temp,
+                rng, pred, pconf, cconf);
+    *state = rng.s;
+  })
+}
+
 int hor_last_routing(void* ep, int32_t* sel, float* w) {
   HOR_TRY({
     Engine* e = (Engine*)ep;
