@@ -25,45 +25,85 @@ uint32_t host_argmax(const float* v, int n) {
   return (uint32_t)best;
 }
 
+// Ids of n probabilities (all >= 0) in descending order, equal values by ascending id: the order
+// of a stable descending sort. Non-negative floats order like their bit patterns, so the key
+// (~bits << 16 | id) sorted ascending gives it; the keys start in id order, so an LSD radix sort
+// needs only the two 16-bit digits of the probability. Longer inputs fall back to a stable sort.
+static void order_desc(const float* p, int n, std::vector<int>& idx) {
+  idx.resize(n);
+  if (n > 65536) {
+    for (int i = 0; i < n; i++) idx[i] = i;
+    std::stable_sort(idx.begin(), idx.end(), [p](int a, int b) { return p[a] > p[b]; });
+    return;
+  }
+  std::vector<uint64_t> a(n), b(n);
+  for (int i = 0; i < n; i++) {
+    uint32_t bits;
+    std::memcpy(&bits, p + i, 4);
+    a[i] = ((uint64_t)(0xFFFFFFFFu - bits) << 16) | (uint64_t)i;
+  }
+  std::vector<uint32_t> cnt(65536);
+  for (int shift = 16; shift <= 32; shift += 16) {
+    std::fill(cnt.begin(), cnt.end(), 0u);
+    for (int i = 0; i < n; i++) cnt[(a[i] >> shift) & 0xFFFF]++;
+    uint32_t acc = 0;
+    for (auto& c : cnt) {
+      uint32_t v = c;
+      c = acc;
+      acc += v;
+    }
+    for (int i = 0; i < n; i++) b[cnt[(a[i] >> shift) & 0xFFFF]++] = a[i];
+    a.swap(b);
+  }
+  for (int i = 0; i < n; i++) idx[i] = (int)(a[i] & 0xFFFF);
+}
+
 // sample.rs:66-112: softmax of logits / temp, then (0 < top_p < 1) the smallest prefix of the
 // probabilities in descending order (ties by id) whose running sum reaches top_p, renormalised,
-// and one uniform draw walked over it.
+// and one uniform draw walked over it. The exponentials and divisions run in parallel; every sum
+// keeps the reference's order (the denominator by id, the nucleus sums in sorted order).
 uint32_t host_sample(const float* logits, int n, float temp, float top_p, Rng& rng) {
   if (temp <= 0.0f) return host_argmax(logits, n);
-  std::vector<std::pair<int, float>> pr(n);
+  std::vector<float> p(n);
   float m = -INFINITY;
+#pragma omp parallel for reduction(max : m) schedule(static)
   for (int i = 0; i < n; i++) {
-    pr[i] = {i, logits[i] / temp};
-    m = std::fmax(m, pr[i].second);
+    p[i] = logits[i] / temp;
+    m = std::fmax(m, p[i]);
   }
+#pragma omp parallel for schedule(static)
+  for (int i = 0; i < n; i++) p[i] = exp_pinned(p[i] - m);
   float sum = 0.0f;
-  for (auto& p : pr) {
-    p.second = exp_pinned(p.second - m);
-    sum += p.second;
-  }
-  for (auto& p : pr) p.second /= sum;
+  for (int i = 0; i < n; i++) sum += p[i];
+#pragma omp parallel for schedule(static)
+  for (int i = 0; i < n; i++) p[i] /= sum;
   if (top_p > 0.0f && top_p < 1.0f) {
-    std::stable_sort(pr.begin(), pr.end(), [](const auto& a, const auto& b) { return a.second > b.second; });
+    std::vector<int> idx;
+    order_desc(p.data(), n, idx);
     float cum = 0.0f;
-    size_t cut = pr.size();
-    for (size_t i = 0; i < pr.size(); i++) {
-      cum += pr[i].second;
+    int cut = n;
+    for (int j = 0; j < n; j++) {
+      cum += p[idx[j]];
       if (cum >= top_p) {
-        cut = i + 1;
+        cut = j + 1;
         break;
       }
     }
-    pr.resize(cut);
     float s = -0.0f;
-    for (auto& p : pr) s = s + p.second;
-    for (auto& p : pr) p.second /= s;
+    for (int j = 0; j < cut; j++) s = s + p[idx[j]];
+    float r = rng.next_f32(), c2 = 0.0f;
+    for (int j = 0; j < cut; j++) {
+      c2 += p[idx[j]] / s;
+      if (r < c2) return (uint32_t)idx[j];
+    }
+    return (uint32_t)idx[cut - 1];
   }
   float r = rng.next_f32(), cum = 0.0f;
-  for (auto& p : pr) {
-    cum += p.second;
-    if (r < cum) return (uint32_t)p.first;
+  for (int i = 0; i < n; i++) {
+    cum += p[i];
+    if (r < cum) return (uint32_t)i;
   }
-  return pr.empty() ? 0 : (uint32_t)pr.back().first;
+  return (uint32_t)(n - 1);
 }
 
 // sample.rs:29-47: Gumbel-max over the finite logits; temp <= 0 is the plain argmax.
@@ -118,8 +158,36 @@ void score_block(const float* all, int V, const uint32_t* blk, int blk_len, cons
         }
     if (temp <= 0.0f) pred[i] = host_argmax(row, V);
   }
-  if (temp > 0.0f)
-    for (int i = 0; i < blk_len; i++) pred[i] = gumbel_argmax(rows.data() + (size_t)i * V, V, temp, rng);
+  if (temp > 0.0f) {
+    // gumbel_argmax row after row: the draws, one per finite logit, are taken in that order
+    // first (the cheap sequential part); the two logarithms per draw and the argmax then run in
+    // parallel with the same first-maximum rule.
+    std::vector<size_t> off(blk_len + 1, 0);
+    for (int i = 0; i < blk_len; i++) {
+      const float* row = rows.data() + (size_t)i * V;
+      size_t c = 0;
+      for (int k = 0; k < V; k++) c += std::isfinite(row[k]) ? 1 : 0;
+      off[i + 1] = off[i] + c;
+    }
+    std::vector<float> u(off[blk_len]);
+    for (size_t j = 0; j < u.size(); j++) u[j] = std::clamp(rng.next_f32(), 1e-9f, 1.0f - 1e-9f);
+#pragma omp parallel for schedule(static)
+    for (int i = 0; i < blk_len; i++) {
+      const float* row = rows.data() + (size_t)i * V;
+      size_t j = off[i];
+      int best = 0;
+      float bv = -INFINITY;
+      for (int k = 0; k < V; k++) {
+        if (!std::isfinite(row[k])) continue;
+        const float val = row[k] / temp + -log_pinned(-log_pinned(u[j++]));
+        if (val > bv) {
+          bv = val;
+          best = k;
+        }
+      }
+      pred[i] = (uint32_t)best;
+    }
+  }
 #pragma omp parallel for schedule(static)
   for (int i = 0; i < blk_len; i++) {
     const float* row = rows.data() + (size_t)i * V;
