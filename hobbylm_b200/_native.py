@@ -26,7 +26,7 @@ EXPORTS = (
     "hg_q8_pack", "hg_q8_scale_stride", "hg_q8_unpack_qs", "hg_op_q8_matvec", "hg_op_q8_matmul",
     "hg_op_moe_scratch_bytes", "hg_op_moe_ffn", "hg_op_kv_attn_scratch_bytes", "hg_op_kv_attn", "hg_rope_tables",
     "hg_decode_greedy", "hg_engine_stream", "hg_decode_kernel_count", "hg_debug_time_attention",
-    "hg_op_q8_matvec_noalloc", "hg_host_sample", "hg_host_score_block",
+    "hg_op_q8_matvec_noalloc", "hg_host_sample", "hg_host_score_block", "hg_generate_embeds",
 )
 NOALLOC_SCRATCH_BYTES = 4 << 20  # HG_NOALLOC_SCRATCH_BYTES
 
@@ -115,6 +115,7 @@ def lib():
         "hg_forward_x": (i32, [vp, vp, vp, vp, vp]),
         "hg_decode_batch": (i32, [vp, vp, i32, vp, vp, vp]),
         "hg_generate": (i32, [vp, vp, i32, C.POINTER(GenOptsC), TOKEN_CB, vp, vp]),
+        "hg_generate_embeds": (i32, [vp, vp, i32, vp, i32, C.POINTER(GenOptsC), TOKEN_CB, vp, vp]),
         "hg_run_block": (i32, [vp, vp, vp, i32, i32, i32, vp]),
         "hg_host_sample": (i32, [vp, i32, f32, f32, C.POINTER(u64), vp]),
         "hg_host_score_block": (i32, [vp, i32, vp, i32, vp, i32, u32, f32, f32, C.POINTER(u64), vp, vp, vp]),

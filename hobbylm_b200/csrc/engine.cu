@@ -845,18 +845,24 @@ void seq_free(hg_seq* s) {
   delete s;
 }
 
-int generate(hg_engine* e, const uint32_t* ids, int n, const hg_gen_opts* opts, hg_token_cb cb, void* user,
-             uint32_t* out_ids) {
+// Engine::generate (lib.rs:107-162): n_rows caller rows of d_model floats (lib.rs:118-121's
+// embeds; host memory) and then the n prompt ids are prefilled (two prefills over consecutive
+// positions equal one), followed by the sampling loop.
+int generate(hg_engine* e, const float* rows, int n_rows, const uint32_t* ids, int n, const hg_gen_opts* opts,
+             hg_token_cb cb, void* user, uint32_t* out_ids) {
   hg_gen_opts o = opts ? *opts : hg_gen_opts{256, 0.0f, 0.95f, 1234, 1.0f};
-  if (n <= 0) return 0;
+  if (n < 0 || n_rows < 0) throw Error(HG_ERR_INVALID, "negative length");
+  if (n + n_rows == 0) return 0;  // lib.rs:122-124
   std::unique_ptr<hg_seq, void (*)(hg_seq*)> s(seq_create(e, e->cfg.context_length), seq_free);
   const int V = e->cfg.vocab_size, valid = std::min(50257, V);
   const bool host_path = o.temp > 0.0f || o.rep_penalty != 1.0f;
   std::vector<float> logits(host_path ? V : 0);
   Rng rng(o.seed);
   uint32_t gpu_next = 0;
-  prefill(e, s.get(), ids, nullptr, n, host_path ? logits.data() : nullptr, &gpu_next);
-  int pos = n, count = 0;
+  if (n_rows > 0)
+    prefill(e, s.get(), nullptr, rows, n_rows, n == 0 && host_path ? logits.data() : nullptr, &gpu_next);
+  if (n > 0) prefill(e, s.get(), ids, nullptr, n, host_path ? logits.data() : nullptr, &gpu_next);
+  int pos = n_rows + n, count = 0;
   std::vector<uint32_t> out;
   for (int it = 0; it < o.max_new; it++) {
     uint32_t next;
@@ -1255,7 +1261,23 @@ int hg_generate(hg_engine* e, const uint32_t* ids, int n, const hg_gen_opts* opt
   try {
     need(e && (ids || n == 0), "null argument");
     DeviceGuard g(e->device);
-    return generate(e, ids, n, opts, cb, user, out_ids);
+    if (n <= 0) return 0;
+    return generate(e, nullptr, 0, ids, n, opts, cb, user, out_ids);
+  } catch (const ::hg::Error& ex) {
+    set_last_error(ex.what());
+    return ex.code;
+  } catch (const std::exception& ex) {
+    set_last_error(ex.what());
+    return HG_ERR_INVALID;
+  }
+}
+
+int hg_generate_embeds(hg_engine* e, const float* embeds, int n_embeds, const uint32_t* ids, int n,
+                       const hg_gen_opts* opts, hg_token_cb cb, void* user, uint32_t* out_ids) {
+  try {
+    need(e && (embeds || n_embeds == 0) && (ids || n == 0), "null argument");
+    DeviceGuard g(e->device);
+    return generate(e, embeds, n_embeds, ids, n, opts, cb, user, out_ids);
   } catch (const ::hg::Error& ex) {
     set_last_error(ex.what());
     return ex.code;

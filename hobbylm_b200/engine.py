@@ -248,10 +248,14 @@ class Engine:
         return [int(t) for t in out[:n]]
 
     def generate(self, prompt_ids: Iterable[int], opts: GenOpts | None = None,
-                 on_token: Callable[[int], bool] | None = None) -> list[int]:
-        """Engine::generate (lib.rs:107-162) on token ids. on_token(id) returns False to stop."""
+                 on_token: Callable[[int], bool] | None = None, embeds=None) -> list[int]:
+        """Engine::generate (lib.rs:107-162) on token ids. on_token(id) returns False to stop.
+        embeds: optional [n][d_model] rows prefilled before the prompt (lib.rs:118-121)."""
         opts = opts or GenOpts()
         ids = _u32(list(prompt_ids))
+        rows = None
+        if embeds is not None:
+            rows = np.ascontiguousarray(embeds, dtype=np.float32).reshape(-1, self.cfg["d_model"])
         out = np.empty(max(opts.max_new, 1), np.uint32)
         err: list[BaseException] = []
 
@@ -266,7 +270,12 @@ class Engine:
 
         cfun = TOKEN_CB(cb)
         o = opts.c()
-        n = check(lib().hg_generate(self.h, ids.ctypes.data, len(ids), C.byref(o), cfun, None, out.ctypes.data))
+        if rows is None:
+            n = check(lib().hg_generate(self.h, ids.ctypes.data, len(ids), C.byref(o), cfun, None, out.ctypes.data))
+        else:
+            n = check(lib().hg_generate_embeds(self.h, rows.ctypes.data if len(rows) else None, len(rows),
+                                               ids.ctypes.data if len(ids) else None, len(ids), C.byref(o), cfun,
+                                               None, out.ctypes.data))
         if err:
             raise err[0]
         return [int(t) for t in out[:n]]

@@ -165,6 +165,11 @@ int hg_debug_time_attention(hg_engine* e, hg_seq** seqs, int n, int iters, float
  * out_ids (may be NULL) receives up to opts->max_new ids. Returns the count (>= 0) or an error. */
 int hg_generate(hg_engine* e, const uint32_t* ids, int n, const hg_gen_opts* opts, hg_token_cb cb, void* user,
                 uint32_t* out_ids);
+/* Engine::generate (lib.rs:107-162) with `embeds`: n_embeds caller rows of d_model floats (host
+ * memory, e.g. modality vectors) precede the prompt ids' embeddings in the prefill
+ * (lib.rs:118-121); either part may be empty. Otherwise as hg_generate. */
+int hg_generate_embeds(hg_engine* e, const float* embeds, int n_embeds, const uint32_t* ids, int n,
+                       const hg_gen_opts* opts, hg_token_cb cb, void* user, uint32_t* out_ids);
 
 /* Model::run_block (model.rs:472-510): n token ids at positions hg_seq_len(s).. attend to the
  * sequence's prefix and to every one of the n rows (bidirectional within the block), with the

@@ -75,6 +75,7 @@ def lib():
         "hor_sample": (i, [f32p, i, f, f, C.POINTER(C.c_uint64), C.POINTER(C.c_uint32)]),
         "hor_score_block": (i, [f32p, i, u32p, i, vp, i, C.c_uint32, f, f, C.POINTER(C.c_uint64), u32p, f32p, f32p]),
         "hor_forward_bidir": (i, [vp, u32p, i, f32p]),
+        "hor_generate_embeds": (i, [vp, f32p, i, vp, i, i, f, f, C.c_uint64, f, u32p, C.POINTER(i)]),
         "hor_generate_diffusion": (i, [vp, u32p, i, i, i, i, f, f, i, f, C.c_uint64, i, f, u32p, C.POINTER(i)]),
         "hor_forward": (i, [vp, vp, C.c_uint32, i, f32p]),
         "hor_last_routing": (i, [vp, i32p, f32p]),
@@ -186,6 +187,17 @@ class Engine:
         out = np.zeros(self.vocab, np.float32)
         _check(lib().hor_forward(self.h, cache.h, int(token), int(pos), out))
         return out
+
+    def generate_embeds(self, rows, ids, max_new: int, temp: float = 0.0, top_p: float = 0.95, seed: int = 1234,
+                        rep_penalty: float = 1.0) -> np.ndarray:
+        """Engine::generate with embeds (lib.rs:107-126): rows [n][d_model] before the prompt ids."""
+        rows = np.ascontiguousarray(rows, dtype=np.float32).reshape(-1, self.cfg["d_model"])
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        out = np.zeros(max(max_new, 1), np.uint32)
+        n = C.c_int()
+        _check(lib().hor_generate_embeds(self.h, rows, rows.shape[0], ids.ctypes.data if len(ids) else None, len(ids),
+                                         max_new, temp, top_p, seed, rep_penalty, out, C.byref(n)))
+        return out[:n.value].copy()
 
     def run_block(self, cache: "Cache", ids, commit: bool = False, want_logits: bool = True):
         """Model::run_block (model.rs:472-510) at base = len(cache): logits [n][vocab] (or None);

@@ -1778,24 +1778,26 @@ int hor_last_routing(void* ep, int32_t* sel, float* w) {
 // Engine::generate on token ids (lib.rs:107-162). Writes generated ids to out_ids (max_new), the
 // logits each sampled token was chosen from to out_logits ([max_new][vocab], may be null), and the
 // wall time of the forward() calls to *forward_s. Returns the count via *n_out.
-int hor_generate(void* ep, const uint32_t* ids, int n, int max_new, float temp, float top_p, uint64_t seed,
-                 float rep_penalty, uint32_t* out_ids, float* out_logits, int* n_out, double* forward_s,
-                 double* prefill_s) {
+static int generate_rows(Engine* e, const float* rows, int n_rows, const uint32_t* ids, int n, int max_new,
+                         float temp, float top_p, uint64_t seed, float rep_penalty, uint32_t* out_ids,
+                         float* out_logits, int* n_out, double* forward_s, double* prefill_s) {
   HOR_TRY({
-    Engine* e = (Engine*)ep;
     const Config& c = e->cfg;
     int V = c.vocab_size, d = c.d_model;
     *n_out = 0;
     if (forward_s) *forward_s = 0;
-    if (n <= 0) return 0;
+    if (n + n_rows <= 0) return 0;  // lib.rs:122-124
     KvCache cache;
     e->model.new_cache(cache);
     Rng rng(seed);
-    std::vector<float> in((size_t)n * d), logits(V);
+    // lib.rs:118-121: the caller's rows first, then the prompt's token embeddings
+    std::vector<float> in((size_t)(n_rows + n) * d), logits(V);
+    if (n_rows > 0) memcpy(in.data(), rows, (size_t)n_rows * d * 4);
     for (int t = 0; t < n; t++) {
       if ((int64_t)ids[t] >= V) throw Error("token id out of range");
-      memcpy(&in[(size_t)t * d], &e->model.token_embd[(size_t)ids[t] * d], d * 4);
+      memcpy(&in[(size_t)(n_rows + t) * d], &e->model.token_embd[(size_t)ids[t] * d], d * 4);
     }
+    n += n_rows;
     int pos = n;
     auto t0 = std::chrono::steady_clock::now();
     e->model.prefill(in.data(), n, cache, logits.data());
@@ -1824,6 +1826,26 @@ int hor_generate(void* ep, const uint32_t* ids, int n, int max_new, float temp, 
     *n_out = (int)outv.size();
     if (forward_s) *forward_s = fs;
   })
+}
+
+int hor_generate(void* ep, const uint32_t* ids, int n, int max_new, float temp, float top_p, uint64_t seed,
+                 float rep_penalty, uint32_t* out_ids, float* out_logits, int* n_out, double* forward_s,
+                 double* prefill_s) {
+  if (n <= 0) {
+    *n_out = 0;
+    if (forward_s) *forward_s = 0;
+    return 0;
+  }
+  return generate_rows((Engine*)ep, nullptr, 0, ids, n, max_new, temp, top_p, seed, rep_penalty, out_ids, out_logits,
+                       n_out, forward_s, prefill_s);
+}
+
+// Engine::generate with `embeds` (lib.rs:107-126): n_rows caller rows of d_model floats precede the
+// prompt ids' embeddings in one prefill.
+int hor_generate_embeds(void* ep, const float* rows, int n_rows, const uint32_t* ids, int n, int max_new, float temp,
+                        float top_p, uint64_t seed, float rep_penalty, uint32_t* out_ids, int* n_out) {
+  return generate_rows((Engine*)ep, rows, n_rows, ids, n, max_new, temp, top_p, seed, rep_penalty, out_ids, nullptr,
+                       n_out, nullptr, nullptr);
 }
 
 // Append synthetic K/V rows ([n][kv_dim] per layer, all layers share the arrays) to a cache, for

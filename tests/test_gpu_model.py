@@ -242,6 +242,19 @@ def test_forward_x_matches_forward_and_oracle(engine130, oracle130, model130, na
             pos, tok = pos + 1, nxt
 
 
+def test_generate_with_embeds_matches_oracle(engine130, oracle130):
+    """Engine::generate with `embeds` (lib.rs:107-126): caller rows before the prompt ids, greedy and
+    sampled, and rows alone, token for token against the oracle's single prefill over all inputs."""
+    d = engine130.cfg["d_model"]
+    rows = (np.random.default_rng(31).standard_normal((3, d)) * 0.02).astype(np.float32)
+    ids = synth.prompt_ids(20, 32)
+    for o in (GenOpts(max_new=12), GenOpts(max_new=12, temp=0.8, top_p=0.9, seed=5, rep_penalty=1.2)):
+        ref = oracle130.generate_embeds(rows, ids, o.max_new, o.temp, o.top_p, o.seed, o.rep_penalty)
+        assert engine130.generate(ids, o, embeds=rows) == [int(t) for t in ref]
+    ref = oracle130.generate_embeds(rows, [], 6)
+    assert engine130.generate([], GenOpts(max_new=6), embeds=rows) == [int(t) for t in ref]
+
+
 def test_errors(engine130, model130):
     from hobbylm_b200 import Engine
 

@@ -70,3 +70,12 @@ def test_host_sampling_errors(native):
     p, f1, f2 = np.zeros(1, np.uint32), np.zeros(1, np.float32), np.zeros(1, np.float32)
     assert lib.hg_host_score_block(x.ctypes.data, 8, blk.ctypes.data, 1, None, 0, 7, 1.0, 0.0, C.byref(st),
                                    p.ctypes.data, f1.ctypes.data, f2.ctypes.data) == -8
+
+
+def test_generate_embeds_binding_rejects_null_engine(native):
+    """hg_generate_embeds checks its arguments before any GPU work (the call works without a GPU)."""
+    rows = np.zeros((2, 8), np.float32)
+    out = np.zeros(4, np.uint32)
+    rc = native.lib().hg_generate_embeds(None, rows.ctypes.data, 2, None, 0, None, native.TOKEN_CB(lambda t, u: 1),
+                                         None, out.ctypes.data)
+    assert rc == -1 and b"null argument" in native.lib().hg_last_error()

@@ -91,3 +91,13 @@ def test_config2_router_margins_are_logged(oracle_mod, record_property):
     record_property("median_top6_top7_margin", float(np.median(margins)))
     print(f"config 2 router: min top-6/7 margin {min(margins):.3e}, median {np.median(margins):.3e}")
     assert min(margins) > 0.0
+
+
+def test_generate_with_embedding_rows_is_generate_of_ids(eng, emb):
+    """lib.rs:118-121: `embeds` rows that are the prompt's own token embeddings, ahead of the rest of
+    the prompt (or instead of it), generate exactly what the ids do."""
+    ids = synth.prompt_ids(16, 25)
+    a, _, _, _ = eng.generate(ids, 8, rep_penalty=1.3)
+    b = eng.generate_embeds(emb[ids[:5]], ids[5:], 8, rep_penalty=1.3)
+    c = eng.generate_embeds(emb[ids], [], 8, rep_penalty=1.3)
+    assert list(a) == list(b) == list(c)
