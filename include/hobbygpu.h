@@ -12,7 +12,7 @@
  *
  * The reference (harishsg993010/HobbyLM, hobby-rs) is a Rust crate with no FFI; each entry point
  * below names the Rust item (file:line) whose behaviour it takes over. A Rust caller binds them
- * with an `extern "C"` block (see INTEGRATION.md).
+ * with an `extern "C"` block.
  */
 #ifndef HOBBYGPU_H
 #define HOBBYGPU_H
@@ -197,8 +197,9 @@ int hg_debug_last_routing(hg_engine* e, int slot, int32_t* sel);
 /* ---- host-side weight packing (the load-time re-quantization, usable without a GPU) ---- */
 
 /* Q8Tensor::quantize (quant.rs:78-102) of a row-major f32 [rows][cols] matrix into the device
- * layout: qs_out [rows][cols] int8 (lane-chunked), scales_out [rows][scale_stride]
- * f32 with scale_stride = hg_q8_scale_stride(cols). */
+ * layout: qs_out [rows][cols] int8 in the lane-chunked order (for 32-blocks 4c..4c+3 of a row, byte
+ * c*128 + l*16 + (b%4)*4 + j holds element 32b + 4l + j; the blocks b >= 4nc, nc = cols / 128,
+ * follow as nc*128 + (b-4nc)*32 + l*4 + j), scales_out [rows][scale_stride] f32 with scale_stride = hg_q8_scale_stride(cols). */
 int hg_q8_pack(const float* w, int64_t rows, int64_t cols, int8_t* qs_out, float* scales_out);
 int hg_q8_scale_stride(int64_t cols);
 /* Inverse of the lane-chunked byte permutation (for tests): packed row bytes -> reference order. */
