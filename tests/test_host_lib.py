@@ -27,6 +27,12 @@ def test_library_exports_every_header_symbol(native):
     assert sorted(set(native.EXPORTS)) == names
 
 
+def test_integration_guide_covers_every_entry_point():
+    """The binding guide a hobby-rs maintainer follows names every function of the header."""
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    assert not [n for n in _header_functions() if n not in doc]
+
+
 def _pack(native, w):
     rows, cols = w.shape
     ss = native.lib().hg_q8_scale_stride(cols)
