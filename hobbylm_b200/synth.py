@@ -50,10 +50,11 @@ class Preset:
     init_std: float = 0.02
 
 
-# hobbylm/config.py:118-129
+# hobbylm/config.py:118-134
 PRESETS = {
     "130M": Preset(512, 12, 1, 8, 2, 64, 1536, 192, 32, 8, 0),
     "500M": Preset(768, 16, 1, 12, 3, 128, 2304, 320, 36, 6, 1),
+    "1B": Preset(1024, 20, 1, 16, 8, 128, 2816, 224, 64, 8, 1),
 }
 # a few-MB model of the same architecture for smoke runs (not a reference preset)
 TINY = Preset(256, 2, 1, 4, 1, 64, 512, 128, 8, 2, 1)

@@ -6,7 +6,7 @@ Run here (where the reference checkout is readable), never on the GPU box:
 
 It imports the reference's own Python code and writes, under tests/golden/:
 
-* synth_digests_{130M,500M}.json — per-tensor sha256 (f32 row-major bytes) of the F32 GGUF written by
+* synth_digests_{130M,500M,1B}.json — per-tensor sha256 (f32 row-major bytes) of the F32 GGUF written by
   the reference exporter (export/to_gguf.py:38-133) from ``MoETransformer(get_config(preset))``
   after ``torch.manual_seed(0)`` (hobbylm/model.py:259-313). The exporter's HF-hub tokenizer download
   (to_gguf.py:18-35) is replaced by placeholder tokens, and the 130M preset (no shared expert) gets
@@ -209,11 +209,20 @@ def reference_torch_embeds_logits(ref: str) -> dict:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("HOBBYLM_REFERENCE", ""))
-    ap.add_argument("--only", choices=("all", "bidir", "embeds"), default="all",
-                    help="bidir: only the diffusion fixtures; embeds: only the inputs_embeds fixture")
+    ap.add_argument("--only", choices=("all", "bidir", "embeds", "digests"), default="all",
+                    help="bidir: only the diffusion fixtures; embeds: only the inputs_embeds fixture; "
+                         "digests: only the synth_digests files of --presets")
+    ap.add_argument("--presets", default="130M,500M,1B", help="presets whose exporter digests are written")
     a = ap.parse_args()
     if not a.reference or not os.path.isdir(a.reference):
         raise SystemExit("--reference must point at the HobbyLM checkout")
+    if a.only == "digests":
+        for preset in a.presets.split(","):
+            d = reference_gguf_digests(a.reference, preset)
+            with open(os.path.join(HERE, f"synth_digests_{preset}.json"), "w") as f:
+                json.dump(d, f, indent=1, sort_keys=True)
+            print(preset, len(d["digests"]), "tensors")
+        return
     if a.only in ("all", "embeds"):
         el = reference_torch_embeds_logits(a.reference)
         np.savez(os.path.join(HERE, "torch_embeds_logits_130M.npz"), **el)
@@ -229,7 +238,7 @@ def main():
     print("diffusion cases", len(dg["cases"]))
     if a.only == "bidir":
         return
-    for preset in ("130M", "500M"):
+    for preset in a.presets.split(","):
         d = reference_gguf_digests(a.reference, preset)
         with open(os.path.join(HERE, f"synth_digests_{preset}.json"), "w") as f:
             json.dump(d, f, indent=1, sort_keys=True)

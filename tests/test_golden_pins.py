@@ -18,7 +18,7 @@ from hobbylm_b200 import synth
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 
 
-@pytest.mark.parametrize("preset", ["130M", "500M"])
+@pytest.mark.parametrize("preset", ["130M", "500M", "1B"])
 def test_synth_matches_reference_export(preset):
     with open(os.path.join(GOLDEN, f"synth_digests_{preset}.json")) as f:
         g = json.load(f)
