@@ -79,3 +79,26 @@ def test_generate_embeds_binding_rejects_null_engine(native):
     rc = native.lib().hg_generate_embeds(None, rows.ctypes.data, 2, None, 0, None, native.TOKEN_CB(lambda t, u: 1),
                                          None, out.ctypes.data)
     assert rc == -1 and b"null argument" in native.lib().hg_last_error()
+
+
+@pytest.mark.parametrize("case", ["one_finite", "tiny_top_p", "huge_temp", "n1"])
+def test_host_sample_edge_cases_match_oracle(native, oracle_mod, case):
+    rng = np.random.default_rng(11)
+    x = _logits(rng, VOCAB, "normal")
+    temp, top_p = 0.8, 0.9
+    if case == "one_finite":
+        x[:] = -np.inf
+        x[4242] = 1.0
+    elif case == "tiny_top_p":
+        top_p = 1e-7
+    elif case == "huge_temp":
+        temp = 1e6
+    else:
+        x = np.array([0.5], np.float32)
+    s_lib = s_ora = 7
+    for _ in range(3):
+        a, s_lib = _lib_sample(native, x, temp, top_p, s_lib)
+        b, s_ora = oracle_mod.sample(x, temp, top_p, s_ora)
+        assert (a, s_lib) == (b, s_ora), case
+    if case == "one_finite":
+        assert a == 4242
