@@ -46,6 +46,13 @@ def parse():
     ap.add_argument("--diffusion", action="store_true",
                     help="measure diffusion decode (Engine::generate_diffusion) instead of the headline (one GPU)")
     ap.add_argument("--seqs", type=int, default=N_SEQS, help=argparse.SUPPRESS)
+    ap.add_argument("--attn-case", action="store_true",
+                    help="time the decode-attention op alone on a config-3-shaped case (one GPU); "
+                         "--seqs/--lo/--hi/--pages/--layers shape it")
+    ap.add_argument("--lo", type=int, default=512, help=argparse.SUPPRESS)
+    ap.add_argument("--hi", type=int, default=4096, help=argparse.SUPPRESS)
+    ap.add_argument("--pages", choices=("random", "ordered"), default="random", help=argparse.SUPPRESS)
+    ap.add_argument("--layers", type=int, default=0, help=argparse.SUPPRESS)
     return ap.parse_args()
 
 
@@ -283,8 +290,8 @@ def run_ours(args):
         "data": "synthetic (random-init seed-0 weights, random prompt ids)",
         "config": {"workload": "config5: 500M Q8_0, 256 seqs, prompts U[1024,8192] seed 5, greedy decode",
                    "global_batch": args.seqs, "seqs_per_gpu": n_local, "parallelism": f"seq-shard x{world}",
-                   "context_at_start": {"min": min(reduce_min_list(ctx_start, world)),
-                                        "mean": sum(ctx_start) / max(n_local, 1)},
+                   "context_at_start": {"min": int(reduce_min(min(ctx_start) if ctx_start else 0, world)),
+                                        "mean": reduce_sum(sum(ctx_start), world) / max(total_tokens / args.steps, 1)},
                    "l2": "inputs larger than L2 (KV cache ~60 GB)", "prefill_s_rank0": round(prefill_s, 1)},
         "e2e": {"value": round(total_tokens / e2e_s, 1), "unit": "tok/s",
                 "h2d_bytes_per_step": int(reduce_sum(n_local * 12, world)),
@@ -313,8 +320,16 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def reduce_min_list(v, world):
-    return [min(v)] if v else [0]
+def reduce_min(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return float(t.item())
 
 
 def run_bs1(eng_path: str, local: int, prompt_len: int = 2048, steps: int = 512) -> dict:
@@ -503,12 +518,84 @@ def run_reference(args):
     print(json.dumps(res), flush=True)
 
 
+def run_attn_case(args):
+    """The decode-attention op alone (hg_op_kv_attn: QK-norm + RoPE + KV append, scores, softmax,
+    value sums) on a config-3-shaped case, for timing and profiling the attention kernels: --seqs
+    sequences with contexts U[--lo, --hi] (seed 3), the 500M head shapes (12 q / 3 kv heads,
+    head_dim 128), 16-position pages placed by a random permutation (--pages ordered: consecutive
+    pages), K/V/q ~ N(0,1), QK-norm gains 1, RoPE base 1e4. --layers L lays the pool out as the
+    engine does for an L-layer model (one page holds K and V of every layer; layer 0 is read).
+    Each step is one call; inputs are created on the device and outputs are not checked here (the
+    parity tests compare this entry point with the oracle)."""
+    import ctypes as C
+
+    import numpy as np
+    import torch
+
+    from hobbylm_b200 import _native as native
+
+    nh, nkv, hd, eps, theta = 12, 3, 128, 1e-5, 10000.0
+    rng = np.random.default_rng(3)
+    ctx = rng.integers(args.lo, args.hi + 1, args.seqs)
+    max_pos = int(ctx.max()) + args.steps + 1
+    bt_stride = (max_pos + 15) // 16
+    n_pages = args.seqs * bt_stride
+    perm = rng.permutation(n_pages).astype(np.int32).reshape(args.seqs, bt_stride)
+    if args.pages == "ordered":
+        perm = np.arange(n_pages, dtype=np.int32).reshape(args.seqs, bt_stride)
+    page_floats = nkv * 16 * hd
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(3)
+    page_stride = page_floats
+    if args.layers > 0:  # [page][layer][K | V]
+        pool = torch.zeros((n_pages, args.layers, 2, page_floats), device=dev)
+        pool[:, 0].normal_(generator=g)
+        k_pool, v_pool = pool[:, 0, 0], pool[:, 0, 1]
+        page_stride = args.layers * 2 * page_floats
+    else:
+        k_pool = torch.randn((n_pages, page_floats), generator=g, device=dev)
+        v_pool = torch.randn((n_pages, page_floats), generator=g, device=dev)
+    cos = torch.empty((max_pos, hd // 2), dtype=torch.float32)
+    sin = torch.empty_like(cos)
+    native.check(native.lib().hg_rope_tables(hd, max_pos, theta, cos.data_ptr(), sin.data_ptr()))
+    d_cos, d_sin = cos.to(dev), sin.to(dev)
+    ones = torch.ones(hd, device=dev)
+    d_bt = torch.from_numpy(perm).to(dev)
+    pos = torch.from_numpy(ctx.astype(np.int32)).to(dev)
+    qkv = torch.randn((args.seqs, (nh + 2 * nkv) * hd), generator=g, device=dev)
+    out = torch.empty((args.seqs, nh * hd), device=dev)
+    a = native.KvAttnArgs()
+    a.n_seqs, a.n_heads, a.n_kv_heads, a.head_dim, a.max_pos, a.eps = args.seqs, nh, nkv, hd, max_pos, eps
+    a.qkv, a.q_norm, a.k_norm = qkv.data_ptr(), ones.data_ptr(), ones.data_ptr()
+    a.rope_cos, a.rope_sin, a.pos, a.block_table = d_cos.data_ptr(), d_sin.data_ptr(), pos.data_ptr(), d_bt.data_ptr()
+    a.bt_stride, a.k_pool, a.v_pool, a.page_stride, a.out = (
+        bt_stride, k_pool.data_ptr(), v_pool.data_ptr(), page_stride, out.data_ptr())
+    scratch = torch.empty(native.lib().hg_op_kv_attn_scratch_bytes(C.byref(a)), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    times = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        native.check(native.lib().hg_op_kv_attn(C.byref(a), scratch.data_ptr(), C.c_void_p(stream.cuda_stream)))
+        e1.record(stream)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+        pos += 1
+    kv_bytes = 2 * nkv * hd * 4 * (int(ctx.sum()) + args.seqs * args.steps)  # K + V rows read per call (upper)
+    best = min(times[1:] if len(times) > 1 else times)
+    print(json.dumps({"attn_case": True, "seqs": args.seqs, "pages": args.pages, "layers": args.layers,
+                      "contexts": [int(ctx.min()), int(ctx.mean()), int(ctx.max())],
+                      "ms_per_call": round(best, 4), "kv_gb_per_s": round(kv_bytes / (best / 1e3) / 1e9, 1)}))
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif args.diffusion:
         run_diffusion(args)
+    elif args.attn_case:
+        run_attn_case(args)
     elif args.bs1_only:
         from hobbylm_b200 import synth
 

@@ -6,6 +6,7 @@
 // loads the library until the process exits, and is shared by every call: concurrent or
 // overlapping calls on one device race on it. Every byte a call reads is written by the same call
 // first (the quantized rows and their scales), so nothing needs clearing between calls.
+#include <climits>
 #include <mutex>
 #include <string>
 
@@ -21,7 +22,9 @@ namespace {
 constexpr int kMaxDevices = 64;
 
 // Host code only has a host-side stand-in for g_noalloc_scratch; the device address is looked up
-// once per device, with that device current, and cached.
+// once per device, with that device current, and cached. The cache assumes the device's primary
+// context (the one the runtime API uses) for the life of the process: after cudaDeviceReset the
+// cached address would be stale.
 void* noalloc_scratch(int dev) {
   static std::mutex mu;
   static void* addr[kMaxDevices] = {};
@@ -48,6 +51,9 @@ extern "C" int hg_op_q8_matvec_noalloc(const int8_t* qs, const float* scales, in
   try {
     if (!qs || !scales || !x || !y || rows <= 0 || cols <= 0 || cols % 32 != 0 || ntok <= 0)
       throw Error(HG_ERR_INVALID, "bad argument");
+    // the kernels index rows and columns with int: bound both before the scratch size is formed
+    // (with cols <= INT_MAX and ntok <= INT_MAX the products below cannot wrap in size_t)
+    if (rows > INT_MAX || cols > INT_MAX) throw Error(HG_ERR_INVALID, "rows and cols must be at most INT_MAX");
     const size_t need = up256((size_t)ntok * (size_t)cols) + (size_t)ntok * host_q8_ss(cols) * 4;
     if (need > HG_NOALLOC_SCRATCH_BYTES)
       throw Error(HG_ERR_INVALID, "hg_op_q8_matvec_noalloc: ntok * cols needs " + std::to_string(need) +

@@ -22,6 +22,7 @@ that produce such a file:
 from __future__ import annotations
 
 import hashlib
+import dataclasses
 import os
 import tempfile
 from dataclasses import dataclass
@@ -266,7 +267,9 @@ def cached_model(preset: str = "130M", seed: int = 0, *, quant: str = "q8_0", co
         tempfile.gettempdir(), "hobbylm_b200_cache")
     os.makedirs(root, exist_ok=True)
     eps_tag = f"{rms_eps:g}".replace("-", "m")
-    name = f"hobbylm-{preset}-s{seed}-{quant}-ctx{context_length}-eps{eps_tag}.gguf"
+    tag = preset if isinstance(preset, str) else "p" + "x".join(str(getattr(preset, f.name))
+                                                               for f in dataclasses.fields(preset))
+    name = f"hobbylm-{tag}-s{seed}-{quant}-ctx{context_length}-eps{eps_tag}.gguf"
     return make_model_gguf(os.path.join(root, name), preset, seed, quant=quant,
                            context_length=context_length, rms_eps=rms_eps)
 

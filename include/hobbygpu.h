@@ -236,7 +236,9 @@ int hg_op_q8_matvec(const int8_t* qs, const float* scales, int64_t rows, int64_t
  * whose scratch (ntok * cols bytes + ntok * hg_q8_scale_stride(cols) * 4, rounded up) exceed it
  * are rejected with HG_ERR_INVALID. All calls share the array: calls that overlap on the GPU
  * race and must be ordered by the caller. The first call on a device looks up the array's device
- * address with that device current; make that first call before any stream capture. */
+ * address with that device current; make that first call before any stream capture. The address
+ * is cached for the device's primary context: do not call this after cudaDeviceReset on a device
+ * that has already used it. rows and cols above INT_MAX are rejected with HG_ERR_INVALID. */
 #define HG_NOALLOC_SCRATCH_BYTES (4u << 20)
 int hg_op_q8_matvec_noalloc(const int8_t* qs, const float* scales, int64_t rows, int64_t cols, const float* x,
                             float* y, int ntok, void* stream);

@@ -309,3 +309,98 @@ def test_greedy_decode_config4(model500, oracle_mod):
                 lg, _ = eng.forward(kv, tok)
     finally:
         eng.close()
+
+
+def _oracle_prefills(ora, prompts):
+    caches, logits = [], []
+    for p in prompts:
+        c = ora.new_cache()
+        logits.append(ora.prefill(c, p))
+        caches.append(c)
+    return caches, logits
+
+
+def _masked_argmax(lg):
+    lm = lg.copy()
+    lm[50257:] = -np.inf
+    return int(np.argmax(lm))
+
+
+def _batched_vs_oracle(model, oracle_mod, n_seqs, lo, hi, seed, steps, greedy_steps):
+    """n_seqs sequences of the model (prompt lengths U[lo, hi]) prefilled on the GPU and by the
+    oracle, then `steps` batched decode steps through hg_decode_batch with every sequence's logits
+    and next id bit-compared with the oracle's one-sequence Model::forward, then `greedy_steps`
+    device-driven steps (hg_decode_greedy) whose ids must equal the oracle's greedy ids."""
+    from hobbylm_b200 import Engine
+
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(lo, hi + 1, n_seqs)
+    prompts = [synth.prompt_ids(int(n), seed * 1000 + i) for i, n in enumerate(lens)]
+    ora = oracle_mod.Engine(model, quant=True)
+    eng = Engine.load(model, max_batch=n_seqs, kv_pool_tokens=int(lens.sum()) + n_seqs * (steps + greedy_steps + 32))
+    caches = []
+    try:
+        ocs, olg = _oracle_prefills(ora, prompts)
+        toks = []
+        for i, p in enumerate(prompts):
+            c = eng.new_cache()
+            caches.append(c)
+            lg = eng.prefill(c, p)
+            assert np.array_equal(lg.view(np.uint32), olg[i].view(np.uint32)), f"prefill seq {i}"
+            toks.append(_masked_argmax(lg))
+        for step in range(steps):
+            nb, lb = eng.decode_batch(caches, toks, want_logits=True)
+            for i in range(n_seqs):
+                ref = ora.forward(ocs[i], toks[i], int(lens[i]) + step)
+                assert np.array_equal(lb[i].view(np.uint32), ref.view(np.uint32)), \
+                    f"step {step} seq {i} (context {int(lens[i]) + step}): rel L2 {_rel(lb[i], ref)}"
+                assert int(nb[i]) == _masked_argmax(ref), f"step {step} seq {i}: next id"
+            toks = [int(v) for v in nb]
+        if greedy_steps:
+            dev = eng.decode_greedy(caches, toks, greedy_steps)
+            for i in range(n_seqs):
+                t = toks[i]
+                for k in range(greedy_steps):
+                    t = _masked_argmax(ora.forward(ocs[i], t, int(lens[i]) + steps + k))
+                    assert int(dev[k][i]) == t, f"greedy step {k} seq {i}"
+        for c in ocs:
+            c.close()
+    finally:
+        for c in caches:
+            c.close()
+        eng.close()
+        ora.close()
+
+
+def test_batched_500m_large_batch_kernels_match_oracle(model500, oracle_mod):
+    """The 500M engine with 80 sequences (240 (token, kv head) pairs: the large-batch attention
+    kernels on the engine's layered KV pool, head_dim 128), prompts of 64-300 ids: 8 batched steps
+    bit-identical to the oracle sequence by sequence, then 4 device-driven greedy steps."""
+    _batched_vs_oracle(model500, oracle_mod, 80, 64, 300, 81, 8, 4)
+
+
+@pytest.mark.slow
+def test_batched_500m_config5_batch_matches_oracle(model500, oracle_mod):
+    """The config-5 batch size (256 sequences, the step graph without programmatic launches, the
+    lm_head's 64-token chunks, expert groups of many entries) on short prompts (8-64 ids): 4
+    batched steps bit-identical to the oracle sequence by sequence, then 2 greedy steps."""
+    _batched_vs_oracle(model500, oracle_mod, 256, 8, 64, 82, 4, 2)
+
+
+# The 1B preset's attention and expert shapes (hobbylm/config.py:130-134: d 1024, 16 q / 8 kv heads
+# of 128, GQA group 2, 64 experts top-8 of width 224, dense 2816) on two layers, so the model stays
+# small enough to generate and check quickly.
+PRESET_1B_2L = synth.Preset(1024, 2, 1, 16, 8, 128, 2816, 224, 64, 8, 1)
+
+
+@pytest.fixture(scope="module")
+def model1b2l():
+    return synth.cached_model(PRESET_1B_2L, 0)
+
+
+def test_gqa_group2_1b_shapes_match_oracle(model1b2l, oracle_mod):
+    """A GQA group-2 model with the 1B preset's widths: prefill, then batch 1 (the small-batch
+    kernels) and batch 30 (240 (token, kv head) pairs: the large-batch kernels) bit-identical to
+    the oracle, then device-driven greedy ids."""
+    _batched_vs_oracle(model1b2l, oracle_mod, 1, 40, 40, 91, 12, 8)
+    _batched_vs_oracle(model1b2l, oracle_mod, 30, 16, 80, 92, 6, 4)

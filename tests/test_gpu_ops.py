@@ -132,11 +132,26 @@ def test_moe_op_config2_bitexact(native, oracle_mod, moe_inputs, T):
     assert np.array_equal(_bits(y), _bits(y_ref)), f"max |d| {np.abs(y - y_ref).max()}"
 
 
-@pytest.mark.parametrize("n_seqs,steps", [(64, 4), (72, 2)])
+def _oracle_attn_steps(oracle_mod, rope, caches, qkv, pos, nh, nkv, hd, eps, ones):
+    """One oracle attention step (append + attend) per sequence, sequences in parallel threads
+    (the oracle call is single-threaded, stateless and releases the GIL)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    def one(s):
+        kc, vc = caches[s]
+        return oracle_mod.attn_step(rope, nh, nkv, hd, eps, ones, ones, qkv[s].copy(), int(pos[s]), kc, vc)
+
+    with ThreadPoolExecutor(max_workers=16) as ex:
+        return list(ex.map(one, range(len(caches))))
+
+
+@pytest.mark.parametrize("n_seqs,steps", [(64, 256), (72, 24)])
 def test_kv_attn_config3(native, oracle_mod, n_seqs, steps):
-    """Config 3 (reduced step count): 64 sequences, ctx ~ U[512, 4096] (seed 3), 500M head shapes,
-    K/V/Q ~ N(0,1), QK-norm gains 1, RoPE base 1e4, 16-token pages placed by a random permutation.
-    64 sequences take the small-batch value-sum kernel (one warp per q head), 72 the large one."""
+    """Config 3: 64 sequences, ctx ~ U[512, 4096] (seed 3), 500M head shapes, K/V/Q ~ N(0,1),
+    QK-norm gains 1, RoPE base 1e4, 16-token pages placed by a random permutation, one appended
+    and attended token per sequence per step for all 256 steps. Every sequence's output is
+    bit-compared with the oracle at every step, and at the end every appended K and V row of every
+    sequence. 72 sequences (216 (sequence, kv head) pairs) take the large-batch kernel path."""
     import torch
 
     nh, nkv, hd, eps, theta = 12, 3, 128, 1e-5, 10000.0
@@ -148,53 +163,53 @@ def test_kv_attn_config3(native, oracle_mod, n_seqs, steps):
     perm = rng.permutation(n_pages).astype(np.int32).reshape(n_seqs, bt_stride)
     kvd = nkv * hd
     page_floats = nkv * 16 * hd
-    k_pool = np.zeros((n_pages, page_floats), np.float32)
-    v_pool = np.zeros((n_pages, page_floats), np.float32)
+    k_pool = np.zeros((n_pages, nkv, 16, hd), np.float32)
+    v_pool = np.zeros((n_pages, nkv, 16, hd), np.float32)
     caches = []
     for s in range(n_seqs):
         kc = np.zeros((max_pos, kvd), np.float32)
         vc = np.zeros((max_pos, kvd), np.float32)
-        kc[: ctx[s]] = rng.standard_normal((ctx[s], kvd)).astype(np.float32)
-        vc[: ctx[s]] = rng.standard_normal((ctx[s], kvd)).astype(np.float32)
-        for p in range(ctx[s]):
-            pg, sl = perm[s, p // 16], p % 16
-            k_pool[pg].reshape(nkv, 16, hd)[:, sl] = kc[p].reshape(nkv, hd)
-            v_pool[pg].reshape(nkv, 16, hd)[:, sl] = vc[p].reshape(nkv, hd)
+        n = int(ctx[s])
+        kc[:n] = rng.standard_normal((n, kvd)).astype(np.float32)
+        vc[:n] = rng.standard_normal((n, kvd)).astype(np.float32)
+        p = np.arange(n)
+        k_pool[perm[s, p // 16], :, p % 16] = kc[:n].reshape(n, nkv, hd)
+        v_pool[perm[s, p // 16], :, p % 16] = vc[:n].reshape(n, nkv, hd)
         caches.append((kc, vc))
     rope = oracle_mod.Rope(hd, max_pos, theta)
     cos, sin = rope.tables()
     ones = np.ones(hd, np.float32)
-    d_k, d_v = _dev(k_pool), _dev(v_pool)
+    d_k, d_v = _dev(k_pool.reshape(n_pages, page_floats)), _dev(v_pool.reshape(n_pages, page_floats))
     d_bt, d_cos, d_sin, d_g = _dev(perm), _dev(cos), _dev(sin), _dev(ones)
     pos = ctx.astype(np.int32).copy()
+    a = native.KvAttnArgs()
+    a.n_seqs, a.n_heads, a.n_kv_heads, a.head_dim, a.max_pos, a.eps = n_seqs, nh, nkv, hd, max_pos, eps
+    a.q_norm, a.k_norm = d_g.data_ptr(), d_g.data_ptr()
+    a.rope_cos, a.rope_sin, a.block_table = d_cos.data_ptr(), d_sin.data_ptr(), d_bt.data_ptr()
+    a.bt_stride, a.k_pool, a.v_pool, a.page_stride = bt_stride, d_k.data_ptr(), d_v.data_ptr(), page_floats
+    scratch = torch.empty(native.lib().hg_op_kv_attn_scratch_bytes(C.byref(a)), dtype=torch.uint8, device="cuda")
     worst = 0.0
     for step in range(steps):
         qkv = rng.standard_normal((n_seqs, (nh + 2 * nkv) * hd)).astype(np.float32)
         d_qkv, d_pos = _dev(qkv), _dev(pos)
         d_out = torch.empty((n_seqs, nh * hd), dtype=torch.float32, device="cuda")
-        a = native.KvAttnArgs()
-        a.n_seqs, a.n_heads, a.n_kv_heads, a.head_dim, a.max_pos, a.eps = n_seqs, nh, nkv, hd, max_pos, eps
-        a.qkv, a.q_norm, a.k_norm = d_qkv.data_ptr(), d_g.data_ptr(), d_g.data_ptr()
-        a.rope_cos, a.rope_sin, a.pos, a.block_table = d_cos.data_ptr(), d_sin.data_ptr(), d_pos.data_ptr(), d_bt.data_ptr()
-        a.bt_stride, a.k_pool, a.v_pool, a.page_stride, a.out = bt_stride, d_k.data_ptr(), d_v.data_ptr(), page_floats, d_out.data_ptr()
-        scratch = torch.empty(native.lib().hg_op_kv_attn_scratch_bytes(C.byref(a)), dtype=torch.uint8, device="cuda")
+        a.qkv, a.pos, a.out = d_qkv.data_ptr(), d_pos.data_ptr(), d_out.data_ptr()
         native.check(native.lib().hg_op_kv_attn(C.byref(a), scratch.data_ptr(), None))
-        torch.cuda.synchronize()
+        refs = _oracle_attn_steps(oracle_mod, rope, caches, qkv, pos, nh, nkv, hd, eps, ones)
         out = d_out.cpu().numpy()
         for s in range(n_seqs):
-            kc, vc = caches[s]
-            ref = oracle_mod.attn_step(rope, nh, nkv, hd, eps, ones, ones, qkv[s].copy(), int(pos[s]), kc, vc)
+            ref = refs[s]
             rel = np.linalg.norm(out[s] - ref) / np.linalg.norm(ref)
             worst = max(worst, rel)
             assert np.array_equal(_bits(out[s]), _bits(ref)), f"step {step} seq {s}: rel L2 {rel}"
         pos += 1
-    # the appended K (QK-normed + roped) and V rows equal the oracle's cache rows
-    kp = d_k.cpu().numpy()
-    vp = d_v.cpu().numpy()
-    for s in range(4):
+    # every appended K (QK-normed + roped) and V row of every sequence equals the oracle's cache row
+    kp = d_k.cpu().numpy().reshape(n_pages, nkv, 16, hd)
+    vp = d_v.cpu().numpy().reshape(n_pages, nkv, 16, hd)
+    for s in range(n_seqs):
         kc, vc = caches[s]
-        for p in range(int(ctx[s]), int(pos[s])):
-            pg, sl = perm[s, p // 16], p % 16
-            assert np.array_equal(vp[pg].reshape(nkv, 16, hd)[:, sl].ravel(), vc[p])
-            kr = kp[pg].reshape(nkv, 16, hd)[:, sl].ravel()
-            assert np.array_equal(_bits(kr), _bits(kc[p]))
+        p = np.arange(int(ctx[s]), int(pos[s]))
+        got_k = kp[perm[s, p // 16], :, p % 16].reshape(len(p), kvd)
+        got_v = vp[perm[s, p // 16], :, p % 16].reshape(len(p), kvd)
+        assert np.array_equal(_bits(got_k), _bits(kc[p])), f"seq {s}: appended K rows differ"
+        assert np.array_equal(_bits(got_v), _bits(vc[p])), f"seq {s}: appended V rows differ"

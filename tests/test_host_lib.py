@@ -251,3 +251,14 @@ def test_gguf_tensor_dequant_matches_gguf_py(native, tmp_path, qtype):
     # wrong element count and missing tensor are errors, not silent truncation
     assert lib.hg_gguf_tensor_f32(str(tmp_path / "q.gguf").encode(), b"t", out.ctypes.data, out.size - 1) == -1
     assert lib.hg_gguf_tensor_f32(str(tmp_path / "q.gguf").encode(), b"nope", out.ctypes.data, out.size) == -4
+
+
+def test_noalloc_matvec_rejects_out_of_range_shapes_before_any_device_work(native):
+    """Rows or columns beyond INT_MAX, or a column count whose scratch size would wrap, are
+    rejected from the arguments alone (dummy non-null pointers; no device is touched)."""
+    lib = native.lib()
+    p = C.c_void_p(16)
+    for rows, cols, ntok in ((64, 1 << 62, 4), (1 << 31, 768, 1), (64, (1 << 31) + 32, 1)):
+        rc = lib.hg_op_q8_matvec_noalloc(p, p, rows, cols, p, p, ntok, None)
+        assert rc == -1, (rows, cols, ntok)  # HG_ERR_INVALID
+        assert b"INT_MAX" in lib.hg_last_error()

@@ -40,10 +40,16 @@ def _run(native, fn, rows, cols, ntok, seed):
     return dy.cpu().numpy()
 
 
-def test_noalloc_matches_allocating_matvec_on_two_calls(native):
+@pytest.mark.parametrize("calls", [
+    ((2304, 768, 3, 11), (768, 1536, 17, 12)),   # small, then large
+    ((768, 1536, 17, 13), (2304, 768, 1, 14)),   # large, then small: stale bytes from the first
+                                                 # call lie where the second reads its scales
+    ((320, 768, 1, 15), (768, 320, 1, 16)),      # one token per call (the single-token kernel)
+])
+def test_noalloc_matches_allocating_matvec_on_two_calls(native, calls):
     lib = native.lib()
     # two calls in a row share the scratch array; the second must not see the first's contents
-    for rows, cols, ntok, seed in ((2304, 768, 3, 11), (768, 1536, 17, 12)):
+    for rows, cols, ntok, seed in calls:
         got = _run(native, lib.hg_op_q8_matvec_noalloc, rows, cols, ntok, seed)
         ref = _run(native, lib.hg_op_q8_matvec, rows, cols, ntok, seed)
         assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (rows, cols, ntok)
