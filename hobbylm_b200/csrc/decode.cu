@@ -13,8 +13,8 @@
 // reproduce the reference bit for bit given the same inputs, and so do the RMSNorm / QK-norm sums
 // and the attention softmax / value sums, which run sequentially in position order like the
 // reference's loops (one thread per chain).
+#include <algorithm>
 #include <cfloat>
-
 #include <utility>
 
 #include "hg_model.cuh"
@@ -48,24 +48,45 @@ static inline void launch_pdl(bool pdl, void (*kern)(P...), dim3 grid, dim3 bloc
 // Block reductions
 // ------------------------------------------------------------------------------------------
 // Sequential f32 sum of squares of xs[0..n) (ops.rs:85-95 `ss += v * v`, no FMA) computed by one
-// thread; every thread of the block receives the result.
+// thread; every thread of the block receives the result. xs is 16-byte aligned and n % 16 == 0;
+// the shared-memory loads run one 16-element group ahead of the adds, so the dependent add
+// latency, not the load latency, sets the pace.
+__device__ __forceinline__ float seq_sumsq_smem(const float* xs, int n) {
+  const float4* x4 = reinterpret_cast<const float4*>(xs);
+  const int ng = n >> 4;
+  float ss = 0.0f;
+  float4 a[4], b[4];
+  auto add4 = [&](const float4* v) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      ss = fadd(ss, fmul(v[i].x, v[i].x));
+      ss = fadd(ss, fmul(v[i].y, v[i].y));
+      ss = fadd(ss, fmul(v[i].z, v[i].z));
+      ss = fadd(ss, fmul(v[i].w, v[i].w));
+    }
+  };
+  if (ng > 0) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) a[i] = x4[i];
+  }
+  int g = 0;
+  for (; g + 1 < ng; g += 2) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) b[i] = x4[(g + 1) * 4 + i];
+    add4(a);
+    if (g + 2 < ng) {
+#pragma unroll
+      for (int i = 0; i < 4; i++) a[i] = x4[(g + 2) * 4 + i];
+    }
+    add4(b);
+  }
+  if (g < ng) add4(a);
+  return ss;
+}
+
 __device__ inline float seq_sumsq_block(const float* xs, int n, float* red) {
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float ss = 0.0f;
-    const float4* x4 = reinterpret_cast<const float4*>(xs);  // n % 4 == 0, xs 16-byte aligned
-    const int n4 = n >> 2;
-    float4 a = n4 > 0 ? x4[0] : make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int i = 0; i < n4; i++) {
-      const float4 b = i + 1 < n4 ? x4[i + 1] : a;  // next group's load issued before this group's adds
-      ss = fadd(ss, fmul(a.x, a.x));
-      ss = fadd(ss, fmul(a.y, a.y));
-      ss = fadd(ss, fmul(a.z, a.z));
-      ss = fadd(ss, fmul(a.w, a.w));
-      a = b;
-    }
-    red[0] = ss;
-  }
+  if (threadIdx.x == 0) red[0] = seq_sumsq_smem(xs, n);
   __syncthreads();
   return red[0];
 }
@@ -376,24 +397,23 @@ __global__ void __launch_bounds__(ROUTE_THREADS) k_route(Dims D, DecodeBufs B, L
     if (r < k) rank_e[r] = e;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float w[MAX_TOPK];
-    for (int r = 0; r < k; r++) w[r] = score_s[rank_e[r]];
-    if (D.wnorm) {
+  // rank r's selection by thread r: the k experts of a token are distinct, so their list slots
+  // are claimed independently (the order of the active-expert list changes no result)
+  if (threadIdx.x < k) {
+    const int r = threadIdx.x, e = rank_e[r];
+    float w = score_s[e];
+    if (D.wnorm) {  // the weights' sum in rank order (model.rs:288-292)
       float s = -0.0f;
-      for (int r = 0; r < k; r++) s = fadd(s, w[r]);
+      for (int rr = 0; rr < k; rr++) s = fadd(s, score_s[rank_e[rr]]);
       s = fadd(s, 1e-9f);
-      for (int r = 0; r < k; r++) w[r] = __fdiv_rn(w[r], s);
+      w = __fdiv_rn(w, s);
     }
-    for (int r = 0; r < k; r++) {
-      int e = rank_e[r];
-      B.sel[t * k + r] = e;
-      B.selw[t * k + r] = w[r];
-      if (B.dbg_sel) B.dbg_sel[((size_t)layer * B.T + t) * k + r] = e;
-      int slot = atomicAdd(&B.ecount[e], 1);
-      if (slot == 0) B.active[atomicAdd(&B.ecount[ne], 1)] = e;
-      B.elist[(size_t)e * B.T + slot] = t * 32 + r;
-    }
+    B.sel[t * k + r] = e;
+    B.selw[t * k + r] = w;
+    if (B.dbg_sel) B.dbg_sel[((size_t)layer * B.T + t) * k + r] = e;
+    const int slot = atomicAdd(&B.ecount[e], 1);
+    if (slot == 0) B.active[atomicAdd(&B.ecount[ne], 1)] = e;
+    B.elist[(size_t)e * B.T + slot] = t * 32 + r;
   }
 }
 
@@ -579,19 +599,27 @@ __global__ void __launch_bounds__(ROWS * 8) k_ffn_down(Dims D, DecodeBufs B, Lay
 // ------------------------------------------------------------------------------------------
 // Attention (model.rs:199-233) over a paged f32 KV pool, in the reference's arithmetic order.
 //
-// k_qk_prep: QK-norm (sequential sum, model.rs:753-763) + RoPE of each token's q heads and k
-//   heads; the k and v rows are appended to their page slot.
-// k_attn_scores: work item = (token, kv head, run of chunks of ATT_CHUNK positions), 8 warps x 8
-//   positions per chunk. s[t][h][j] = dot(q_h, k_j) * (1/sqrt(hd)) in the ops::dot order; the
-//   chunk maximum per head and warp.
-// k_attn_softmax: softmax (ops.rs:112-128) per (token, q head): global max, e_j = exp(s_j - max)
-//   (parallel), sum = sequential f32 sum over j, inv = 1/sum.
-// k_attn_pv / k_attn_pv_hw: every (head, dim) chain accumulates o += (e_j * inv) * v_j[dim]
-//   sequentially over j (model.rs:227-232); the result is quantized per 32-block for the output
-//   projection (quant.rs:112-123).
+// k_qk_prep: QK-norm (sequential sum, model.rs:753-763) + RoPE of each token's q heads into qn,
+//   and of its k heads, appended with its v heads to their page slot; resets the score maxima.
+// k_attn_scores: work units of 32 positions of one (token, kv head), dealt to CTAs in contiguous
+//   runs. A unit's K rows (two pages) and the group's q rows are staged into shared memory by
+//   cp.async (SC_SLOTS units in flight per CTA); one thread per (position, q head) computes
+//   s = dot(q_h, k_j) * (1/sqrt(hd)) in the ops::dot order; per-(token, head) maxima are merged
+//   with an atomic max on an order-preserving key.
+// k_attn_softmax: per (token, q head): e_j = exp(s_j - max) (parallel), sum = sequential f32 sum
+//   over j (one thread), inv = 1/sum (ops.rs:112-128).
+// k_attn_pv / k_attn_pv_small: every (head, dim) chain accumulates o += (e_j * inv) * v_j[dim]
+//   sequentially over j (model.rs:227-232), V and e staged through a cp.async ring; the result
+//   is quantized per 32-block for the output projection (quant.rs:112-123).
 // ------------------------------------------------------------------------------------------
 
-constexpr int ATT_MAX_BT = 4096;  // block-table entries staged in shared memory (contexts <= 65536)
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // per-head RMSNorm with a sequential sum (model.rs:753-763) + rotate-half RoPE (ops.rs:157-166)
 // of one head vector by one warp. buf: this warp's HD-float shared scratch; dst may alias buf.
@@ -633,53 +661,28 @@ __device__ __forceinline__ void norm_rope_warp(const float* src, const float* w,
   __syncwarp();
 }
 
-// Work split of k_attn_scores: each item is (token, kv head, run of G consecutive chunks) with G
-// chosen so that there are about ATT_ITEMS_PER_CTA items per CTA: items are dealt round-robin, and
-// several smaller items per CTA keep the most loaded CTA near the mean (one item per CTA left
-// some CTAs with two full items, twice the mean). prefix_s[t] = first item of token t; returns the
-// item count and writes G to *g_out. Positions beyond max_pos raise an error.
-constexpr int ATT_ITEMS_PER_CTA = 8;
-
-__device__ inline int attn_item_prefix(const AttnArgs& A, int* prefix_s, int* g_s) {
-  if (threadIdx.x == 0) {
-    long long chunks = 0;
-    for (int t = 0; t < A.T; t++) {
-      int p = A.pos[t];
-      int nch = (p + 1 + ATT_CHUNK - 1) / ATT_CHUNK;
-      if (p >= 0 && p < A.max_pos && nch <= A.max_chunks) chunks += nch;
-    }
-    long long want = (long long)gridDim.x * ATT_ITEMS_PER_CTA;
-    int G = (int)((chunks * A.nkv + want - 1) / want);
-    G = G < 1 ? 1 : G;
-    int acc = 0;
-    prefix_s[0] = 0;
-    for (int t = 0; t < A.T; t++) {
-      int p = A.pos[t];
-      int nch = (p + 1 + ATT_CHUNK - 1) / ATT_CHUNK;
-      if (p < 0 || p >= A.max_pos || nch > A.max_chunks) {
-        nch = 0;
-        if (A.err) atomicExch(A.err, HG_ERR_CONTEXT);
-      }
-      acc += ((nch + G - 1) / G) * A.nkv;
-      prefix_s[t + 1] = acc;
-    }
-    *g_s = G;
-  }
-  __syncthreads();
-  return prefix_s[A.T];
+// A token's position is usable when its page is inside the block table and below max_pos;
+// otherwise the token does no attention work and the step reports HG_ERR_CONTEXT.
+__device__ __forceinline__ bool attn_pos_ok(const AttnArgs& A, int pos) {
+  return pos >= 0 && pos < A.max_pos && pos / PAGE < A.bt_stride;
 }
 
 // QK-norm (sequential sum, model.rs:753-763) + RoPE of every q head of a token into qn, and of
 // the token's k heads, appended with its v heads to their page slot (model.rs:199-210). One CTA
-// per token, one warp per head (q heads first, then kv heads).
+// per token, one warp per head (q heads first, then kv heads). Also resets the token's score
+// maxima (read by k_attn_softmax two kernels later).
 template <int HD>
 __global__ void k_qk_prep(AttnArgs A) {
   extern __shared__ __align__(16) float prep_s[];  // one HD-float scratch per warp
   const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_wait();
   pdl_trigger();
+  for (int h = threadIdx.x; h < A.nh; h += blockDim.x) A.mkey[(size_t)t * A.nh + h] = 0u;
   const int pos = A.pos[t];
-  if (pos < 0 || pos >= A.max_pos || pos / PAGE >= A.bt_stride) return;  // flagged by k_attn_scores
+  if (!attn_pos_ok(A, pos)) {
+    if (threadIdx.x == 0 && A.err) atomicExch(A.err, HG_ERR_CONTEXT);
+    return;
+  }
   const float* qkv = A.qkv + (size_t)t * A.qkv_stride;
   const int qd = A.nh * HD, kvd = A.nkv * HD;
   const float* cs = A.rope_cos + (size_t)pos * (HD / 2);
@@ -701,127 +704,179 @@ __global__ void k_qk_prep(AttnArgs A) {
   }
 }
 
-template <int HD, int REP>
-__global__ void __launch_bounds__(256) k_attn_scores(AttnArgs A) {
-  constexpr int E = HD / 32;
-  __shared__ __align__(16) float q_s[REP][HD];
-  __shared__ int prefix_s[257];
-  __shared__ int g_s;
-  __shared__ int pg_s[1024];  // page ids of the item's chunks (ATT_CHUNK / PAGE per chunk)
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  pdl_wait();
-  pdl_trigger();
-  const int total = attn_item_prefix(A, prefix_s, &g_s);
-  const int G = g_s;
-  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
-  for (int item = blockIdx.x; item < total; item += gridDim.x) {
+// Units of 32 positions (two pages) of the tokens, kv head by kv head: u_count[t] units per
+// (token, kv head). prefix_s[t] = first unit of token t (nkv * sum of earlier counts);
+// prefix_s[T] = total. Computed by warp 0 (T <= SC_MAX_T).
+constexpr int ATT_UNIT = 32;
+constexpr int SC_MAX_T = 1024;
+
+__device__ __forceinline__ int attn_units_of(const AttnArgs& A, int t) {
+  const int p = A.pos[t];
+  return attn_pos_ok(A, p) ? (p + 1 + ATT_UNIT - 1) / ATT_UNIT : 0;
+}
+
+__device__ inline void attn_unit_prefix(const AttnArgs& A, int* prefix_s) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const int per = (A.T + 31) / 32, t0 = lane * per;
+    int run = 0;
+    for (int i = 0; i < per; i++) run += t0 + i < A.T ? attn_units_of(A, t0 + i) * A.nkv : 0;
+    int incl = run;  // inclusive scan of the lanes' run totals
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    int acc = incl - run;
+    for (int i = 0; i < per; i++) {
+      if (t0 + i < A.T) {
+        prefix_s[t0 + i] = acc;
+        acc += attn_units_of(A, t0 + i) * A.nkv;
+      }
+    }
+    if (lane == 31) prefix_s[A.T] = incl;
+  }
+  __syncthreads();
+}
+
+// A CTA walks its contiguous run of units in order: (token, kv head, unit within the head).
+struct UnitCursor {
+  int t, kvh, s, nu;  // nu = units per (token, kv head) of token t
+  __device__ void seek(const AttnArgs& A, const int* prefix_s, int u) {
     int lo = 0, hi = A.T - 1;
     while (lo < hi) {
-      int mid = (lo + hi + 1) >> 1;
-      if (prefix_s[mid] <= item) lo = mid;
+      const int mid = (lo + hi + 1) >> 1;
+      if (prefix_s[mid] <= u) lo = mid;
       else hi = mid - 1;
     }
-    const int t = lo, rem = item - prefix_s[t];
-    const int kvh = rem % A.nkv, cg = rem / A.nkv;
-    const int pos = A.pos[t], n = pos + 1;
-    const int nch = (n + ATT_CHUNK - 1) / ATT_CHUNK;
-    const int cbeg = cg * G, cend = min(nch, cbeg + G);
-    const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
-    __syncthreads();
-    const int pg0 = cbeg * (ATT_CHUNK / PAGE), npg = min((cend - cbeg) * (ATT_CHUNK / PAGE), 1024);
-    for (int i = threadIdx.x; i < npg; i += blockDim.x) pg_s[i] = pg0 + i < A.bt_stride ? bt[pg0 + i] : 0;
-    // the group's q heads, QK-normed and roped by k_qk_prep (which also appended the new K row)
-    const float* qsrc = A.qn + ((size_t)t * A.nh + kvh * REP) * HD;
-    for (int i = threadIdx.x; i < REP * HD; i += blockDim.x) q_s[i / HD][i % HD] = qsrc[i];
-    __syncthreads();
-    // ops::dot lane mapping: accumulator m's SIMD lane l sums elements 32i + 8m + l (FMA, i
-    // ascending); lane sums are (a0+a1)+(a2+a3), then the 8-lane tree. Here a group of 8 threads
-    // (l = lane % 8) owns one position, so the 4 accumulators stay in registers and only the tree
-    // needs shuffles (3 per head); a warp scores 4 positions at a time.
-    const int l = lane & 7, pp = lane >> 3;
-    float qv[REP][E][4];
-#pragma unroll
-    for (int h = 0; h < REP; h++)
-#pragma unroll
-      for (int i = 0; i < E; i++)
-#pragma unroll
-        for (int m = 0; m < 4; m++) qv[h][i][m] = q_s[h][32 * i + 8 * m + l];
-    float* srow = A.S + ((size_t)t * A.nh + kvh * REP) * A.s_stride;
-    const float* kbase = A.k_pool + (long long)kvh * PAGE * HD;
-    auto prefetch_rows = [&](int c) {
-      const int p = c * ATT_CHUNK + warp * 8 + (lane >> 2);
-      if (c < cend && p < n) {
-        const int pgi = p / PAGE - pg0;
-        const int page = pgi < 1024 ? pg_s[pgi] : bt[p / PAGE];
-        const float* r = kbase + (long long)page * A.page_stride + (long long)(p % PAGE) * HD + (lane & 3) * (HD / 4);
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(r));
-      }
-    };
-    prefetch_rows(cbeg);
-    for (int c = cbeg; c < cend; c++) {
-      const int c0 = c * ATT_CHUNK;
-      prefetch_rows(c + 1);
-      float mx[REP];
-#pragma unroll
-      for (int h = 0; h < REP; h++) mx[h] = -INFINITY;
-      // this warp's 8 positions: c0 + 8 warp + 4 sub + pp, both sub-groups' K loads issued first
-      float kv[2][E][4];
-#pragma unroll
-      for (int sub = 0; sub < 2; sub++) {
-        const int p = c0 + warp * 8 + sub * 4 + pp;
-        const int pc = p < n ? p : c0;  // positions past the end read a valid row, unused
-        const int pgi = pc / PAGE - pg0;
-        const int page = pgi < 1024 ? pg_s[pgi] : bt[pc / PAGE];
-        const float* kp = A.k_pool + (long long)page * A.page_stride + ((long long)kvh * PAGE + (pc % PAGE)) * HD;
-#pragma unroll
-        for (int i = 0; i < E; i++)
-#pragma unroll
-          for (int m = 0; m < 4; m++) kv[sub][i][m] = p < n ? kp[32 * i + 8 * m + l] : 0.0f;
-      }
-#pragma unroll
-      for (int sub = 0; sub < 2; sub++) {
-        const int p = c0 + warp * 8 + sub * 4 + pp;
-#pragma unroll
-        for (int h = 0; h < REP; h++) {
-          float a[4];
-#pragma unroll
-          for (int m = 0; m < 4; m++) {
-            float cacc = 0.0f;
-#pragma unroll
-            for (int i = 0; i < E; i++) cacc = __fmaf_rn(qv[h][i][m], kv[sub][i][m], cacc);
-            a[m] = cacc;
-          }
-          float sc = fmul(hsum8_group(fadd(fadd(a[0], a[1]), fadd(a[2], a[3]))), scale);
-          if (p < n) {
-            if (l == 0) srow[(size_t)h * A.s_stride + p] = sc;
-            mx[h] = fmaxf(mx[h], sc);
-          }
-        }
-      }
-      // per-warp maximum of this chunk: cmax[t][h][c * 8 + warp] (no block barrier needed)
-#pragma unroll
-      for (int h = 0; h < REP; h++) mx[h] = warp_max(mx[h]);
-      if (lane < REP) {
-        float mv = mx[0];
-#pragma unroll
-        for (int h = 1; h < REP; h++)
-          if (lane == h) mv = mx[h];
-        A.cmax[((size_t)t * A.nh + kvh * REP + lane) * (size_t)A.max_chunks * 8 + c * 8 + warp] = mv;
-      }
-    }
+    t = lo;
+    nu = (prefix_s[t + 1] - prefix_s[t]) / A.nkv;
+    const int rem = u - prefix_s[t];
+    kvh = nu > 0 ? rem / nu : 0;
+    s = nu > 0 ? rem - kvh * nu : 0;
   }
+  __device__ void next(const AttnArgs& A, const int* prefix_s) {
+    if (++s < nu) return;
+    s = 0;
+    if (++kvh < A.nkv) return;
+    kvh = 0;
+    do {
+      ++t;
+      nu = t < A.T ? (prefix_s[t + 1] - prefix_s[t]) / A.nkv : 1;
+    } while (nu == 0);
+  }
+};
+
+constexpr int SC_SLOTS = 4;  // units in flight per scores CTA
+
+template <int HD, int REP>
+struct ScoresShape {
+  static constexpr int NT = 32 * REP;  // one thread per (position, q head) of a unit
+  static constexpr int PW = 32 / REP;  // positions per warp; lane = head * PW + position
+  static constexpr int CH = HD / 4;    // 16-byte chunks per K row
+  static constexpr int QS = HD + 4;    // padded q row (floats): the group's heads on distinct banks
+  static constexpr int SLOT = ATT_UNIT * HD + REP * QS;  // floats per ring slot
+  static constexpr size_t SMEM = (size_t)SC_SLOTS * SLOT * 4 + (SC_MAX_T + 1) * 4;
+};
+
+// K chunk c (16 bytes) of unit row r is stored at chunk c ^ (r & 7): the PW rows a warp reads at
+// once then lie on distinct bank groups.
+template <int HD, int REP>
+__global__ void __launch_bounds__(32 * REP) k_attn_scores(AttnArgs A) {
+  using S = ScoresShape<HD, REP>;
+  extern __shared__ __align__(16) float sc_smem[];
+  float* ring = sc_smem;
+  int* prefix_s = reinterpret_cast<int*>(sc_smem + SC_SLOTS * S::SLOT);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = lane / S::PW, p = lane - h * S::PW, r = warp * S::PW + p;  // r: row within the unit
+  attn_unit_prefix(A, prefix_s);  // positions are older than the previous kernel
+  pdl_wait();  // qn and the appended K rows come from k_qk_prep
+  pdl_trigger();
+  const long long total = prefix_s[A.T];
+  const int u0 = (int)(total * blockIdx.x / gridDim.x), u1 = (int)(total * (blockIdx.x + 1) / gridDim.x);
+  const int count = u1 - u0;
+  if (count <= 0) return;
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+  UnitCursor ic, cc;  // issue / compute cursors
+  ic.seek(A, prefix_s, u0);
+  cc = ic;
+  auto issue = [&](int i) {
+    if (i < count) {
+      float* slot = ring + (i % SC_SLOTS) * S::SLOT;
+      const int pos = A.pos[ic.t], npg = pos / PAGE + 1, pg0 = ic.s * (ATT_UNIT / PAGE);
+      const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[ic.t] : ic.t) * A.bt_stride;
+      const float* kb = A.k_pool + (long long)ic.kvh * PAGE * HD;
+#pragma unroll
+      for (int i2 = tid; i2 < ATT_UNIT * S::CH; i2 += S::NT) {
+        const int row = i2 / S::CH, c = i2 - row * S::CH, pg = pg0 + row / PAGE;
+        if (pg < npg)
+          cp_async16(slot + row * HD + ((c ^ (row & 7)) << 2),
+                     kb + (long long)bt[pg] * A.page_stride + (row % PAGE) * HD + c * 4);
+      }
+      const float* q = A.qn + ((size_t)ic.t * A.nh + ic.kvh * REP) * HD;
+      for (int i2 = tid; i2 < REP * S::CH; i2 += S::NT) {
+        const int hh = i2 / S::CH, c = i2 - hh * S::CH;
+        cp_async16(slot + ATT_UNIT * HD + hh * S::QS + c * 4, q + hh * HD + c * 4);
+      }
+      ic.next(A, prefix_s);
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int k = 0; k < SC_SLOTS - 1; k++) issue(k);
+  float mx = -INFINITY;  // running maximum of this thread's head over the current (token, kv head)
+  for (int i = 0; i < count; i++) {
+    cp_async_wait<SC_SLOTS - 2>();
+    __syncthreads();  // unit i has landed for every thread; every thread is done with unit i - 1
+    issue(i + SC_SLOTS - 1);
+    const float* slot = ring + (i % SC_SLOTS) * S::SLOT;
+    const float* kr = slot + r * HD;
+    const float* qh = slot + ATT_UNIT * HD + h * S::QS;
+    // ops::dot (ops.rs:7-36): accumulator m's SIMD lane l sums elements 32i + 8m + l with FMA in
+    // order of i; chunk c holds elements 4c..4c+3, i.e. m = (c % 8) / 2, l = 4 (c % 2) + 0..3
+    float acc[4][8];
+#pragma unroll
+    for (int m = 0; m < 4; m++)
+#pragma unroll
+      for (int l = 0; l < 8; l++) acc[m][l] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < S::CH; c++) {
+      const float4 k4 = *reinterpret_cast<const float4*>(kr + ((c ^ (r & 7)) << 2));
+      const float4 q4 = *reinterpret_cast<const float4*>(qh + (c << 2));
+      const int m = (c & 7) >> 1, l0 = (c & 1) * 4;
+      acc[m][l0 + 0] = __fmaf_rn(q4.x, k4.x, acc[m][l0 + 0]);
+      acc[m][l0 + 1] = __fmaf_rn(q4.y, k4.y, acc[m][l0 + 1]);
+      acc[m][l0 + 2] = __fmaf_rn(q4.z, k4.z, acc[m][l0 + 2]);
+      acc[m][l0 + 3] = __fmaf_rn(q4.w, k4.w, acc[m][l0 + 3]);
+    }
+    float sl[8];
+#pragma unroll
+    for (int l = 0; l < 8; l++) sl[l] = fadd(fadd(acc[0][l], acc[1][l]), fadd(acc[2][l], acc[3][l]));
+    const float tot = fadd(fadd(fadd(sl[0], sl[4]), fadd(sl[2], sl[6])), fadd(fadd(sl[1], sl[5]), fadd(sl[3], sl[7])));
+    const float sc = fmul(tot, scale);
+    const int n = A.pos[cc.t] + 1, j = cc.s * ATT_UNIT + r;
+    const int hq = cc.kvh * REP + h;
+    if (j < n) {
+      A.S[((size_t)cc.t * A.nh + hq) * A.s_stride + j] = sc;
+      mx = fmaxf(mx, sc);
+    }
+    // the (token, kv head) run ends at the CTA's last unit or at its last unit in the head
+    const bool flush = i + 1 == count || cc.s + 1 == cc.nu;
+    if (flush) {
+#pragma unroll
+      for (int o = 1; o < S::PW; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (p == 0 && mx > -INFINITY) atomicMax(A.mkey + (size_t)cc.t * A.nh + hq, f2key(mx));
+      mx = -INFINITY;
+    }
+    cc.next(A, prefix_s);
+  }
+  cp_async_wait<0>();  // no copy may land after the CTA exits
 }
 
 // ------------------------------------------------------------------------------------------
-// Split attention output for batches with enough (token, kv head) pairs to fill the GPU.
-//
-// k_attn_softmax: one CTA per (token, q head). e = exp(s - max) goes back into S and the
+// Softmax denominator: one CTA per (token, q head). e = exp(s - max) goes back into S and the
 // sequential denominator (ops.rs:118-122) is summed by one thread from shared memory while the
 // other warps compute the next chunk's exponentials; 1/sum goes to rinv[t][h].
-// k_attn_pv: one CTA per (token, kv head), thread = output dim, one chain per q head of the group:
-// o_h[d] += (e_h,j * inv_h) * v_j[d] in position order (model.rs:227-232). The kv head's V rows
-// are read once for all its q heads, straight from the pool with a register prefetch of one page
-// (16 rows) ahead; probabilities are staged per 64-position chunk in a 3-slot shared ring.
 // ------------------------------------------------------------------------------------------
 constexpr int SMX_ECH = 1024;   // softmax positions per chunk
 constexpr int SMX_THREADS = 256;
@@ -859,24 +914,15 @@ __device__ __forceinline__ float seq_sum_smem(const float* eb, int cnt, float su
 __global__ void __launch_bounds__(SMX_THREADS) k_attn_softmax(AttnArgs A) {
   constexpr int PER = (SMX_ECH + SMX_THREADS - 33) / (SMX_THREADS - 32);  // exps per thread (warps 1..)
   __shared__ __align__(16) float ebuf[2][SMX_ECH];
-  __shared__ float m_s;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int t = blockIdx.x / A.nh, h = blockIdx.x - t * A.nh;
   pdl_wait();
   pdl_trigger();
   const int pos = A.pos[t];
-  if (pos < 0 || pos >= A.max_pos) return;  // flagged by k_attn_scores
-  const int n = pos + 1, nch = (n + ATT_CHUNK - 1) / ATT_CHUNK;
+  if (!attn_pos_ok(A, pos)) return;  // flagged by k_qk_prep
+  const int n = pos + 1;
   float* erow = A.S + ((size_t)t * A.nh + h) * A.s_stride;
-  if (warp == 0) {  // max over the per-warp chunk maxima
-    const float* cm = A.cmax + ((size_t)t * A.nh + h) * (size_t)A.max_chunks * 8;
-    float m = -INFINITY;
-    for (int c = lane; c < nch * 8; c += 32) m = fmaxf(m, cm[c]);
-    m = warp_max(m);
-    if (lane == 0) m_s = m;
-  }
-  __syncthreads();
-  const float mrow = m_s;
+  const float mrow = key2f(A.mkey[(size_t)t * A.nh + h]);
   const int nchunks = (n + SMX_ECH - 1) / SMX_ECH;
   {
     const int cnt = min(SMX_ECH, n);
@@ -926,219 +972,224 @@ __global__ void __launch_bounds__(SMX_THREADS) k_attn_softmax(AttnArgs A) {
   if (tid == 0) A.rinv[(size_t)t * A.nh + h] = __fdiv_rn(1.0f, sum);
 }
 
-// k_attn_pv shapes: NT output dims (threads, whole warps) per CTA, so HD / NT CTAs per (token, kv
-// head); SLOTS V pages in shared memory per CTA, SLOTS - 2 of them in flight (a CTA issues page
-// pg + SLOTS - 2 while warps may still read page pg - 1). Large batches: many CTAs share each SM,
-// two pages in flight each. Small batches (down to one sequence) use k_attn_pv_hw (one warp per q
-// head, pages staged through registers) because each CTA must stream its whole context alone.
-constexpr int PV_NT_LARGE = 64, PV_SLOTS_LARGE = 4;
-constexpr int PV_DEPTH_SMALL = 16;  // pages in flight per k_attn_pv_hw CTA (held in registers)
-constexpr int PV_SMALL_MAX_PAIRS = 192;  // (token, kv head) pairs up to which k_attn_pv_hw is used (measured crossover)
+// ------------------------------------------------------------------------------------------
+// Value sums. Both kernels stream a (token, kv head)'s V rows and the group's e rows (exp
+// weights, from k_attn_softmax) in stages of PV_STAGE positions through a ring of cp.async
+// copies, one CTA barrier per stage. Each stage's probabilities p = e * inv (ops.rs:124-126) are
+// formed one stage ahead of the chains that use them, so a chain step is one shared-memory V
+// load, one multiply and the dependent add.
+//
+// k_attn_pv (many (token, kv head) pairs): CTA = (token, kv head), thread = output dim, the
+// REP chains of the group's q heads per thread sharing each V load.
+// k_attn_pv_small (few pairs, down to one token): CTA = (token, kv head, 32-dim slice), warp = q
+// head, lane = dim: one chain per thread, so a warp spends ~3 instructions per position and the
+// chain's add latency sets the pace.
+// ------------------------------------------------------------------------------------------
+constexpr int PV_STAGE = 32;        // positions per stage (large kernel)
+constexpr int PV_SLOTS = 5;         // ring slots (large kernel): 3 stages in flight ahead of the chain
+constexpr int PVS_STAGE = 64;       // positions per stage (small kernel)
+constexpr int PVS_SLOTS = 6;        // ring slots (small kernel)
+constexpr int PV_SMALL_MAX_PAIRS = 48;  // (token, kv head) pairs up to which k_attn_pv_small runs
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+template <int HD, int REP>
+struct PvShape {
+  static constexpr int NT = HD;
+  static constexpr int SLOT = PV_STAGE * HD + REP * PV_STAGE;  // V rows, then e rows
+  static constexpr size_t SMEM = (size_t)PV_SLOTS * SLOT * 4;
+};
 
-// CTA = (token, kv head, slice of NT output dims); thread = output dim. Splitting a head's dims over
-// HD / NT CTAs lets a long sequence's value sums run as independent CTAs (no page barrier shared
-// by all of its dims).
-template <int HD, int REP, int NT, int SLOTS>
-__global__ void __launch_bounds__(NT) k_attn_pv(AttnArgs A) {
-  static_assert(NT % 32 == 0 && HD % NT == 0, "whole warps (the output quantization is per warp)");
-  static_assert(REP == 1 || REP == 2 || REP == 4, "GQA group of 1, 2 or 4 q heads");
-  constexpr int AHEAD = SLOTS - 2;
-  constexpr int DS = HD / NT;                // CTAs per (token, kv head)
-  constexpr int RSEG = NT / 4;               // 16-byte segments per V row slice
-  constexpr int SEG = PAGE * RSEG;           // per page
-  constexpr int ESEG = REP * PAGE / 4;       // 16-byte segments of e per page (one row piece per head)
-  extern __shared__ __align__(16) unsigned char dsm[];
-  float* v_s = reinterpret_cast<float*>(dsm);                                   // [SLOTS][PAGE][NT]
-  float* e_s = v_s + (size_t)SLOTS * PAGE * NT;                                 // [SLOTS][REP][PAGE]
-  int* bt_s = reinterpret_cast<int*>(e_s + (size_t)SLOTS * REP * PAGE);        // page ids
-  __shared__ __align__(16) float p_s[PAGE][4];  // p of each row of the current page for the group's heads
-  __shared__ float inv_s[REP];
-  const int tid = threadIdx.x, lane = tid & 31;
-  const int slice = blockIdx.x % DS, tk = blockIdx.x / DS;
-  const int t = tk / A.nkv, kvh = tk - t * A.nkv, d = slice * NT + tid;
-  const int pos = A.pos[t];  // positions and page ids are older than the previous kernel
-  if (pos < 0 || pos >= A.max_pos) {  // flagged by k_attn_scores
-    pdl_wait();
-    pdl_trigger();
-    return;
-  }
-  const int n = pos + 1, npages = (n + PAGE - 1) / PAGE;
-  const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
-  for (int p = tid; p < npages; p += NT) bt_s[p] = bt[p];
-  const int h0 = kvh * REP;
-  pdl_wait();  // 1/sum and e come from k_attn_softmax
-  pdl_trigger();
-  if (tid < REP) inv_s[tid] = A.rinv[(size_t)t * A.nh + h0 + tid];
-  const float* erow0 = A.S + ((size_t)t * A.nh + h0) * A.s_stride;
-  const float* vpage0 = A.v_pool + (long long)kvh * PAGE * HD + slice * NT;
-  // page pg's V rows of this slice and its e (exp weights) of every head of the group into slot
-  // pg % SLOTS: one commit group per page. e rows run to s_stride >= npages * PAGE.
-  auto issue = [&](int pg) {
-    if (pg < npages) {
-      const float* src = vpage0 + (long long)bt_s[pg] * A.page_stride;
-      float* dst = v_s + (size_t)(pg % SLOTS) * PAGE * NT;
-#pragma unroll
-      for (int sg = tid; sg < SEG; sg += NT) {
-        const int row = sg / RSEG, col = sg - row * RSEG;
-        cp_async16(dst + row * NT + col * 4, src + row * HD + col * 4);
-      }
-      if (tid < ESEG) {
-        const int r = tid / (PAGE / 4), q = tid - r * (PAGE / 4);
-        cp_async16(e_s + ((size_t)(pg % SLOTS) * REP + r) * PAGE + q * 4, erow0 + (size_t)r * A.s_stride + pg * PAGE + q * 4);
-      }
-    }
-    cp_async_commit();
-  };
-  float o[REP];
-#pragma unroll
-  for (int r = 0; r < REP; r++) o[r] = 0.0f;
-  __syncthreads();  // bt_s, inv_s
-#pragma unroll
-  for (int k = 0; k < AHEAD; k++) issue(k);
-  for (int pg = 0; pg < npages; pg++) {
-    // slot (pg + AHEAD) % SLOTS is not read by any thread (AHEAD <= SLOTS - 2; every thread is past
-    // page pg - 2, and pg - 1 uses another slot)
-    issue(pg + AHEAD);
-    cp_async_wait<AHEAD>();  // this thread's copies of page pg have landed
-    __syncthreads();         // everyone's have, and everyone is done with page pg - 1
-    const int slot = pg % SLOTS;
-    for (int idx = tid; idx < PAGE * REP; idx += NT) {
-      const int r = idx / PAGE, j = idx - r * PAGE;
-      p_s[j][r] = fmul(e_s[((size_t)slot * REP + r) * PAGE + j], inv_s[r]);  // softmax p (ops.rs:124-126)
-    }
-    __syncthreads();
-    const float* vs = v_s + (size_t)slot * PAGE * NT + tid;
-    const float4* pq = reinterpret_cast<const float4*>(&p_s[0][0]);
-    const int rows = min(PAGE, n - pg * PAGE);
-    auto step = [&](int r) {
-      const float4 p = pq[r];
-      const float v = vs[r * NT];
-      o[0] = fadd(o[0], fmul(p.x, v));
-      if (REP > 1) o[REP > 1 ? 1 : 0] = fadd(o[REP > 1 ? 1 : 0], fmul(p.y, v));
-      if (REP > 2) o[REP > 2 ? 2 : 0] = fadd(o[REP > 2 ? 2 : 0], fmul(p.z, v));
-      if (REP > 3) o[REP > 3 ? 3 : 0] = fadd(o[REP > 3 ? 3 : 0], fmul(p.w, v));
-    };
-    if (rows == PAGE) {
-#pragma unroll
-      for (int r = 0; r < PAGE; r++) step(r);
-    } else {
-      for (int r = 0; r < rows; r++) step(r);
-    }
-  }
-  cp_async_wait<0>();  // no copy may land after the CTA exits
-  const int qd = A.nh * HD;
-#pragma unroll
-  for (int r = 0; r < REP; r++) {
-    const int hd = (h0 + r) * HD + d;
-    if (A.out) A.out[(size_t)t * qd + hd] = o[r];
-    if (A.qo) {  // a warp holds one 32-block of the head
-      float dq;
-      int8_t q = quant_lane(o[r], &dq);
-      const int nbq = qd >> 5;
-      A.qo[(size_t)t * qd + q8_pos(hd, nbq)] = q;
-      if (lane == 0) A.so[(size_t)t * q8_ss(nbq) + (hd >> 5)] = dq;
-    }
-  }
-}
-
-// Small batches: CTA = (token, kv head, 32-dim slice), one warp per q head of the group (lane =
-// output dim), all warps reading the same staged pages. A warp does one chain per lane, about four
-// instructions per position. The pages come in through registers: each thread holds its 16-byte
-// piece of the next D pages (plain 128-bit loads keep far more bytes in flight per CTA than
-// cp.async here), stores one page per step into a shared double buffer, and the warps chain over it.
-template <int HD, int REP, int D>
-__global__ void __launch_bounds__(32 * REP) k_attn_pv_hw(AttnArgs A) {
-  static_assert(HD % 32 == 0 && REP == 4, "32-dim slices, GQA group of 4 (one 16-byte V piece per thread)");
-  constexpr int NT = 32 * REP, DS = HD / 32;
-  constexpr int ESEG = REP * PAGE / 4;  // 16-byte pieces of e per page
-  extern __shared__ __align__(16) unsigned char dsm[];
-  int* bt_s = reinterpret_cast<int*>(dsm);  // page ids
-  __shared__ __align__(16) float v_s[2][PAGE][32];
-  __shared__ __align__(16) float e_s[2][REP][PAGE];
-  __shared__ __align__(16) float p_s[REP][PAGE];
-  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  const int slice = blockIdx.x % DS, tk = blockIdx.x / DS;
-  const int t = tk / A.nkv, kvh = tk - t * A.nkv, d = slice * 32 + lane, h = kvh * REP + w;
-  const int pos = A.pos[t];  // positions, page ids and V rows are older than the previous kernel
-  if (pos < 0 || pos >= A.max_pos) {  // flagged by k_attn_scores
-    pdl_wait();
-    pdl_trigger();
-    return;
-  }
-  const int n = pos + 1, npages = (n + PAGE - 1) / PAGE;
-  const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
-  for (int p = tid; p < npages; p += NT) bt_s[p] = bt[p];
-  // this thread's pieces: V row tid / 8, dims 4 * (tid % 8) .. + 3 of the slice; e piece tid (< ESEG)
-  const int vrow = tid >> 3, vcol = (tid & 7) * 4;
-  const float* vsrc = A.v_pool + (long long)kvh * PAGE * HD + slice * 32 + vrow * HD + vcol;
-  const int er = tid / (PAGE / 4), eq = tid - er * (PAGE / 4);
-  const float* esrc = A.S + ((size_t)t * A.nh + kvh * REP + (tid < ESEG ? er : 0)) * A.s_stride + eq * 4;
-  auto load_v = [&](int pg, float4& v) {
-    if (pg < npages) v = __ldg(reinterpret_cast<const float4*>(vsrc + (long long)bt_s[pg] * A.page_stride));
-  };
-  auto load_e = [&](int pg, float4& e) {  // e rows run to s_stride >= npages * PAGE
-    if (pg < npages && tid < ESEG) e = *reinterpret_cast<const float4*>(esrc + pg * PAGE);
-  };
-  auto load = [&](int pg, float4& v, float4& e) {
-    load_v(pg, v);
-    load_e(pg, e);
-  };
-  float4 rv[D], re[D];
-  float o = 0.0f;
-  __syncthreads();  // bt_s
-#pragma unroll
-  for (int k = 0; k < D; k++) load_v(k, rv[k]);
-  pdl_wait();  // 1/sum and e come from k_attn_softmax
-  pdl_trigger();
-  const float inv = A.rinv[(size_t)t * A.nh + h];
-#pragma unroll
-  for (int k = 0; k < D; k++) load_e(k, re[k]);
-  for (int pg0 = 0; pg0 < npages; pg0 += D) {
-#pragma unroll
-    for (int k = 0; k < D; k++) {
-      const int pg = pg0 + k;
-      if (pg >= npages) break;  // uniform over the CTA
-      // buffer pg & 1 was last read for page pg - 2, before the previous step's barrier
-      *reinterpret_cast<float4*>(&v_s[pg & 1][vrow][vcol]) = rv[k];
-      if (tid < ESEG) *reinterpret_cast<float4*>(&e_s[pg & 1][er][eq * 4]) = re[k];
-      load(pg + D, rv[k], re[k]);
-      __syncthreads();
-      if (lane < PAGE) p_s[w][lane] = fmul(e_s[pg & 1][w][lane], inv);  // ops.rs:124-126
-      __syncwarp();
-      const float* vs = &v_s[pg & 1][0][lane];
-      const float4* pq = reinterpret_cast<const float4*>(&p_s[w][0]);
-      const int rows = min(PAGE, n - pg * PAGE);
-      if (rows == PAGE) {
-#pragma unroll
-        for (int q = 0; q < PAGE / 4; q++) {
-          const float4 p = pq[q];
-          o = fadd(o, fmul(p.x, vs[(4 * q + 0) * 32]));
-          o = fadd(o, fmul(p.y, vs[(4 * q + 1) * 32]));
-          o = fadd(o, fmul(p.z, vs[(4 * q + 2) * 32]));
-          o = fadd(o, fmul(p.w, vs[(4 * q + 3) * 32]));
-        }
-      } else {
-        for (int r = 0; r < rows; r++) o = fadd(o, fmul(p_s[w][r], vs[r * 32]));
-      }
-    }
-  }
-  const int qd = A.nh * HD, hd = h * HD + d;
+// quantize the finished chain value o of (token t, output element hd) for the output projection
+__device__ __forceinline__ void pv_emit(const AttnArgs& A, int t, int hd, float o) {
+  const int qd = A.nh * A.hd, lane = threadIdx.x & 31;
   if (A.out) A.out[(size_t)t * qd + hd] = o;
-  if (A.qo) {  // the warp holds one 32-block of the head
+  if (A.qo) {  // a warp holds one 32-block of the head
     float dq;
     int8_t q = quant_lane(o, &dq);
     const int nbq = qd >> 5;
     A.qo[(size_t)t * qd + q8_pos(hd, nbq)] = q;
     if (lane == 0) A.so[(size_t)t * q8_ss(nbq) + (hd >> 5)] = dq;
   }
+}
+
+template <int HD, int REP>
+__global__ void __launch_bounds__(HD) k_attn_pv(AttnArgs A) {
+  static_assert(HD % 32 == 0 && (REP == 1 || REP == 2 || REP == 4), "whole warps; GQA group of 1, 2 or 4");
+  using S = PvShape<HD, REP>;
+  extern __shared__ __align__(16) float pv_smem[];
+  __shared__ __align__(16) float p_s[2][PV_STAGE][4];
+  const int tid = threadIdx.x;
+  const int t = blockIdx.x / A.nkv, kvh = blockIdx.x - t * A.nkv, h0 = kvh * REP;
+  const int pos = A.pos[t];  // positions and page ids are older than the previous kernel
+  if (!attn_pos_ok(A, pos)) {  // flagged by k_qk_prep
+    pdl_wait();
+    pdl_trigger();
+    return;
+  }
+  const int n = pos + 1, nst = (n + PV_STAGE - 1) / PV_STAGE, npg = pos / PAGE + 1;
+  const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
+  const float* vb = A.v_pool + (long long)kvh * PAGE * HD;
+  const float* e0 = A.S + ((size_t)t * A.nh + h0) * A.s_stride;
+  // V rows (older than the previous kernel) may be fetched before the wait; the e rows may not, so
+  // the ring is filled after it
+  pdl_wait();
+  pdl_trigger();
+  // 1/sum of the head of each (position, head) pair this thread forms p for in make_p
+  constexpr int PK = (REP * PV_STAGE + S::NT - 1) / S::NT;
+  float inv_k[PK];
+#pragma unroll
+  for (int k = 0; k < PK; k++) {
+    const int i = tid + k * S::NT;
+    inv_k[k] = i < REP * PV_STAGE ? A.rinv[(size_t)t * A.nh + h0 + i / PV_STAGE] : 0.0f;
+  }
+  auto issue = [&](int st) {
+    if (st < nst) {
+      float* slot = pv_smem + (st % PV_SLOTS) * S::SLOT;
+#pragma unroll
+      for (int i = tid; i < PV_STAGE * HD / 4; i += S::NT) {
+        const int row = i / (HD / 4), c = i - row * (HD / 4), pg = st * (PV_STAGE / PAGE) + row / PAGE;
+        if (pg < npg) cp_async16(slot + row * HD + c * 4, vb + (long long)bt[pg] * A.page_stride + (row % PAGE) * HD + c * 4);
+      }
+      if (tid < REP * PV_STAGE / 4) {  // e rows run to s_stride >= npg * PAGE
+        const int r = tid / (PV_STAGE / 4), q = tid - r * (PV_STAGE / 4);
+        if (st * PV_STAGE + q * 4 < npg * PAGE)
+          cp_async16(slot + PV_STAGE * HD + r * PV_STAGE + q * 4, e0 + (size_t)r * A.s_stride + st * PV_STAGE + q * 4);
+      }
+    }
+    cp_async_commit();
+  };
+  // p of stage st into p_s[st & 1] (threads cover (position, head) pairs)
+  auto make_p = [&](int st) {
+    if (st < nst) {
+      const float* es = pv_smem + (st % PV_SLOTS) * S::SLOT + PV_STAGE * HD;
+#pragma unroll
+      for (int k = 0; k < PK; k++) {
+        const int i = tid + k * S::NT, r = i / PV_STAGE, j = i - r * PV_STAGE;
+        if (i < REP * PV_STAGE) p_s[st & 1][j][r] = fmul(es[r * PV_STAGE + j], inv_k[k]);
+      }
+    }
+  };
+#pragma unroll
+  for (int k = 0; k < PV_SLOTS - 1; k++) issue(k);
+  cp_async_wait<PV_SLOTS - 2>();
+  __syncthreads();
+  make_p(0);
+  float o[REP];
+#pragma unroll
+  for (int r = 0; r < REP; r++) o[r] = 0.0f;
+  for (int st = 0; st < nst; st++) {
+    // stages <= st + 1 have landed (issued: up to st + PV_SLOTS - 2); p of stage st is in p_s
+    cp_async_wait<PV_SLOTS - 3>();
+    __syncthreads();  // also: every thread is done with stage st - 1 (its slot and p_s buffer)
+    issue(st + PV_SLOTS - 1);
+    make_p(st + 1);
+    const float* vs = pv_smem + (st % PV_SLOTS) * S::SLOT + tid;
+    const float4* pq = reinterpret_cast<const float4*>(&p_s[st & 1][0][0]);
+    const int rows = min(PV_STAGE, n - st * PV_STAGE);
+    auto step = [&](int j) {
+      const float4 pj = pq[j];
+      const float v = vs[j * HD];
+      o[0] = fadd(o[0], fmul(pj.x, v));
+      if (REP > 1) o[REP > 1 ? 1 : 0] = fadd(o[REP > 1 ? 1 : 0], fmul(pj.y, v));
+      if (REP > 2) o[REP > 2 ? 2 : 0] = fadd(o[REP > 2 ? 2 : 0], fmul(pj.z, v));
+      if (REP > 3) o[REP > 3 ? 3 : 0] = fadd(o[REP > 3 ? 3 : 0], fmul(pj.w, v));
+    };
+    if (rows == PV_STAGE) {
+#pragma unroll
+      for (int j = 0; j < PV_STAGE; j++) step(j);
+    } else {
+      for (int j = 0; j < rows; j++) step(j);
+    }
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int r = 0; r < REP; r++) pv_emit(A, t, (h0 + r) * HD + tid, o[r]);
+}
+
+template <int REP>
+struct PvSmallShape {
+  static constexpr int NT = 32 * REP;
+  static constexpr int SLOT = PVS_STAGE * 32 + REP * PVS_STAGE;  // V rows of the slice, then e rows
+  static constexpr size_t SMEM = (size_t)PVS_SLOTS * SLOT * 4;
+};
+
+template <int HD, int REP>
+__global__ void __launch_bounds__(32 * REP) k_attn_pv_small(AttnArgs A) {
+  static_assert(HD % 32 == 0 && (REP == 1 || REP == 2 || REP == 4), "32-dim slices; GQA group of 1, 2 or 4");
+  using S = PvSmallShape<REP>;
+  constexpr int DS = HD / 32;  // slices per head
+  extern __shared__ __align__(16) float pv_smem[];
+  __shared__ __align__(16) float p_s[REP][2][PVS_STAGE];  // per warp (head), double-buffered
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int slice = blockIdx.x % DS, tk = blockIdx.x / DS;
+  const int t = tk / A.nkv, kvh = tk - t * A.nkv, h = kvh * REP + w, d = slice * 32 + lane;
+  const int pos = A.pos[t];
+  if (!attn_pos_ok(A, pos)) {  // flagged by k_qk_prep
+    pdl_wait();
+    pdl_trigger();
+    return;
+  }
+  const int n = pos + 1, nst = (n + PVS_STAGE - 1) / PVS_STAGE, npg = pos / PAGE + 1;
+  const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
+  const float* vb = A.v_pool + (long long)kvh * PAGE * HD + slice * 32;
+  const float* e0 = A.S + ((size_t)t * A.nh + kvh * REP) * A.s_stride;
+  pdl_wait();
+  pdl_trigger();
+  const float inv = A.rinv[(size_t)t * A.nh + h];
+  auto issue = [&](int st) {
+    if (st < nst) {
+      float* slot = pv_smem + (st % PVS_SLOTS) * S::SLOT;
+#pragma unroll
+      for (int i = tid; i < PVS_STAGE * 8; i += S::NT) {  // 8 chunks per 32-float row slice
+        const int row = i >> 3, c = i & 7, pg = st * (PVS_STAGE / PAGE) + row / PAGE;
+        if (pg < npg) cp_async16(slot + row * 32 + c * 4, vb + (long long)bt[pg] * A.page_stride + (row % PAGE) * HD + c * 4);
+      }
+      for (int i = tid; i < REP * PVS_STAGE / 4; i += S::NT) {
+        const int r = i / (PVS_STAGE / 4), q = i - r * (PVS_STAGE / 4);
+        if (st * PVS_STAGE + q * 4 < npg * PAGE)
+          cp_async16(slot + PVS_STAGE * 32 + r * PVS_STAGE + q * 4, e0 + (size_t)r * A.s_stride + st * PVS_STAGE + q * 4);
+      }
+    }
+    cp_async_commit();
+  };
+  // this warp's p of stage st (lane j covers positions j, j + 32)
+  auto make_p = [&](int st) {
+    if (st < nst) {
+      const float* es = pv_smem + (st % PVS_SLOTS) * S::SLOT + PVS_STAGE * 32 + w * PVS_STAGE;
+#pragma unroll
+      for (int j = lane; j < PVS_STAGE; j += 32) p_s[w][st & 1][j] = fmul(es[j], inv);
+    }
+  };
+#pragma unroll
+  for (int k = 0; k < PVS_SLOTS - 1; k++) issue(k);
+  cp_async_wait<PVS_SLOTS - 2>();
+  __syncthreads();
+  make_p(0);
+  float o = 0.0f;
+  for (int st = 0; st < nst; st++) {
+    cp_async_wait<PVS_SLOTS - 3>();
+    __syncthreads();  // stage st + 1 landed; every warp is done with stage st - 1
+    issue(st + PVS_SLOTS - 1);
+    make_p(st + 1);  // p_s[w][(st + 1) & 1] was last read by this warp's chain over stage st - 1
+    __syncwarp();
+    const float* vs = pv_smem + (st % PVS_SLOTS) * S::SLOT + lane;
+    const float4* pq = reinterpret_cast<const float4*>(&p_s[w][st & 1][0]);
+    const int rows = min(PVS_STAGE, n - st * PVS_STAGE);
+    if (rows == PVS_STAGE) {
+#pragma unroll
+      for (int q = 0; q < PVS_STAGE / 4; q++) {
+        const float4 pj = pq[q];
+        o = fadd(o, fmul(pj.x, vs[(4 * q + 0) * 32]));
+        o = fadd(o, fmul(pj.y, vs[(4 * q + 1) * 32]));
+        o = fadd(o, fmul(pj.z, vs[(4 * q + 2) * 32]));
+        o = fadd(o, fmul(pj.w, vs[(4 * q + 3) * 32]));
+      }
+    } else {
+      for (int j = 0; j < rows; j++) o = fadd(o, fmul(p_s[w][st & 1][j], vs[j * 32]));
+    }
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+  pv_emit(A, t, h * HD + d, o);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -1294,70 +1345,85 @@ void launch_ffn(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaStrea
   }
 }
 
-int attn_grid(int T, int nkv, int max_chunks) {
-  long long items = (long long)T * nkv * max_chunks;
-  long long g = items < 4 * 148 ? items : 4 * 148;
-  return (int)(g > 0 ? g : 1);
+// SMs of each device (set by prepare_attn, before any capture)
+static int g_attn_sms[64];
+
+template <int HD, int REP>
+static size_t scores_smem(int T) {
+  return (size_t)SC_SLOTS * ScoresShape<HD, REP>::SLOT * 4 + (((size_t)T + 1) * 4 + 15) / 16 * 16;
 }
 
-template <int HD, int NT>
-constexpr int pv_nt() { return NT < HD ? NT : HD; }
-
-// dynamic shared memory of k_attn_pv: the V and e rings, then the page ids
-constexpr size_t pv_smem(int nt, int slots, int rep, int bt_stride) {
-  return (size_t)slots * PAGE * nt * 4 + (size_t)slots * rep * PAGE * 4 + (size_t)bt_stride * 4;
-}
-
-template <int HD, int REP, int NT, int SLOTS>
-static void launch_pv(const AttnArgs& A, cudaStream_t st) {
-  launch_pdl(A.T <= PDL_MAX_T, k_attn_pv<HD, REP, NT, SLOTS>, dim3(A.T * A.nkv * (HD / NT)), dim3(NT), pv_smem(NT, SLOTS, REP, A.bt_stride),
-             st, A);
+// Units are dealt to the scores CTAs in contiguous runs, so the grid only needs to fill the GPU:
+// every resident CTA slot, or one CTA per unit when there are fewer units than that.
+template <int HD, int REP>
+static int scores_grid(const AttnArgs& A, size_t smem) {
+  int dev = 0, per_sm = 1;
+  cudaGetDevice(&dev);
+  const int sms = (dev >= 0 && dev < 64 && g_attn_sms[dev] > 0) ? g_attn_sms[dev] : 148;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_attn_scores<HD, REP>, 32 * REP, smem);
+  const long long units = (long long)A.T * A.nkv * ((A.max_pos + ATT_UNIT - 1) / ATT_UNIT);
+  const long long g = std::min<long long>(units, (long long)sms * std::max(per_sm, 1));
+  return (int)std::max<long long>(g, 1);
 }
 
 template <int HD, int REP>
-static cudaError_t launch_attn_t(const AttnArgs& A, int grid, cudaStream_t st, int which) {
+static cudaError_t launch_attn_t(const AttnArgs& A, cudaStream_t st, int which) {
+  const bool pdl = A.T <= PDL_MAX_T;
   if (which & 1) {
     const int nw = A.nh + A.nkv;
-    launch_pdl(A.T <= PDL_MAX_T, k_qk_prep<HD>, dim3(A.T), dim3(32 * nw), (size_t)nw * HD * 4, st, A);
-    launch_pdl(A.T <= PDL_MAX_T, k_attn_scores<HD, REP>, dim3(grid), dim3(256), 0, st, A);
+    launch_pdl(pdl, k_qk_prep<HD>, dim3(A.T), dim3(32 * nw), (size_t)nw * HD * 4, st, A);
+    const size_t sm = scores_smem<HD, REP>(A.T);
+    launch_pdl(pdl, k_attn_scores<HD, REP>, dim3(scores_grid<HD, REP>(A, sm)), dim3(32 * REP), sm, st, A);
   }
   if (which & 2) {
-    launch_pdl(A.T <= PDL_MAX_T, k_attn_softmax, dim3(A.T * A.nh), dim3(SMX_THREADS), 0, st, A);
-    if (REP == 4 && A.T * A.nkv <= PV_SMALL_MAX_PAIRS)
-      launch_pdl(A.T <= PDL_MAX_T, k_attn_pv_hw<HD, 4, PV_DEPTH_SMALL>, dim3(A.T * A.nkv * (HD / 32)), dim3(128), (size_t)A.bt_stride * 4, st, A);
+    launch_pdl(pdl, k_attn_softmax, dim3(A.T * A.nh), dim3(SMX_THREADS), 0, st, A);
+    if (A.T * A.nkv <= PV_SMALL_MAX_PAIRS)
+      launch_pdl(pdl, k_attn_pv_small<HD, REP>, dim3(A.T * A.nkv * (HD / 32)), dim3(32 * REP),
+                 PvSmallShape<REP>::SMEM, st, A);
     else
-      launch_pv<HD, REP, pv_nt<HD, PV_NT_LARGE>(), PV_SLOTS_LARGE>(A, st);
+      launch_pdl(pdl, k_attn_pv<HD, REP>, dim3(A.T * A.nkv), dim3(HD), PvShape<HD, REP>::SMEM, st, A);
   }
   return cudaGetLastError();
 }
 
-static cudaError_t launch_attn_which(const AttnArgs& A, int grid, cudaStream_t st, int which) {
+static cudaError_t launch_attn_which(const AttnArgs& A, cudaStream_t st, int which) {
   int rep = A.nh / A.nkv;
-  if (A.bt_stride > ATT_MAX_BT || !A.rinv || !A.qn || A.nh + A.nkv > 32) return cudaErrorInvalidValue;
-  if (A.hd == 128 && rep == 4) return launch_attn_t<128, 4>(A, grid, st, which);
-  if (A.hd == 64 && rep == 4) return launch_attn_t<64, 4>(A, grid, st, which);
-  if (A.hd == 128 && rep == 2) return launch_attn_t<128, 2>(A, grid, st, which);
-  if (A.hd == 64 && rep == 2) return launch_attn_t<64, 2>(A, grid, st, which);
-  if (A.hd == 128 && rep == 1) return launch_attn_t<128, 1>(A, grid, st, which);
-  if (A.hd == 64 && rep == 1) return launch_attn_t<64, 1>(A, grid, st, which);
+  if (A.T < 1 || A.T > SC_MAX_T || !A.rinv || !A.qn || !A.mkey || A.nh + A.nkv > 32 || A.page_stride % 4 != 0)
+    return cudaErrorInvalidValue;
+  if (A.hd == 128 && rep == 4) return launch_attn_t<128, 4>(A, st, which);
+  if (A.hd == 64 && rep == 4) return launch_attn_t<64, 4>(A, st, which);
+  if (A.hd == 128 && rep == 2) return launch_attn_t<128, 2>(A, st, which);
+  if (A.hd == 64 && rep == 2) return launch_attn_t<64, 2>(A, st, which);
+  if (A.hd == 128 && rep == 1) return launch_attn_t<128, 1>(A, st, which);
+  if (A.hd == 64 && rep == 1) return launch_attn_t<64, 1>(A, st, which);
   return cudaErrorInvalidValue;
 }
-cudaError_t launch_attn_scores_only(const AttnArgs& A, int grid, cudaStream_t st) {
-  return launch_attn_which(A, grid, st, 1);
-}
-cudaError_t launch_attn_out_only(const AttnArgs& A, cudaStream_t st) { return launch_attn_which(A, 1, st, 2); }
+cudaError_t launch_attn_scores_only(const AttnArgs& A, cudaStream_t st) { return launch_attn_which(A, st, 1); }
+cudaError_t launch_attn_out_only(const AttnArgs& A, cudaStream_t st) { return launch_attn_which(A, st, 2); }
 
-// Opt in to the ring's dynamic shared memory on the current device (call before any launch or
-// graph capture).
+// Opt in to the kernels' dynamic shared memory and record the SM count on the current device
+// (call before any launch or graph capture).
 template <int HD, int REP>
 static cudaError_t prepare_attn_t() {
-  // the V rings plus up to ATT_MAX_BT page ids
-  constexpr int NL = pv_nt<HD, PV_NT_LARGE>();
-  return cudaFuncSetAttribute((const void*)k_attn_pv<HD, REP, NL, PV_SLOTS_LARGE>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pv_smem(NL, PV_SLOTS_LARGE, REP, ATT_MAX_BT));
+  cudaError_t e = cudaFuncSetAttribute((const void*)k_attn_scores<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)scores_smem<HD, REP>(SC_MAX_T));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute((const void*)k_attn_pv<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)PvShape<HD, REP>::SMEM);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute((const void*)k_attn_pv_small<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)PvSmallShape<REP>::SMEM);
+  return e;
 }
 
 cudaError_t prepare_attn(int hd, int rep) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < 64) {
+    e = cudaDeviceGetAttribute(&g_attn_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+  }
   if (hd == 128 && rep == 4) return prepare_attn_t<128, 4>();
   if (hd == 64 && rep == 4) return prepare_attn_t<64, 4>();
   if (hd == 128 && rep == 2) return prepare_attn_t<128, 2>();
@@ -1367,7 +1433,7 @@ cudaError_t prepare_attn(int hd, int rep) {
   return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_attn_args(const AttnArgs& A, int grid, cudaStream_t st) { return launch_attn_which(A, grid, st, 3); }
+cudaError_t launch_attn_args(const AttnArgs& A, cudaStream_t st) { return launch_attn_which(A, st, 3); }
 
 void launch_quant_rows(const float* x, int rows, int cols, int8_t* q, float* s, cudaStream_t st) {
   k_quant_rows<<<rows, 256, 0, st>>>(x, cols, q, s);

@@ -190,7 +190,6 @@ void alloc_work(hg_engine* e) {
   const int T = e->max_batch;
   const int d = c.d_model, qd = D.qd, qkvd = D.qkvd, k = c.top_k, ne = c.n_experts, f = c.expert_ffn;
   const int ss_d = host_q8_ss(d), ss_q = host_q8_ss(qd);
-  const int max_chunks = (c.context_length + ATT_CHUNK - 1) / ATT_CHUNK;
   const int act_stride = std::max(c.dense_ffn, (k + 1) * f);
   // prefill sizing
   const int PF = e->pf_rows;
@@ -234,8 +233,7 @@ void alloc_work(hg_engine* e) {
   B.y = a.take<float>((size_t)T * (k + 1) * d);
   B.s_stride = ((long long)c.context_length + 15) & ~15LL;
   B.S = a.take<float>((size_t)T * c.n_heads * B.s_stride);
-  B.cmax = a.take<float>((size_t)T * c.n_heads * max_chunks * 8);
-  B.max_chunks = max_chunks;
+  B.mkey = a.take<uint32_t>((size_t)T * c.n_heads);
   B.rinv = a.take<float>((size_t)T * c.n_heads);
   B.qn = a.take<float>((size_t)T * D.qd);
   B.logits = a.take<float>((size_t)T * c.vocab_size);
@@ -442,7 +440,6 @@ AttnArgs make_attn_args(hg_engine* e, const DecodeBufs& B, int l) {
   A.hd = c.head_dim;
   A.max_pos = c.context_length;
   A.bt_stride = e->bt_stride;
-  A.max_chunks = B.max_chunks;
   A.eps = c.rms_eps;
   A.qkv = B.qkv;
   A.qkv_stride = e->D.qkvd;
@@ -458,7 +455,7 @@ AttnArgs make_attn_args(hg_engine* e, const DecodeBufs& B, int l) {
   A.page_stride = e->page_stride;
   A.S = B.S;
   A.s_stride = B.s_stride;
-  A.cmax = B.cmax;
+  A.mkey = B.mkey;
   A.rinv = B.rinv;
   A.qn = B.qn;
   A.out = nullptr;
@@ -477,7 +474,7 @@ void record_decode(hg_engine* e, const DecodeBufs& B) {
     launch_pre_norm(D, B, mode, e->embd, Ld.attn_norm, B.qa, B.sa, nullptr, 1, 0, st);
     launch_mv_store(D, B, Ld.qkv, B.qa, B.sa, B.qkv, D.qkvd, st);
     AttnArgs A = make_attn_args(e, B, l);
-    HG_CUDA(launch_attn_args(A, attn_grid(B.T, D.nkv, B.max_chunks), st));
+    HG_CUDA(launch_attn_args(A, st));
     launch_mv_resid(D, B, Ld.wo, B.qo, B.so, st);
     launch_route(D, B, Ld, l, 0, st);
     launch_ffn(D, B, Ld, st);
@@ -1135,9 +1132,8 @@ MoeScratch moe_scratch_layout(const hg_moe_weights* w, int ntok) {
 
 size_t kv_s_stride(const hg_kv_attn_args* a) { return ((size_t)a->max_pos + 15) & ~size_t(15); }
 size_t kv_scratch_bytes(const hg_kv_attn_args* a) {
-  int max_chunks = (a->max_pos + ATT_CHUNK - 1) / ATT_CHUNK;
   return align256((size_t)a->n_seqs * a->n_heads * kv_s_stride(a) * 4) +
-         align256((size_t)a->n_seqs * a->n_heads * max_chunks * 8 * 4) +
+         align256((size_t)a->n_seqs * a->n_heads * 4) +
          align256((size_t)a->n_seqs * a->n_heads * 4) + align256((size_t)a->n_seqs * a->n_heads * a->head_dim * 4) + 256;
 }
 
@@ -1348,13 +1344,12 @@ int hg_debug_time_attention(hg_engine* e, hg_seq** seqs, int n, int iters, float
     DecodeBufs B = step_bufs(e, n);
     // the qkv buffer holds the last decode step's projections of the last layer
     AttnArgs A = make_attn_args(e, B, e->cfg.n_layers - 1);
-    const int grid = attn_grid(n, e->D.nkv, B.max_chunks);
     cudaEvent_t ev[3];
     for (auto& x : ev) HG_CUDA(cudaEventCreate(&x));
     float tot_s = 0, tot_o = 0;
     for (int it = 0; it < iters; it++) {
       HG_CUDA(cudaEventRecord(ev[0], st));
-      HG_CUDA(launch_attn_scores_only(A, grid, st));
+      HG_CUDA(launch_attn_scores_only(A, st));
       HG_CUDA(cudaEventRecord(ev[1], st));
       HG_CUDA(launch_attn_out_only(A, st));
       HG_CUDA(cudaEventRecord(ev[2], st));
@@ -1520,7 +1515,6 @@ int hg_op_kv_attn(const hg_kv_attn_args* a, void* scratch, void* stream) {
     need(a->n_seqs > 0 && a->n_seqs <= 256, "n_seqs must be in 1..256");
     need(a->n_heads > 0 && a->n_kv_heads > 0 && a->n_heads % a->n_kv_heads == 0, "bad head counts");
     cudaStream_t st = as_stream(stream);
-    int max_chunks = (a->max_pos + ATT_CHUNK - 1) / ATT_CHUNK;
     char* base = static_cast<char*>(scratch);
     {
       cudaError_t pe = prepare_attn(a->head_dim, a->n_heads / a->n_kv_heads);
@@ -1534,7 +1528,6 @@ int hg_op_kv_attn(const hg_kv_attn_args* a, void* scratch, void* stream) {
     A.hd = a->head_dim;
     A.max_pos = a->max_pos;
     A.bt_stride = a->bt_stride;
-    A.max_chunks = max_chunks;
     A.eps = a->eps;
     A.qkv = a->qkv;
     A.qkv_stride = (a->n_heads + 2 * a->n_kv_heads) * a->head_dim;
@@ -1551,14 +1544,14 @@ int hg_op_kv_attn(const hg_kv_attn_args* a, void* scratch, void* stream) {
     A.s_stride = (long long)kv_s_stride(a);
     A.S = reinterpret_cast<float*>(base);
     const size_t s_bytes = align256((size_t)a->n_seqs * a->n_heads * A.s_stride * 4);
-    A.cmax = reinterpret_cast<float*>(base + s_bytes);
-    A.rinv = reinterpret_cast<float*>(base + s_bytes + align256((size_t)a->n_seqs * a->n_heads * max_chunks * 8 * 4));
+    A.mkey = reinterpret_cast<uint32_t*>(base + s_bytes);
+    A.rinv = reinterpret_cast<float*>(base + s_bytes + align256((size_t)a->n_seqs * a->n_heads * 4));
     A.qn = reinterpret_cast<float*>(reinterpret_cast<char*>(A.rinv) + align256((size_t)a->n_seqs * a->n_heads * 4));
     A.err = nullptr;
     A.out = a->out;
     A.qo = nullptr;
     A.so = nullptr;
-    cudaError_t err = launch_attn_args(A, attn_grid(A.T, A.nkv, max_chunks), st);
+    cudaError_t err = launch_attn_args(A, st);
     if (err == cudaErrorInvalidValue) throw Error(HG_ERR_INVALID, "unsupported head_dim / GQA group");
     HG_CUDA(err);
   })

@@ -19,10 +19,9 @@ void launch_route(const Dims& D, const DecodeBufs& B, const LayerDev& L, int lay
 void launch_ffn(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaStream_t st);
 void launch_moe_combine(const Dims& D, const DecodeBufs& B, float* y_out, cudaStream_t st);
 void launch_quant_rows(const float* x, int rows, int cols, int8_t* q, float* s, cudaStream_t st);
-int attn_grid(int T, int nkv, int max_chunks);
-cudaError_t launch_attn_args(const AttnArgs& A, int grid, cudaStream_t st);
+cudaError_t launch_attn_args(const AttnArgs& A, cudaStream_t st);
 cudaError_t prepare_attn(int hd, int rep);
-cudaError_t launch_attn_scores_only(const AttnArgs& A, int grid, cudaStream_t st);
+cudaError_t launch_attn_scores_only(const AttnArgs& A, cudaStream_t st);
 cudaError_t launch_attn_out_only(const AttnArgs& A, cudaStream_t st);
 void launch_feedback(const DecodeBufs& B, int32_t* tok, int32_t* pos, int32_t* gen, int gen_cap, int32_t* step,
                      cudaStream_t st);

@@ -9,7 +9,6 @@ namespace hg {
 
 constexpr int MAX_LAYERS = 64;
 constexpr int MAX_TOPK = 16;
-constexpr int ATT_CHUNK = 64;  // positions per attention work item (4 pages of 16)
 constexpr int PAGE = 16;       // positions per KV page
 
 // One packed Q8 matrix, or a stack of `count` equally shaped matrices.
@@ -76,8 +75,7 @@ struct DecodeBufs {
   long long s_stride;
   float* rinv;             // [T][nh] 1 / softmax denominator
   float* qn;               // [T][nh][hd] QK-normed, roped q
-  float* cmax;             // [T][nh][max_chunks][8] per-warp chunk maxima of the scores
-  int max_chunks;
+  uint32_t* mkey;          // [T][nh] running maximum of the attention scores (order-preserving key)
   float* logits;           // [T][vocab] or null
   unsigned long long* amax;// [T]
   int32_t* dbg_sel;        // [L][T][k] routing capture
@@ -86,7 +84,7 @@ struct DecodeBufs {
 
 // Arguments of the split-K decode attention kernel (decode.cu).
 struct AttnArgs {
-  int T, nh, nkv, hd, max_pos, bt_stride, max_chunks;
+  int T, nh, nkv, hd, max_pos, bt_stride;
   float eps;
   const float* qkv;  // [T][qkvd]
   int qkv_stride;
@@ -104,7 +102,7 @@ struct AttnArgs {
   long long s_stride;  // >= max_pos, multiple of 16
   float* rinv;     // [T][nh] 1 / softmax denominator
   float* qn;       // [T][nh][hd] QK-normed, roped q (k_qk_prep)
-  float* cmax;     // [T][nh][max_chunks][8] per-warp chunk maxima of the scores
+  uint32_t* mkey;  // [T][nh] maximum score per (token, head) as an order-preserving key (f2key)
   float* out;      // [T][nh*hd] or null
   int8_t* qo;      // [T][nh*hd] or null
   float* so;       // [T][ss(nh*hd/32)]
