@@ -768,27 +768,32 @@ struct UnitCursor {
 };
 
 constexpr int SC_SLOTS = 4;  // units in flight per scores CTA
+constexpr int SC_WARPS = 8;  // 8 warps x 4 positions: one 32-position unit per pass
 
 template <int HD, int REP>
 struct ScoresShape {
-  static constexpr int NT = 32 * REP;  // one thread per (position, q head) of a unit
-  static constexpr int PW = 32 / REP;  // positions per warp; lane = head * PW + position
-  static constexpr int CH = HD / 4;    // 16-byte chunks per K row
-  static constexpr int QS = HD + 4;    // padded q row (floats): the group's heads on distinct banks
-  static constexpr int SLOT = ATT_UNIT * HD + REP * QS;  // floats per ring slot
-  static constexpr size_t SMEM = (size_t)SC_SLOTS * SLOT * 4 + (SC_MAX_T + 1) * 4;
+  static constexpr int NT = 32 * SC_WARPS;
+  static constexpr int CH = HD / 4;  // 16-byte chunks per K row
+  static constexpr int E = HD / 32;  // ops::dot steps per accumulator lane
+  static constexpr int SLOT = ATT_UNIT * HD + REP * HD;  // K rows of the unit, then the group's q rows
+  static constexpr size_t SMEM = (size_t)SC_SLOTS * SLOT * 4;
 };
 
-// K chunk c (16 bytes) of unit row r is stored at chunk c ^ (r & 7): the PW rows a warp reads at
-// once then lie on distinct bank groups.
+// Thread mapping: a warp scores 4 positions of the unit (pp = lane / 8) for all REP q heads of the
+// group; lane l = lane % 8 is SIMD lane l of the four ops::dot accumulators (ops.rs:7-36), so it
+// holds elements 32e + 8m + l of q (registers, reloaded when the unit's (token, kv head) changes)
+// and reads the same elements of its position's K row. K chunk c (16 bytes) of unit row r is
+// stored at chunk c ^ ((r & 3) << 1): the four rows a warp reads at once then fall on distinct
+// banks, so each 32-bit K load is one shared-memory wavefront shared by all REP heads.
 template <int HD, int REP>
-__global__ void __launch_bounds__(32 * REP) k_attn_scores(AttnArgs A) {
+__global__ void __launch_bounds__(32 * SC_WARPS) k_attn_scores(AttnArgs A) {
   using S = ScoresShape<HD, REP>;
+  constexpr int E = S::E;
   extern __shared__ __align__(16) float sc_smem[];
   float* ring = sc_smem;
   int* prefix_s = reinterpret_cast<int*>(sc_smem + SC_SLOTS * S::SLOT);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int h = lane / S::PW, p = lane - h * S::PW, r = warp * S::PW + p;  // r: row within the unit
+  const int l = lane & 7, pp = lane >> 3, r = warp * 4 + pp;  // r: row within the unit
   attn_unit_prefix(A, prefix_s);  // positions are older than the previous kernel
   pdl_wait();  // qn and the appended K rows come from k_qk_prep
   pdl_trigger();
@@ -800,73 +805,89 @@ __global__ void __launch_bounds__(32 * REP) k_attn_scores(AttnArgs A) {
   UnitCursor ic, cc;  // issue / compute cursors
   ic.seek(A, prefix_s, u0);
   cc = ic;
+  // this thread's copies of a unit: chunk c0 of rows rc + RPP k (k < CPT), i.e. two pages
+  static_assert(S::NT % S::CH == 0 && ATT_UNIT % (S::NT / S::CH) == 0, "whole rows per pass");
+  constexpr int RPP = S::NT / S::CH, CPT = ATT_UNIT / RPP;  // rows per pass, copies per thread
+  const int c0 = tid % S::CH, rc = tid / S::CH;
   auto issue = [&](int i) {
     if (i < count) {
       float* slot = ring + (i % SC_SLOTS) * S::SLOT;
       const int pos = A.pos[ic.t], npg = pos / PAGE + 1, pg0 = ic.s * (ATT_UNIT / PAGE);
       const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[ic.t] : ic.t) * A.bt_stride;
-      const float* kb = A.k_pool + (long long)ic.kvh * PAGE * HD;
+      const float* kb = A.k_pool + (long long)ic.kvh * PAGE * HD + c0 * 4;
+      const float* page0 = kb + (long long)bt[pg0] * A.page_stride;
+      const float* page1 = pg0 + 1 < npg ? kb + (long long)bt[pg0 + 1] * A.page_stride : page0;
 #pragma unroll
-      for (int i2 = tid; i2 < ATT_UNIT * S::CH; i2 += S::NT) {
-        const int row = i2 / S::CH, c = i2 - row * S::CH, pg = pg0 + row / PAGE;
-        if (pg < npg)
-          cp_async16(slot + row * HD + ((c ^ (row & 7)) << 2),
-                     kb + (long long)bt[pg] * A.page_stride + (row % PAGE) * HD + c * 4);
+      for (int k = 0; k < CPT; k++) {
+        const int row = rc + RPP * k;
+        if (row < PAGE || pg0 + 1 < npg)
+          cp_async16(slot + row * HD + ((c0 ^ ((row & 3) << 1)) << 2), (row < PAGE ? page0 : page1) + (row % PAGE) * HD);
       }
       const float* q = A.qn + ((size_t)ic.t * A.nh + ic.kvh * REP) * HD;
-      for (int i2 = tid; i2 < REP * S::CH; i2 += S::NT) {
-        const int hh = i2 / S::CH, c = i2 - hh * S::CH;
-        cp_async16(slot + ATT_UNIT * HD + hh * S::QS + c * 4, q + hh * HD + c * 4);
-      }
+      for (int i2 = tid; i2 < REP * S::CH; i2 += S::NT) cp_async16(slot + ATT_UNIT * HD + i2 * 4, q + i2 * 4);
       ic.next(A, prefix_s);
     }
     cp_async_commit();
   };
 #pragma unroll
   for (int k = 0; k < SC_SLOTS - 1; k++) issue(k);
-  float mx = -INFINITY;  // running maximum of this thread's head over the current (token, kv head)
+  // element 32e + 8m + l of unit row r lies in chunk 8e + 2m + l/4, stored at chunk
+  // 8e + 2 (m ^ (r % 4)) + l/4: koff[m] + 32 e floats from the slot
+  int koff[4];
+#pragma unroll
+  for (int m = 0; m < 4; m++) koff[m] = r * HD + ((2 * (m ^ (r & 3)) + (l >> 2)) << 2) + (l & 3);
+  float qv[REP][E][4];
+  float mx[REP];
+#pragma unroll
+  for (int h = 0; h < REP; h++) mx[h] = -INFINITY;  // running maxima over the current (token, kv head)
   for (int i = 0; i < count; i++) {
     cp_async_wait<SC_SLOTS - 2>();
     __syncthreads();  // unit i has landed for every thread; every thread is done with unit i - 1
     issue(i + SC_SLOTS - 1);
     const float* slot = ring + (i % SC_SLOTS) * S::SLOT;
-    const float* kr = slot + r * HD;
-    const float* qh = slot + ATT_UNIT * HD + h * S::QS;
-    // ops::dot (ops.rs:7-36): accumulator m's SIMD lane l sums elements 32i + 8m + l with FMA in
-    // order of i; chunk c holds elements 4c..4c+3, i.e. m = (c % 8) / 2, l = 4 (c % 2) + 0..3
-    float acc[4][8];
+    if (i == 0 || cc.s == 0) {  // a new (token, kv head): its q rows came with this unit
+      const float* qs = slot + ATT_UNIT * HD;
 #pragma unroll
-    for (int m = 0; m < 4; m++)
+      for (int h = 0; h < REP; h++)
 #pragma unroll
-      for (int l = 0; l < 8; l++) acc[m][l] = 0.0f;
+        for (int e = 0; e < E; e++)
 #pragma unroll
-    for (int c = 0; c < S::CH; c++) {
-      const float4 k4 = *reinterpret_cast<const float4*>(kr + ((c ^ (r & 7)) << 2));
-      const float4 q4 = *reinterpret_cast<const float4*>(qh + (c << 2));
-      const int m = (c & 7) >> 1, l0 = (c & 1) * 4;
-      acc[m][l0 + 0] = __fmaf_rn(q4.x, k4.x, acc[m][l0 + 0]);
-      acc[m][l0 + 1] = __fmaf_rn(q4.y, k4.y, acc[m][l0 + 1]);
-      acc[m][l0 + 2] = __fmaf_rn(q4.z, k4.z, acc[m][l0 + 2]);
-      acc[m][l0 + 3] = __fmaf_rn(q4.w, k4.w, acc[m][l0 + 3]);
+          for (int m = 0; m < 4; m++) qv[h][e][m] = qs[h * HD + 32 * e + 8 * m + l];
     }
-    float sl[8];
+    float kv[E][4];
 #pragma unroll
-    for (int l = 0; l < 8; l++) sl[l] = fadd(fadd(acc[0][l], acc[1][l]), fadd(acc[2][l], acc[3][l]));
-    const float tot = fadd(fadd(fadd(sl[0], sl[4]), fadd(sl[2], sl[6])), fadd(fadd(sl[1], sl[5]), fadd(sl[3], sl[7])));
-    const float sc = fmul(tot, scale);
+    for (int m = 0; m < 4; m++) {
+      const float* kr = slot + koff[m];
+#pragma unroll
+      for (int e = 0; e < E; e++) kv[e][m] = kr[32 * e];
+    }
     const int n = A.pos[cc.t] + 1, j = cc.s * ATT_UNIT + r;
-    const int hq = cc.kvh * REP + h;
-    if (j < n) {
-      A.S[((size_t)cc.t * A.nh + hq) * A.s_stride + j] = sc;
-      mx = fmaxf(mx, sc);
+    float* srow = A.S + ((size_t)cc.t * A.nh + cc.kvh * REP) * A.s_stride + j;
+#pragma unroll
+    for (int h = 0; h < REP; h++) {
+      float a[4];
+#pragma unroll
+      for (int m = 0; m < 4; m++) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int e = 0; e < E; e++) acc = __fmaf_rn(qv[h][e][m], kv[e][m], acc);
+        a[m] = acc;
+      }
+      const float sc = fmul(hsum8_group(fadd(fadd(a[0], a[1]), fadd(a[2], a[3]))), scale);
+      if (j < n) {
+        if (l == 0) srow[(size_t)h * A.s_stride] = sc;
+        mx[h] = fmaxf(mx[h], sc);
+      }
     }
     // the (token, kv head) run ends at the CTA's last unit or at its last unit in the head
-    const bool flush = i + 1 == count || cc.s + 1 == cc.nu;
-    if (flush) {
+    if (i + 1 == count || cc.s + 1 == cc.nu) {
 #pragma unroll
-      for (int o = 1; o < S::PW; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      if (p == 0 && mx > -INFINITY) atomicMax(A.mkey + (size_t)cc.t * A.nh + hq, f2key(mx));
-      mx = -INFINITY;
+      for (int h = 0; h < REP; h++) {
+        float v = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 8));
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
+        if (lane == 0 && v > -INFINITY) atomicMax(A.mkey + (size_t)cc.t * A.nh + cc.kvh * REP + h, f2key(v));
+        mx[h] = -INFINITY;
+      }
     }
     cc.next(A, prefix_s);
   }
@@ -985,8 +1006,8 @@ __global__ void __launch_bounds__(SMX_THREADS) k_attn_softmax(AttnArgs A) {
 // head, lane = dim: one chain per thread, so a warp spends ~3 instructions per position and the
 // chain's add latency sets the pace.
 // ------------------------------------------------------------------------------------------
-constexpr int PV_STAGE = 32;        // positions per stage (large kernel)
-constexpr int PV_SLOTS = 5;         // ring slots (large kernel): 3 stages in flight ahead of the chain
+constexpr int PV_STAGE = 16;        // positions per stage (large kernel): one page
+constexpr int PV_SLOTS = 4;         // ring slots (large kernel): 2 stages in flight ahead of the chain
 constexpr int PVS_STAGE = 64;       // positions per stage (small kernel)
 constexpr int PVS_SLOTS = 6;        // ring slots (small kernel)
 constexpr int PV_SMALL_MAX_PAIRS = 48;  // (token, kv head) pairs up to which k_attn_pv_small runs
@@ -1350,7 +1371,7 @@ static int g_attn_sms[64];
 
 template <int HD, int REP>
 static size_t scores_smem(int T) {
-  return (size_t)SC_SLOTS * ScoresShape<HD, REP>::SLOT * 4 + (((size_t)T + 1) * 4 + 15) / 16 * 16;
+  return ScoresShape<HD, REP>::SMEM + (((size_t)T + 1) * 4 + 15) / 16 * 16;
 }
 
 // Units are dealt to the scores CTAs in contiguous runs, so the grid only needs to fill the GPU:
@@ -1360,7 +1381,7 @@ static int scores_grid(const AttnArgs& A, size_t smem) {
   int dev = 0, per_sm = 1;
   cudaGetDevice(&dev);
   const int sms = (dev >= 0 && dev < 64 && g_attn_sms[dev] > 0) ? g_attn_sms[dev] : 148;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_attn_scores<HD, REP>, 32 * REP, smem);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_attn_scores<HD, REP>, 32 * SC_WARPS, smem);
   const long long units = (long long)A.T * A.nkv * ((A.max_pos + ATT_UNIT - 1) / ATT_UNIT);
   const long long g = std::min<long long>(units, (long long)sms * std::max(per_sm, 1));
   return (int)std::max<long long>(g, 1);
@@ -1373,7 +1394,7 @@ static cudaError_t launch_attn_t(const AttnArgs& A, cudaStream_t st, int which) 
     const int nw = A.nh + A.nkv;
     launch_pdl(pdl, k_qk_prep<HD>, dim3(A.T), dim3(32 * nw), (size_t)nw * HD * 4, st, A);
     const size_t sm = scores_smem<HD, REP>(A.T);
-    launch_pdl(pdl, k_attn_scores<HD, REP>, dim3(scores_grid<HD, REP>(A, sm)), dim3(32 * REP), sm, st, A);
+    launch_pdl(pdl, k_attn_scores<HD, REP>, dim3(scores_grid<HD, REP>(A, sm)), dim3(32 * SC_WARPS), sm, st, A);
   }
   if (which & 2) {
     launch_pdl(pdl, k_attn_softmax, dim3(A.T * A.nh), dim3(SMX_THREADS), 0, st, A);
