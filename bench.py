@@ -46,6 +46,12 @@ def parse():
     ap.add_argument("--diffusion", action="store_true",
                     help="measure diffusion decode (Engine::generate_diffusion) instead of the headline (one GPU)")
     ap.add_argument("--seqs", type=int, default=N_SEQS, help=argparse.SUPPRESS)
+    # profiling aid: shorter prompts (same batch) make the untimed prefill quick when only the
+    # context-independent kernels are of interest; the headline always uses U[1024, 8192]
+    ap.add_argument("--prompt-range", type=int, nargs=2, default=(1024, 8192), help=argparse.SUPPRESS)
+    ap.add_argument("--ep", action="store_true",
+                    help="expert parallelism under torchrun: the routed experts split across the ranks, "
+                         "(token, expert) rows exchanged with NCCL inside each step (config 5's variant)")
     ap.add_argument("--attn-case", action="store_true",
                     help="time the decode-attention op alone on a config-3-shaped case (one GPU); "
                          "--seqs/--lo/--hi/--pages/--layers shape it")
@@ -56,12 +62,13 @@ def parse():
     return ap.parse_args()
 
 
-def workload(n_seqs: int = N_SEQS, seed: int = 5):
-    """Prompt lengths ~ U[1024, 8192] and ids ~ U[0, 50257) from torch.Generator(seed)."""
+def workload(n_seqs: int = N_SEQS, seed: int = 5, lo: int = 1024, hi: int = 8192):
+    """Prompt lengths ~ U[lo, hi] (config 5: U[1024, 8192]) and ids ~ U[0, 50257) from
+    torch.Generator(seed)."""
     import torch
 
     g = torch.Generator().manual_seed(seed)
-    lens = torch.randint(1024, 8193, (n_seqs,), generator=g).tolist()
+    lens = torch.randint(lo, hi + 1, (n_seqs,), generator=g).tolist()
     prompts = [torch.randint(0, VALID, (n,), generator=g).numpy().astype("uint32") for n in lens]
     return prompts
 
@@ -218,7 +225,7 @@ def run_ours(args):
     rank, world, local = dist_setup(args)
     torch.cuda.set_device(local)
     path = model_path(rank, world)
-    prompts_all = workload(args.seqs)
+    prompts_all = workload(args.seqs, lo=args.prompt_range[0], hi=args.prompt_range[1])
     mine = shard([len(p) for p in prompts_all], rank, world)
     prompts = [prompts_all[i] for i in mine]
     n_local = len(prompts)
@@ -235,6 +242,10 @@ def run_ours(args):
         caches.append(c)
         toks.append(int(np.argmax(lg)))
     prefill_s = time.time() - t0
+    if args.ep and world > 1:  # before the first decode step: the step graphs hold the exchanges
+        from hobbylm_b200 import ep
+
+        ep.setup(eng)
     stream = torch.cuda.ExternalStream(eng.stream(), device=local)
     # warm-up (captures the step graph)
     if args.warmup:
@@ -288,8 +299,11 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": round(max_s / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8 dot / f32",
         "data": "synthetic (random-init seed-0 weights, random prompt ids)",
-        "config": {"workload": "config5: 500M Q8_0, 256 seqs, prompts U[1024,8192] seed 5, greedy decode",
-                   "global_batch": args.seqs, "seqs_per_gpu": n_local, "parallelism": f"seq-shard x{world}",
+        "config": {"workload": f"config5: 500M Q8_0, {args.seqs} seqs, prompts U[{args.prompt_range[0]},"
+                               f"{args.prompt_range[1]}] seed 5, greedy decode",
+                   "global_batch": args.seqs, "seqs_per_gpu": n_local,
+                   "parallelism": (f"seq-shard x{world} + experts split over {world} ranks (NCCL send/recv)"
+                                   if args.ep and world > 1 else f"seq-shard x{world}"),
                    "context_at_start": {"min": int(reduce_min(min(ctx_start) if ctx_start else 0, world)),
                                         "mean": reduce_sum(sum(ctx_start), world) / max(total_tokens / args.steps, 1)},
                    "l2": "inputs larger than L2 (KV cache ~60 GB)", "prefill_s_rank0": round(prefill_s, 1)},

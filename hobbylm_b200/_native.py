@@ -27,6 +27,7 @@ EXPORTS = (
     "hg_op_moe_scratch_bytes", "hg_op_moe_ffn", "hg_op_kv_attn_scratch_bytes", "hg_op_kv_attn", "hg_rope_tables",
     "hg_decode_greedy", "hg_engine_stream", "hg_decode_kernel_count", "hg_debug_time_attention",
     "hg_op_q8_matvec_noalloc", "hg_host_sample", "hg_host_score_block", "hg_generate_embeds",
+    "hg_ep_unique_id", "hg_engine_ep_init",
 )
 NOALLOC_SCRATCH_BYTES = 4 << 20  # HG_NOALLOC_SCRATCH_BYTES
 
@@ -134,6 +135,8 @@ def lib():
         "hg_rope_tables": (i32, [i32, i32, f32, vp, vp]),
         "hg_decode_greedy": (i32, [vp, vp, i32, vp, i32, vp]),
         "hg_engine_stream": (vp, [vp]),
+        "hg_ep_unique_id": (i32, [vp]),
+        "hg_engine_ep_init": (i32, [vp, vp, i32, i32]),
         "hg_decode_kernel_count": (i32, [vp, i32]),
         "hg_debug_time_attention": (i32, [vp, vp, i32, i32, C.POINTER(f32), C.POINTER(f32)]),
     }

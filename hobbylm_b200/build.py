@@ -19,8 +19,8 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libhobbygpu.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["engine.cu", "decode.cu", "prefill.cu", "noalloc.cu", "gguf.cpp", "sampler.cpp"]
-HEADERS = ["hg_device.cuh", "hg_model.cuh", "hg_launch.h", "hg_host.h"]
+SOURCES = ["engine.cu", "decode.cu", "tc.cu", "ep.cu", "prefill.cu", "noalloc.cu", "gguf.cpp", "sampler.cpp"]
+HEADERS = ["hg_device.cuh", "hg_model.cuh", "hg_launch.h", "hg_host.h", "hg_ep.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # --fmad=false: no implicit FMA contraction; kernels write every fused multiply-add explicitly so the
@@ -71,7 +71,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
         list(ex.map(run, jobs))
     if force or jobs or _stale(LIB, objs):
         tmp = LIB + f".tmp{os.getpid()}"
-        run([nvcc(), *ARCH, "-shared", "-Xcompiler", "-fopenmp", *objs, "-o", tmp, "-lgomp", "-lcudart"])
+        run([nvcc(), *ARCH, "-shared", "-Xcompiler", "-fopenmp", *objs, "-o", tmp, "-lgomp", "-lcudart", "-ldl"])
         os.replace(tmp, LIB)
     return LIB
 

@@ -17,7 +17,7 @@
 #include <cfloat>
 #include <utility>
 
-#include "hg_model.cuh"
+#include "hg_launch.h"
 
 namespace hg {
 
@@ -105,6 +105,15 @@ __global__ void __launch_bounds__(PRE_NORM_THREADS) k_pre_norm(Dims D, DecodeBuf
   __shared__ float red[32];
   const int t = blockIdx.x, d = D.d;
   float* x = B.x + (size_t)t * d;
+  // loads of data older than the previous kernel, issued before the wait: the norm gain, the
+  // residual row (written by the output projection, three kernels back) and the MoE gate weights
+  // (written by the router, two kernels back)
+  const bool first = threadIdx.x < d;
+  const float nw0 = first ? norm_w[threadIdx.x] : 0.0f;
+  const float x0 = (mode != 0 && first) ? x[threadIdx.x] : 0.0f;
+  float sc[MAX_TOPK];
+#pragma unroll
+  for (int r = 0; r < MAX_TOPK; r++) sc[r] = (mode == 2 && r < D.k) ? fmul(B.selw[t * D.k + r], D.wscale) : 0.0f;
   pdl_wait();
   pdl_trigger();
   if (mode == 0) {
@@ -122,17 +131,14 @@ __global__ void __launch_bounds__(PRE_NORM_THREADS) k_pre_norm(Dims D, DecodeBuf
     for (int i = threadIdx.x; i < d; i += blockDim.x) xs[i] = e[i];
   } else if (mode == 1) {
     const float* y = B.y + (size_t)t * (D.k + 1) * d;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) xs[i] = fadd(x[i], y[i]);
+    for (int i = threadIdx.x; i < d; i += blockDim.x) xs[i] = fadd(i == threadIdx.x ? x0 : x[i], y[i]);
   } else if (mode == 2) {
     const float* y = B.y + (size_t)t * (D.k + 1) * d;
-    float sc[MAX_TOPK];
-#pragma unroll
-    for (int r = 0; r < MAX_TOPK; r++) sc[r] = r < D.k ? fmul(B.selw[t * D.k + r], D.wscale) : 0.0f;
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
       float yv[MAX_TOPK + 1];  // every row's element loaded before the rank-order sum
 #pragma unroll
       for (int r = 0; r <= MAX_TOPK; r++) yv[r] = (r < D.k || (r == D.k && D.nsh > 0)) ? y[r * d + i] : 0.0f;
-      const float xi = x[i];
+      const float xi = i == threadIdx.x ? x0 : x[i];
       float o = 0.0f;
 #pragma unroll
       for (int r = 0; r < MAX_TOPK; r++)
@@ -145,14 +151,14 @@ __global__ void __launch_bounds__(PRE_NORM_THREADS) k_pre_norm(Dims D, DecodeBuf
       xs[i] = fadd(xi, o);
     }
   } else {
-    for (int i = threadIdx.x; i < d; i += blockDim.x) xs[i] = x[i];
+    for (int i = threadIdx.x; i < d; i += blockDim.x) xs[i] = i == threadIdx.x ? x0 : x[i];
   }
   if (mode != 3)
     for (int i = threadIdx.x; i < d; i += blockDim.x) x[i] = xs[i];
   float ss = seq_sumsq_block(xs, d, red);
   float scale = __fdiv_rn(1.0f, __fsqrt_rn(fadd(__fdiv_rn(ss, (float)d), D.eps)));
   for (int i = threadIdx.x; i < d; i += blockDim.x) {
-    float h = fmul(fmul(xs[i], scale), norm_w[i]);
+    float h = fmul(fmul(xs[i], scale), i == threadIdx.x ? nw0 : norm_w[i]);
     xs[i] = h;
     if (h_out) h_out[(size_t)t * d + i] = h;
   }
@@ -332,6 +338,10 @@ __global__ void __launch_bounds__(ROUTE_THREADS) k_route(Dims D, DecodeBufs B, L
       for (int i = 0; i < NI; i++) wr[rr][i] = e < D.ne ? Ld.router[(size_t)e * d + 32 * i + rlane] : 0.0f;
     }
   }
+  // weights, before the wait; the gain only when this kernel normalizes (prenormed callers, such
+  // as the op-level MoE entry, pass no gain)
+  const float nw0 = (!prenormed && threadIdx.x < d) ? Ld.ffn_norm[threadIdx.x] : 0.0f;
+  const float bias0 = (Ld.moe && threadIdx.x < D.ne) ? Ld.bias[threadIdx.x] : 0.0f;
   pdl_wait();
   pdl_trigger();
   if (prenormed) {
@@ -342,7 +352,7 @@ __global__ void __launch_bounds__(ROUTE_THREADS) k_route(Dims D, DecodeBufs B, L
     float ss = seq_sumsq_block(hs, d, red);
     float scale = __fdiv_rn(1.0f, __fsqrt_rn(fadd(__fdiv_rn(ss, (float)d), D.eps)));
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
-      float h = fmul(fmul(hs[i], scale), Ld.ffn_norm[i]);
+      float h = fmul(fmul(hs[i], scale), i == threadIdx.x ? nw0 : Ld.ffn_norm[i]);
       hs[i] = h;
       B.h2[(size_t)t * d + i] = h;
     }
@@ -384,7 +394,7 @@ __global__ void __launch_bounds__(ROUTE_THREADS) k_route(Dims D, DecodeBufs B, L
   for (int e = threadIdx.x; e < ne; e += blockDim.x) {
     float sc = D.gsig ? sigmoid_ref(logit_s[e]) : score_s[e];
     score_s[e] = sc;
-    selsc_s[e] = fadd(sc, Ld.bias[e]);
+    selsc_s[e] = fadd(sc, e == (int)threadIdx.x ? bias0 : Ld.bias[e]);
   }
   __syncthreads();
   for (int e = threadIdx.x; e < ne; e += blockDim.x) {
@@ -622,25 +632,25 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // per-head RMSNorm with a sequential sum (model.rs:753-763) + rotate-half RoPE (ops.rs:157-166)
-// of one head vector by one warp. buf: this warp's HD-float shared scratch; dst may alias buf.
+// of one head vector by one warp. wv: this lane's gains (elements lane + 32 j); cv / sv: its cos /
+// sin entries (lane + 32 j < HD / 2); buf: this warp's HD-float shared scratch (16-byte aligned),
+// which receives the result.
 template <int HD>
-__device__ __forceinline__ void norm_rope_warp(const float* src, const float* w, float eps, const float* cs,
-                                               const float* sn, float* buf) {
+__device__ __forceinline__ void norm_rope_warp(const float* src, const float (&wv)[HD / 32], float eps,
+                                               const float (&cv)[HD / 64], const float (&sv)[HD / 64], float* buf) {
   constexpr int HALF = HD / 2;
   const int lane = threadIdx.x & 31;
   for (int i = lane; i < HD; i += 32) buf[i] = src[i];
   __syncwarp();
   float scale = 0.0f;
   if (lane == 0) {
-    float ss = 0.0f;
-#pragma unroll 8
-    for (int i = 0; i < HD; i++) ss = fadd(ss, fmul(buf[i], buf[i]));
+    const float ss = seq_sumsq_smem(buf, HD);
     scale = __fdiv_rn(1.0f, __fsqrt_rn(fadd(__fdiv_rn(ss, (float)HD), eps)));
   }
   scale = __shfl_sync(0xffffffffu, scale, 0);
   float v[HD / 32];
 #pragma unroll
-  for (int j = 0; j < HD / 32; j++) v[j] = fmul(fmul(buf[lane + 32 * j], scale), w[lane + 32 * j]);
+  for (int j = 0; j < HD / 32; j++) v[j] = fmul(fmul(buf[lane + 32 * j], scale), wv[j]);
   __syncwarp();
 #pragma unroll
   for (int j = 0; j < HD / 32; j++) buf[lane + 32 * j] = v[j];
@@ -648,9 +658,9 @@ __device__ __forceinline__ void norm_rope_warp(const float* src, const float* w,
 #pragma unroll
   for (int j = 0; j < HD / 64; j++) {
     const int i = lane + 32 * j;  // i < HALF
-    const float x1 = buf[i], x2 = buf[i + HALF], c = cs[i], sv = sn[i];
-    v[j] = __fsub_rn(fmul(x1, c), fmul(x2, sv));
-    v[j + HD / 64] = fadd(fmul(x2, c), fmul(x1, sv));
+    const float x1 = buf[i], x2 = buf[i + HALF], c = cv[j], sn = sv[j];
+    v[j] = __fsub_rn(fmul(x1, c), fmul(x2, sn));
+    v[j + HD / 64] = fadd(fmul(x2, c), fmul(x1, sn));
   }
   __syncwarp();
 #pragma unroll
@@ -675,28 +685,45 @@ template <int HD>
 __global__ void k_qk_prep(AttnArgs A) {
   extern __shared__ __align__(16) float prep_s[];  // one HD-float scratch per warp
   const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  pdl_wait();
-  pdl_trigger();
+  // everything but the qkv row is older than the previous kernel: the maxima (last read two
+  // kernels ago), the position, the gains, the RoPE rows and the page slot are handled before the
+  // wait
   for (int h = threadIdx.x; h < A.nh; h += blockDim.x) A.mkey[(size_t)t * A.nh + h] = 0u;
   const int pos = A.pos[t];
-  if (!attn_pos_ok(A, pos)) {
+  const bool ok = attn_pos_ok(A, pos);
+  const bool is_q = warp < A.nh, is_k = !is_q && warp < A.nh + A.nkv;
+  float wv[HD / 32], cv[HD / 64], sv[HD / 64];
+  long long off = 0;
+  if (ok && (is_q || is_k)) {
+    const float* w = is_q ? A.q_norm : A.k_norm;
+#pragma unroll
+    for (int j = 0; j < HD / 32; j++) wv[j] = w[lane + 32 * j];
+#pragma unroll
+    for (int j = 0; j < HD / 64; j++) {
+      cv[j] = A.rope_cos[(size_t)pos * (HD / 2) + lane + 32 * j];
+      sv[j] = A.rope_sin[(size_t)pos * (HD / 2) + lane + 32 * j];
+    }
+    if (is_k) {
+      const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
+      off = (long long)bt[pos / PAGE] * A.page_stride + ((long long)(warp - A.nh) * PAGE + pos % PAGE) * HD;
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (!ok) {
     if (threadIdx.x == 0 && A.err) atomicExch(A.err, HG_ERR_CONTEXT);
     return;
   }
   const float* qkv = A.qkv + (size_t)t * A.qkv_stride;
   const int qd = A.nh * HD, kvd = A.nkv * HD;
-  const float* cs = A.rope_cos + (size_t)pos * (HD / 2);
-  const float* sn = A.rope_sin + (size_t)pos * (HD / 2);
   float* buf = prep_s + warp * HD;
-  if (warp < A.nh) {
-    norm_rope_warp<HD>(qkv + warp * HD, A.q_norm, A.eps, cs, sn, buf);
+  if (is_q) {
+    norm_rope_warp<HD>(qkv + warp * HD, wv, A.eps, cv, sv, buf);
     float* dst = A.qn + ((size_t)t * A.nh + warp) * HD;
     for (int j = lane; j < HD; j += 32) dst[j] = buf[j];
-  } else if (warp < A.nh + A.nkv) {
+  } else if (is_k) {
     const int kvh = warp - A.nh;
-    const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
-    const long long off = (long long)bt[pos / PAGE] * A.page_stride + ((long long)kvh * PAGE + pos % PAGE) * HD;
-    norm_rope_warp<HD>(qkv + qd + kvh * HD, A.k_norm, A.eps, cs, sn, buf);
+    norm_rope_warp<HD>(qkv + qd + kvh * HD, wv, A.eps, cv, sv, buf);
     for (int j = lane; j < HD; j += 32) {
       A.k_pool[off + j] = buf[j];
       A.v_pool[off + j] = qkv[qd + kvd + kvh * HD + j];
@@ -709,6 +736,7 @@ __global__ void k_qk_prep(AttnArgs A) {
 // prefix_s[T] = total. Computed by warp 0 (T <= SC_MAX_T).
 constexpr int ATT_UNIT = 32;
 constexpr int SC_MAX_T = 1024;
+constexpr int ATT_MAX_BT = 4096;  // block-table entries per sequence (contexts up to 65,536 positions)
 
 __device__ __forceinline__ int attn_units_of(const AttnArgs& A, int t) {
   const int p = A.pos[t];
@@ -809,14 +837,26 @@ __global__ void __launch_bounds__(32 * SC_WARPS) k_attn_scores(AttnArgs A) {
   static_assert(S::NT % S::CH == 0 && ATT_UNIT % (S::NT / S::CH) == 0, "whole rows per pass");
   constexpr int RPP = S::NT / S::CH, CPT = ATT_UNIT / RPP;  // rows per pass, copies per thread
   const int c0 = tid % S::CH, rc = tid / S::CH;
+  // the issue cursor's unit: its token's position and the unit's two page ids, fetched when the
+  // cursor arrives there (one unit before they are used), so the copies never wait on the loads
+  int f_pos = 0, f_p0 = 0, f_p1 = 0;
+  auto fetch = [&]() {
+    if (ic.t < A.T) {
+      const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[ic.t] : ic.t) * A.bt_stride;
+      const int pg0 = ic.s * (ATT_UNIT / PAGE);
+      f_pos = A.pos[ic.t];
+      f_p0 = bt[pg0];
+      f_p1 = pg0 + 1 < A.bt_stride ? bt[pg0 + 1] : f_p0;  // in the table; used only inside the sequence
+    }
+  };
+  fetch();
   auto issue = [&](int i) {
     if (i < count) {
       float* slot = ring + (i % SC_SLOTS) * S::SLOT;
-      const int pos = A.pos[ic.t], npg = pos / PAGE + 1, pg0 = ic.s * (ATT_UNIT / PAGE);
-      const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[ic.t] : ic.t) * A.bt_stride;
+      const int npg = f_pos / PAGE + 1, pg0 = ic.s * (ATT_UNIT / PAGE);
       const float* kb = A.k_pool + (long long)ic.kvh * PAGE * HD + c0 * 4;
-      const float* page0 = kb + (long long)bt[pg0] * A.page_stride;
-      const float* page1 = pg0 + 1 < npg ? kb + (long long)bt[pg0 + 1] * A.page_stride : page0;
+      const float* page0 = kb + (long long)f_p0 * A.page_stride;
+      const float* page1 = pg0 + 1 < npg ? kb + (long long)f_p1 * A.page_stride : page0;
 #pragma unroll
       for (int k = 0; k < CPT; k++) {
         const int row = rc + RPP * k;
@@ -826,6 +866,7 @@ __global__ void __launch_bounds__(32 * SC_WARPS) k_attn_scores(AttnArgs A) {
       const float* q = A.qn + ((size_t)ic.t * A.nh + ic.kvh * REP) * HD;
       for (int i2 = tid; i2 < REP * S::CH; i2 += S::NT) cp_async16(slot + ATT_UNIT * HD + i2 * 4, q + i2 * 4);
       ic.next(A, prefix_s);
+      fetch();
     }
     cp_async_commit();
   };
@@ -1048,10 +1089,13 @@ __global__ void __launch_bounds__(HD) k_attn_pv(AttnArgs A) {
   }
   const int n = pos + 1, nst = (n + PV_STAGE - 1) / PV_STAGE, npg = pos / PAGE + 1;
   const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
+  int* bt_s = reinterpret_cast<int*>(pv_smem + PV_SLOTS * S::SLOT);  // the sequence's page ids
+  for (int i = tid; i < npg; i += S::NT) bt_s[i] = bt[i];
+  __syncthreads();
   const float* vb = A.v_pool + (long long)kvh * PAGE * HD;
   const float* e0 = A.S + ((size_t)t * A.nh + h0) * A.s_stride;
-  // V rows (older than the previous kernel) may be fetched before the wait; the e rows may not, so
-  // the ring is filled after it
+  // page ids and V rows are older than the previous kernel; the e rows are not, so the ring is
+  // filled after the wait
   pdl_wait();
   pdl_trigger();
   // 1/sum of the head of each (position, head) pair this thread forms p for in make_p
@@ -1068,7 +1112,7 @@ __global__ void __launch_bounds__(HD) k_attn_pv(AttnArgs A) {
 #pragma unroll
       for (int i = tid; i < PV_STAGE * HD / 4; i += S::NT) {
         const int row = i / (HD / 4), c = i - row * (HD / 4), pg = st * (PV_STAGE / PAGE) + row / PAGE;
-        if (pg < npg) cp_async16(slot + row * HD + c * 4, vb + (long long)bt[pg] * A.page_stride + (row % PAGE) * HD + c * 4);
+        if (pg < npg) cp_async16(slot + row * HD + c * 4, vb + (long long)bt_s[pg] * A.page_stride + (row % PAGE) * HD + c * 4);
       }
       if (tid < REP * PV_STAGE / 4) {  // e rows run to s_stride >= npg * PAGE
         const int r = tid / (PV_STAGE / 4), q = tid - r * (PV_STAGE / 4);
@@ -1151,6 +1195,9 @@ __global__ void __launch_bounds__(32 * REP) k_attn_pv_small(AttnArgs A) {
   }
   const int n = pos + 1, nst = (n + PVS_STAGE - 1) / PVS_STAGE, npg = pos / PAGE + 1;
   const int* bt = A.bt + (size_t)(A.bt_row ? A.bt_row[t] : t) * A.bt_stride;
+  int* bt_s = reinterpret_cast<int*>(pv_smem + PVS_SLOTS * S::SLOT);  // the sequence's page ids
+  for (int i = tid; i < npg; i += S::NT) bt_s[i] = bt[i];
+  __syncthreads();
   const float* vb = A.v_pool + (long long)kvh * PAGE * HD + slice * 32;
   const float* e0 = A.S + ((size_t)t * A.nh + kvh * REP) * A.s_stride;
   pdl_wait();
@@ -1162,7 +1209,7 @@ __global__ void __launch_bounds__(32 * REP) k_attn_pv_small(AttnArgs A) {
 #pragma unroll
       for (int i = tid; i < PVS_STAGE * 8; i += S::NT) {  // 8 chunks per 32-float row slice
         const int row = i >> 3, c = i & 7, pg = st * (PVS_STAGE / PAGE) + row / PAGE;
-        if (pg < npg) cp_async16(slot + row * 32 + c * 4, vb + (long long)bt[pg] * A.page_stride + (row % PAGE) * HD + c * 4);
+        if (pg < npg) cp_async16(slot + row * 32 + c * 4, vb + (long long)bt_s[pg] * A.page_stride + (row % PAGE) * HD + c * 4);
       }
       for (int i = tid; i < REP * PVS_STAGE / 4; i += S::NT) {
         const int r = i / (PVS_STAGE / 4), q = i - r * (PVS_STAGE / 4);
@@ -1275,6 +1322,10 @@ template <int EPI>
 static void launch_mv_tokens_t(const Dims& D, const DecodeBufs& B, const Q8M& W, const int8_t* aq, const float* as,
                                float* out, int ostride, cudaStream_t st) {
   int nb = W.cols >> 5;
+  if (tc_usable(W, B.T)) {  // many tokens: the partials come from the tensor cores (tc.cu)
+    launch_mv_tc(D, B, W, aq, as, out, ostride, EPI, st);
+    return;
+  }
   if (B.T == 1) {
     constexpr int ROWS = 8, TT = 1;
     dim3 grid((W.rows + ROWS - 1) / ROWS);
@@ -1335,12 +1386,17 @@ void launch_moe_combine(const Dims& D, const DecodeBufs& B, float* y_out, cudaSt
 }
 
 void launch_ffn(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaStream_t st) {
+  const int nrouted = L.moe ? (D.ne < B.T * D.k ? D.ne : B.T * D.k) : 0;
+  launch_ffn_ex(D, B, L, true, nrouted, st);
+}
+
+void launch_ffn_ex(const Dims& D, const DecodeBufs& B, const LayerDev& L, bool group0, int nrouted, cudaStream_t st) {
   // group 0 (shared expert / dense FFN: T entries) over sh y-slices of one ez-entry chunk each; the
   // routed groups (at most T entries each, usually far fewer) after them, their chunks strided
   // over nz z-CTAs, so few routed CTAs find no work
-  const int ez = B.T == 1 ? 1 : FFN_EZ, sh = (B.T + ez - 1) / ez;
-  const int nrouted = L.moe ? (D.ne < B.T * D.k ? D.ne : B.T * D.k) : 0;
-  const int groups = sh + nrouted, nz = nrouted > 0 ? std::min(sh, FFN_ZMAX) : 1;
+  const int ez = B.T == 1 ? 1 : FFN_EZ, chunks = (B.T + ez - 1) / ez, sh = group0 ? chunks : 0;
+  const int groups = sh + nrouted, nz = nrouted > 0 ? std::min(chunks, FFN_ZMAX) : 1;
+  if (groups == 0) return;
   static_assert(FFN_EZ % 8 == 0, "whole TT-entry steps per chunk");
   const int fdim = L.moe ? D.f : D.df;
   const int nb_up = D.d >> 5;
@@ -1400,16 +1456,18 @@ static cudaError_t launch_attn_t(const AttnArgs& A, cudaStream_t st, int which) 
     launch_pdl(pdl, k_attn_softmax, dim3(A.T * A.nh), dim3(SMX_THREADS), 0, st, A);
     if (A.T * A.nkv <= PV_SMALL_MAX_PAIRS)
       launch_pdl(pdl, k_attn_pv_small<HD, REP>, dim3(A.T * A.nkv * (HD / 32)), dim3(32 * REP),
-                 PvSmallShape<REP>::SMEM, st, A);
+                 PvSmallShape<REP>::SMEM + (size_t)A.bt_stride * 4, st, A);
     else
-      launch_pdl(pdl, k_attn_pv<HD, REP>, dim3(A.T * A.nkv), dim3(HD), PvShape<HD, REP>::SMEM, st, A);
+      launch_pdl(pdl, k_attn_pv<HD, REP>, dim3(A.T * A.nkv), dim3(HD), PvShape<HD, REP>::SMEM + (size_t)A.bt_stride * 4,
+                 st, A);
   }
   return cudaGetLastError();
 }
 
 static cudaError_t launch_attn_which(const AttnArgs& A, cudaStream_t st, int which) {
   int rep = A.nh / A.nkv;
-  if (A.T < 1 || A.T > SC_MAX_T || !A.rinv || !A.qn || !A.mkey || A.nh + A.nkv > 32 || A.page_stride % 4 != 0)
+  if (A.T < 1 || A.T > SC_MAX_T || A.bt_stride > ATT_MAX_BT || !A.rinv || !A.qn || !A.mkey || A.nh + A.nkv > 32 ||
+      A.page_stride % 4 != 0)
     return cudaErrorInvalidValue;
   if (A.hd == 128 && rep == 4) return launch_attn_t<128, 4>(A, st, which);
   if (A.hd == 64 && rep == 4) return launch_attn_t<64, 4>(A, st, which);
@@ -1430,10 +1488,10 @@ static cudaError_t prepare_attn_t() {
                                        (int)scores_smem<HD, REP>(SC_MAX_T));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute((const void*)k_attn_pv<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)PvShape<HD, REP>::SMEM);
+                             (int)(PvShape<HD, REP>::SMEM + ATT_MAX_BT * 4));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute((const void*)k_attn_pv_small<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)PvSmallShape<REP>::SMEM);
+                             (int)(PvSmallShape<REP>::SMEM + ATT_MAX_BT * 4));
   return e;
 }
 

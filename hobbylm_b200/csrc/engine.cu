@@ -13,6 +13,7 @@
 #include <unordered_set>
 #include <vector>
 
+#include "hg_ep.h"
 #include "hg_host.h"
 #include "hg_launch.h"
 
@@ -111,6 +112,7 @@ struct hg_engine {
   int blk_logits_rows = 0;
   std::vector<int32_t> last_sel;  // [n_layers][max_batch][k] from the last decode step
   int last_T = 0;
+  EpCtx* ep = nullptr;  // expert parallelism across ranks (hg_engine_ep_init), or none
   size_t device_bytes() const { return weights.cap + work.cap; }
 };
 
@@ -286,6 +288,7 @@ void load_engine(hg_engine* e, const char* path, const hg_engine_opts& o) {
   HG_CUDA(cudaSetDevice(e->device));
   HG_CUDA(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
   HG_CUDA(prepare_attn(c.head_dim, c.n_heads / c.n_kv_heads));
+  HG_CUDA(prepare_tc());
   e->cfg = c;
   Dims& D = e->D;
   D.d = c.d_model;
@@ -398,7 +401,8 @@ void free_engine(hg_engine* e) {
   e->live_seqs.clear();
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
-  for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);  // (their NCCL calls before the communicator)
+  ep_destroy(e->ep);
   e->weights.release();
   e->work.release();
   if (e->kv) cudaFree(e->kv);
@@ -477,7 +481,8 @@ void record_decode(hg_engine* e, const DecodeBufs& B) {
     HG_CUDA(launch_attn_args(A, st));
     launch_mv_resid(D, B, Ld.wo, B.qo, B.so, st);
     launch_route(D, B, Ld, l, 0, st);
-    launch_ffn(D, B, Ld, st);
+    if (e->ep && Ld.moe) ep_record_moe(e->ep, D, B, Ld, st);  // routed experts on their owners
+    else launch_ffn(D, B, Ld, st);
   }
   int mode = e->layers[D.L - 1].moe ? 2 : 1;
   launch_pre_norm(D, B, mode, e->embd, e->out_norm, B.qa, B.sa, nullptr, 0, 1, st);
@@ -1317,6 +1322,27 @@ int hg_decode_greedy(hg_engine* e, hg_seq** seqs, int n, const uint32_t* tokens,
 
 void* hg_engine_stream(const hg_engine* e) { return e ? (void*)e->stream : nullptr; }
 
+int hg_ep_unique_id(void* out) {
+  HG_API_TRY({
+    need(out, "null argument");
+    ep_unique_id(out);
+  })
+}
+
+int hg_engine_ep_init(hg_engine* e, const void* nccl_id, int rank, int world) {
+  HG_API_TRY({
+    need(e && nccl_id, "null argument");
+    need(!e->ep, "expert parallelism is already set up on this engine");
+    DeviceGuard g(e->device);
+    HG_CUDA(cudaStreamSynchronize(e->stream));
+    // step graphs recorded before hold the local experts: drop them
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+    e->graph_kernels.clear();
+    e->ep = ep_create(e->D, e->max_batch, e->device, nccl_id, rank, world);
+  })
+}
+
 int hg_decode_kernel_count(hg_engine* e, int n) {
   try {
     need(e && n > 0 && n <= e->max_batch, "bad argument");
@@ -1416,6 +1442,7 @@ int hg_op_q8_matvec(const int8_t* qs, const float* scales, int64_t rows, int64_t
     HG_CUDA(cudaMallocAsync((void**)&aq, (size_t)ntok * cols, st));
     HG_CUDA(cudaMallocAsync((void**)&as, (size_t)ntok * ss * 4, st));
     launch_quant_rows(x, ntok, (int)cols, aq, as, st);
+    HG_CUDA(prepare_tc());
     Dims D{};
     DecodeBufs B{};
     B.T = ntok;

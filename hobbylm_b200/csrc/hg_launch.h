@@ -17,6 +17,9 @@ void launch_pre_norm(const Dims& D, const DecodeBufs& B, int mode, const float* 
                      int8_t* q_out, float* s_out, float* h_out, int reset_moe, int reset_amax, cudaStream_t st);
 void launch_route(const Dims& D, const DecodeBufs& B, const LayerDev& L, int layer, int prenormed, cudaStream_t st);
 void launch_ffn(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaStream_t st);
+// group0: run the shared expert / dense FFN group; nrouted: routed-expert groups (slots of the
+// active-expert list B.active, counted in B.ecount[D.ne])
+void launch_ffn_ex(const Dims& D, const DecodeBufs& B, const LayerDev& L, bool group0, int nrouted, cudaStream_t st);
 void launch_moe_combine(const Dims& D, const DecodeBufs& B, float* y_out, cudaStream_t st);
 void launch_quant_rows(const float* x, int rows, int cols, int8_t* q, float* s, cudaStream_t st);
 cudaError_t launch_attn_args(const AttnArgs& A, cudaStream_t st);
@@ -25,6 +28,13 @@ cudaError_t launch_attn_scores_only(const AttnArgs& A, cudaStream_t st);
 cudaError_t launch_attn_out_only(const AttnArgs& A, cudaStream_t st);
 void launch_feedback(const DecodeBufs& B, int32_t* tok, int32_t* pos, int32_t* gen, int gen_cap, int32_t* step,
                      cudaStream_t st);
+
+// tc.cu: the tcgen05 Q8 matvec for steps of at least TC_MIN_T tokens (rows of 128-byte lane chunks)
+constexpr int TC_MIN_T = 32;
+cudaError_t prepare_tc();
+bool tc_usable(const Q8M& W, int T);
+void launch_mv_tc(const Dims& D, const DecodeBufs& B, const Q8M& W, const int8_t* aq, const float* as, float* out,
+                  int ostride, int epi, cudaStream_t st);
 
 // prefill.cu
 void launch_kp_norm(float* in, const float* add, int rows, int d, const float* w, float eps, float* h_out, int8_t* q,

@@ -195,6 +195,21 @@ class Engine:
     def stream(self) -> int:
         return int(lib().hg_engine_stream(self.h) or 0)
 
+    @staticmethod
+    def ep_unique_id() -> bytes:
+        """A new NCCL unique id (128 bytes) for expert parallelism (hobbylm_b200.ep)."""
+        buf = C.create_string_buffer(128)
+        check(lib().hg_ep_unique_id(buf))
+        return buf.raw
+
+    def ep_init(self, nccl_id: bytes, rank: int, world: int) -> None:
+        """Split the routed experts over `world` ranks (hg_engine_ep_init); call on every rank
+        before the first decode step. hobbylm_b200.ep.setup does the id exchange."""
+        if len(nccl_id) != 128:
+            raise HgError(-1, "an NCCL unique id is 128 bytes")
+        buf = C.create_string_buffer(bytes(nccl_id), 128)
+        check(lib().hg_engine_ep_init(self.h, buf, int(rank), int(world)))
+
     def decode_kernel_count(self, n: int) -> int:
         return check(lib().hg_decode_kernel_count(self.h, n))
 

@@ -151,6 +151,21 @@ int hg_decode_greedy(hg_engine* e, hg_seq** seqs, int n, const uint32_t* tokens,
 /* The engine's CUDA stream (a cudaStream_t), for callers that order or time work around it. */
 void* hg_engine_stream(const hg_engine* e);
 
+/* No counterpart in the reference (hobby-rs runs every expert in one process). Expert
+ * parallelism for batched decode on several GPUs: each rank (one process, one engine per GPU)
+ * decodes its own sequences, and the routed experts of every MoE layer are split evenly across the
+ * ranks (rank q owns experts [q E/W, (q+1) E/W)). A step sends each (token, selected expert) row to
+ * the expert's owner and the expert's output back over NCCL (two grouped send/recv exchanges per
+ * MoE layer, inside the step's CUDA graph); the shared expert and attention stay local. Results
+ * equal the one-GPU engine's bit for bit. hg_ep_unique_id fills out[128] with a new NCCL unique
+ * id; rank 0 makes one and gives the bytes to every rank (e.g. over torch.distributed), and each
+ * rank calls hg_engine_ep_init once, before its first decode step; the call returns when all
+ * `world` ranks have joined. Afterwards every rank must take its decode steps (hg_decode_batch /
+ * hg_decode_greedy / hg_forward) in lockstep: each step's exchanges pair up across ranks. n_experts
+ * must be a multiple of world (HG_ERR_INVALID otherwise); HG_ERR_CUDA if NCCL cannot be loaded. */
+int hg_ep_unique_id(void* out);
+int hg_engine_ep_init(hg_engine* e, const void* nccl_id, int rank, int world);
+
 /* Kernels one decode step of batch size n launches (kernel nodes of its CUDA graph), or < 0. */
 int hg_decode_kernel_count(hg_engine* e, int n);
 

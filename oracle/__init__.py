@@ -95,6 +95,7 @@ def lib():
         "hor_moe_free": (None, [vp]),
         "hor_moe_run": (i, [vp, f32p, i, i, f32p, vp, vp]),
         "hor_moe_sel_scores": (i, [vp, f32p, f32p]),
+        "hor_moe_expert": (i, [vp, f32p, i, f32p]),
         "hor_rope_create": (i, [i, i, f, C.POINTER(vp)]),
         "hor_rope_free": (None, [vp]),
         "hor_rope_tables": (i, [vp, f32p, f32p]),
@@ -388,6 +389,12 @@ class Moe:
         w = np.zeros((T, self.top_k), np.float32)
         _check(lib().hor_moe_run(self.h, x, T, mode, y, _ptr(sel), _ptr(w)))
         return y, sel, w
+
+    def expert(self, x, e: int) -> np.ndarray:
+        """Expert e's SwiGLU output on one row (e = -1: the shared expert), unscaled."""
+        y = np.zeros(self.d, np.float32)
+        _check(lib().hor_moe_expert(self.h, np.ascontiguousarray(x, np.float32), int(e), y))
+        return y
 
     def sel_scores(self, x) -> np.ndarray:
         out = np.zeros(self.ne, np.float32)

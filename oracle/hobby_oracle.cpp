@@ -1990,6 +1990,24 @@ int hor_moe_run(void* p, const float* x, int T, int mode, float* y, int32_t* sel
     }
   })
 }
+// One expert's SwiGLU output on one normed row (model.rs:300-305 for e >= 0, 313-318 for the shared
+// expert, e = -1), unscaled: the unit of work an expert-parallel rank computes for another.
+int hor_moe_expert(void* p, const float* x, int e, float* y) {
+  HOR_TRY({
+    MoeOp* op = (MoeOp*)p;
+    const Config& c = op->c;
+    const int f = c.expert_ffn;
+    if (e < -1 || e >= c.n_experts || (e == -1 && c.n_shared == 0)) throw Error("bad expert");
+    std::vector<float> gb(f), ub(f);
+    const Mat& G = e < 0 ? op->L.m.gate_sh : op->L.m.gate_exps[e];
+    const Mat& U = e < 0 ? op->L.m.up_sh : op->L.m.up_exps[e];
+    const Mat& Dn = e < 0 ? op->L.m.down_sh : op->L.m.down_exps[e];
+    G.matvec(x, gb.data());
+    U.matvec(x, ub.data());
+    for (int i = 0; i < f; i++) gb[i] = silu(gb[i]) * ub[i];
+    Dn.matvec(gb.data(), y);
+  })
+}
 // Router selection scores (sigmoid(W_r x) + bias) for one token, for margin reporting.
 int hor_moe_sel_scores(void* p, const float* x, float* sel_scores) {
   HOR_TRY({

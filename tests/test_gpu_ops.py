@@ -35,8 +35,11 @@ def _bits(a):
 
 
 @pytest.mark.parametrize("rows,cols", SHAPES)
-@pytest.mark.parametrize("ntok", [1, 3, 17])
+@pytest.mark.parametrize("ntok", [1, 3, 17, 40, 256])
 def test_q8_matvec_bitexact(native, oracle_mod, rows, cols, ntok):
+    """Decode matvec order (quant.rs:44-67) for one to 256 tokens. From 32 tokens on, rows whose
+    width is a multiple of 128 take the tensor-core kernel (exact int32 lane partials from
+    tcgen05.mma kind::i8, f32 chains on the CUDA cores); the others and smaller steps take dp4a."""
     import torch
 
     rng = np.random.default_rng(rows * 7 + cols + ntok)
