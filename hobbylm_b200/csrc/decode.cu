@@ -1159,8 +1159,21 @@ __global__ void __launch_bounds__(HD) k_attn_pv(AttnArgs A) {
       if (REP > 3) o[REP > 3 ? 3 : 0] = fadd(o[REP > 3 ? 3 : 0], fmul(pj.w, v));
     };
     if (rows == PV_STAGE) {
+      // the stage's V and p values into registers first, then the dependent adds
+      float vr[PV_STAGE];
+      float4 pr[PV_STAGE];
 #pragma unroll
-      for (int j = 0; j < PV_STAGE; j++) step(j);
+      for (int j = 0; j < PV_STAGE; j++) {
+        vr[j] = vs[j * HD];
+        pr[j] = pq[j];
+      }
+#pragma unroll
+      for (int j = 0; j < PV_STAGE; j++) {
+        o[0] = fadd(o[0], fmul(pr[j].x, vr[j]));
+        if (REP > 1) o[REP > 1 ? 1 : 0] = fadd(o[REP > 1 ? 1 : 0], fmul(pr[j].y, vr[j]));
+        if (REP > 2) o[REP > 2 ? 2 : 0] = fadd(o[REP > 2 ? 2 : 0], fmul(pr[j].z, vr[j]));
+        if (REP > 3) o[REP > 3 ? 3 : 0] = fadd(o[REP > 3 ? 3 : 0], fmul(pr[j].w, vr[j]));
+      }
     } else {
       for (int j = 0; j < rows; j++) step(j);
     }
@@ -1170,17 +1183,22 @@ __global__ void __launch_bounds__(HD) k_attn_pv(AttnArgs A) {
   for (int r = 0; r < REP; r++) pv_emit(A, t, (h0 + r) * HD + tid, o[r]);
 }
 
-template <int REP>
+// With only a few CTAs on the GPU (a handful of sequences) each must keep its own copies far ahead
+// of its chain to cover DRAM latency: those launches use the deep ring.
+constexpr int PVS_SLOTS_DEEP = 16;
+constexpr int PVS_DEEP_MAX_PAIRS = 12;
+
+template <int REP, int NSLOT>
 struct PvSmallShape {
   static constexpr int NT = 32 * REP;
   static constexpr int SLOT = PVS_STAGE * 32 + REP * PVS_STAGE;  // V rows of the slice, then e rows
-  static constexpr size_t SMEM = (size_t)PVS_SLOTS * SLOT * 4;
+  static constexpr size_t SMEM = (size_t)NSLOT * SLOT * 4;
 };
 
-template <int HD, int REP>
+template <int HD, int REP, int PVS_SLOTS>
 __global__ void __launch_bounds__(32 * REP) k_attn_pv_small(AttnArgs A) {
   static_assert(HD % 32 == 0 && (REP == 1 || REP == 2 || REP == 4), "32-dim slices; GQA group of 1, 2 or 4");
-  using S = PvSmallShape<REP>;
+  using S = PvSmallShape<REP, PVS_SLOTS>;
   constexpr int DS = HD / 32;  // slices per head
   extern __shared__ __align__(16) float pv_smem[];
   __shared__ __align__(16) float p_s[REP][2][PVS_STAGE];  // per warp (head), double-buffered
@@ -1243,13 +1261,29 @@ __global__ void __launch_bounds__(32 * REP) k_attn_pv_small(AttnArgs A) {
     const float4* pq = reinterpret_cast<const float4*>(&p_s[w][st & 1][0]);
     const int rows = min(PVS_STAGE, n - st * PVS_STAGE);
     if (rows == PVS_STAGE) {
+      // 16-position groups: the next group's V and p values are loaded into registers before the
+      // current group's dependent adds, so the add chain never waits on shared memory
+      constexpr int G = 16, NG = PVS_STAGE / G;
+      float vr[2][G];
+      float4 pr[2][G / 4];
+      auto load = [&](int g, int b) {
 #pragma unroll
-      for (int q = 0; q < PVS_STAGE / 4; q++) {
-        const float4 pj = pq[q];
-        o = fadd(o, fmul(pj.x, vs[(4 * q + 0) * 32]));
-        o = fadd(o, fmul(pj.y, vs[(4 * q + 1) * 32]));
-        o = fadd(o, fmul(pj.z, vs[(4 * q + 2) * 32]));
-        o = fadd(o, fmul(pj.w, vs[(4 * q + 3) * 32]));
+        for (int k = 0; k < G; k++) vr[b][k] = vs[(g * G + k) * 32];
+#pragma unroll
+        for (int k = 0; k < G / 4; k++) pr[b][k] = pq[g * (G / 4) + k];
+      };
+      load(0, 0);
+#pragma unroll
+      for (int g = 0; g < NG; g++) {
+        if (g + 1 < NG) load(g + 1, (g + 1) & 1);
+        const int b = g & 1;
+#pragma unroll
+        for (int k = 0; k < G / 4; k++) {
+          o = fadd(o, fmul(pr[b][k].x, vr[b][4 * k + 0]));
+          o = fadd(o, fmul(pr[b][k].y, vr[b][4 * k + 1]));
+          o = fadd(o, fmul(pr[b][k].z, vr[b][4 * k + 2]));
+          o = fadd(o, fmul(pr[b][k].w, vr[b][4 * k + 3]));
+        }
       }
     } else {
       for (int j = 0; j < rows; j++) o = fadd(o, fmul(p_s[w][st & 1][j], vs[j * 32]));
@@ -1386,6 +1420,10 @@ void launch_moe_combine(const Dims& D, const DecodeBufs& B, float* y_out, cudaSt
 }
 
 void launch_ffn(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaStream_t st) {
+  if (ffn_tc_usable(D, B, L)) {  // many tokens: the tensor-core FFN (tc.cu)
+    launch_ffn_tc(D, B, L, st);
+    return;
+  }
   const int nrouted = L.moe ? (D.ne < B.T * D.k ? D.ne : B.T * D.k) : 0;
   launch_ffn_ex(D, B, L, true, nrouted, st);
 }
@@ -1454,9 +1492,12 @@ static cudaError_t launch_attn_t(const AttnArgs& A, cudaStream_t st, int which) 
   }
   if (which & 2) {
     launch_pdl(pdl, k_attn_softmax, dim3(A.T * A.nh), dim3(SMX_THREADS), 0, st, A);
-    if (A.T * A.nkv <= PV_SMALL_MAX_PAIRS)
-      launch_pdl(pdl, k_attn_pv_small<HD, REP>, dim3(A.T * A.nkv * (HD / 32)), dim3(32 * REP),
-                 PvSmallShape<REP>::SMEM + (size_t)A.bt_stride * 4, st, A);
+    if (A.T * A.nkv <= PVS_DEEP_MAX_PAIRS)
+      launch_pdl(pdl, k_attn_pv_small<HD, REP, PVS_SLOTS_DEEP>, dim3(A.T * A.nkv * (HD / 32)), dim3(32 * REP),
+                 PvSmallShape<REP, PVS_SLOTS_DEEP>::SMEM + (size_t)A.bt_stride * 4, st, A);
+    else if (A.T * A.nkv <= PV_SMALL_MAX_PAIRS)
+      launch_pdl(pdl, k_attn_pv_small<HD, REP, PVS_SLOTS>, dim3(A.T * A.nkv * (HD / 32)), dim3(32 * REP),
+                 PvSmallShape<REP, PVS_SLOTS>::SMEM + (size_t)A.bt_stride * 4, st, A);
     else
       launch_pdl(pdl, k_attn_pv<HD, REP>, dim3(A.T * A.nkv), dim3(HD), PvShape<HD, REP>::SMEM + (size_t)A.bt_stride * 4,
                  st, A);
@@ -1490,8 +1531,12 @@ static cudaError_t prepare_attn_t() {
     e = cudaFuncSetAttribute((const void*)k_attn_pv<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)(PvShape<HD, REP>::SMEM + ATT_MAX_BT * 4));
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute((const void*)k_attn_pv_small<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(PvSmallShape<REP>::SMEM + ATT_MAX_BT * 4));
+    e = cudaFuncSetAttribute((const void*)k_attn_pv_small<HD, REP, PVS_SLOTS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(PvSmallShape<REP, PVS_SLOTS>::SMEM + ATT_MAX_BT * 4));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute((const void*)k_attn_pv_small<HD, REP, PVS_SLOTS_DEEP>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(PvSmallShape<REP, PVS_SLOTS_DEEP>::SMEM + ATT_MAX_BT * 4));
   return e;
 }
 

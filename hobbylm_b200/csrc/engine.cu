@@ -232,6 +232,9 @@ void alloc_work(hg_engine* e) {
   B.elist = a.take<int32_t>((size_t)ne * T);
   B.act = a.take<float>((size_t)T * act_stride);
   B.act_stride = act_stride;
+  B.ubuf = a.take<float>((size_t)T * act_stride);
+  B.qact = a.take<int8_t>((size_t)T * act_stride);
+  B.sact = a.take<float>((size_t)T * std::max(host_q8_ss(c.dense_ffn), (k + 1) * host_q8_ss(f)));
   B.y = a.take<float>((size_t)T * (k + 1) * d);
   B.s_stride = ((long long)c.context_length + 15) & ~15LL;
   B.S = a.take<float>((size_t)T * c.n_heads * B.s_stride);
@@ -1110,7 +1113,8 @@ size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
 // Scratch layout of hg_op_moe_ffn (device buffer supplied by the caller).
 struct MoeScratch {
-  size_t off_qh, off_sh, off_sel, off_selw, off_ecount, off_active, off_elist, off_act, off_y, off_err, total;
+  size_t off_qh, off_sh, off_sel, off_selw, off_ecount, off_active, off_elist, off_act, off_ubuf, off_qact, off_sact,
+      off_y, off_err, total;
 };
 MoeScratch moe_scratch_layout(const hg_moe_weights* w, int ntok) {
   MoeScratch s{};
@@ -1129,6 +1133,9 @@ MoeScratch moe_scratch_layout(const hg_moe_weights* w, int ntok) {
   s.off_active = take((size_t)ne * 4);
   s.off_elist = take((size_t)ne * ntok * 4);
   s.off_act = take((size_t)ntok * (k + 1) * f * 4);
+  s.off_ubuf = take((size_t)ntok * (k + 1) * f * 4);
+  s.off_qact = take((size_t)ntok * (k + 1) * f);
+  s.off_sact = take((size_t)ntok * (k + 1) * host_q8_ss(f) * 4);
   s.off_y = take((size_t)ntok * (k + 1) * d * 4);
   s.off_err = take(16);
   s.total = o;
@@ -1486,6 +1493,7 @@ int hg_op_moe_ffn(const hg_moe_weights* w, const float* x, int ntok, float* y, i
              w->top_k <= w->n_experts && w->n_experts <= 128,
          "unsupported MoE shape");
     cudaStream_t st = as_stream(stream);
+    HG_CUDA(prepare_tc());
     const int d = w->d_model, f = w->expert_ffn, k = w->top_k, ne = w->n_experts;
     MoeScratch L = moe_scratch_layout(w, ntok);
     char* base = static_cast<char*>(scratch);
@@ -1511,6 +1519,9 @@ int hg_op_moe_ffn(const hg_moe_weights* w, const float* x, int ntok, float* y, i
     B.elist = reinterpret_cast<int32_t*>(base + L.off_elist);
     B.act = reinterpret_cast<float*>(base + L.off_act);
     B.act_stride = (k + 1) * f;
+    B.ubuf = reinterpret_cast<float*>(base + L.off_ubuf);
+    B.qact = reinterpret_cast<int8_t*>(base + L.off_qact);
+    B.sact = reinterpret_cast<float*>(base + L.off_sact);
     B.y = reinterpret_cast<float*>(base + L.off_y);
     B.err = reinterpret_cast<int32_t*>(base + L.off_err);
     LayerDev Ld{};

@@ -35,6 +35,10 @@ cudaError_t prepare_tc();
 bool tc_usable(const Q8M& W, int T);
 void launch_mv_tc(const Dims& D, const DecodeBufs& B, const Q8M& W, const int8_t* aq, const float* as, float* out,
                   int ostride, int epi, cudaStream_t st);
+// the FFN of a layer on the tensor cores (gate, up, SwiGLU + quantization, down); needs B.ubuf,
+// B.qact and B.sact
+bool ffn_tc_usable(const Dims& D, const DecodeBufs& B, const LayerDev& L);
+void launch_ffn_tc(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaStream_t st);
 
 // prefill.cu
 void launch_kp_norm(float* in, const float* add, int rows, int d, const float* w, float eps, float* h_out, int8_t* q,

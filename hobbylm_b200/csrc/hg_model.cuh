@@ -70,6 +70,9 @@ struct DecodeBufs {
   int32_t* elist;          // [ne][T] packed (t * 32 + rank)
   float* act;              // [T][act_stride] SwiGLU activations per (token, slot)
   int act_stride;          // floats per token (max(dense_ffn, (k + 1) * expert_ffn))
+  float* ubuf;             // [T][act_stride] up-projection outputs (tensor-core FFN), or null
+  int8_t* qact;            // [T][act_stride] quantized SwiGLU activations (tensor-core FFN), or null
+  float* sact;             // their per-32 scales: [T][slots][ss(width)]
   float* y;                // [T][k + 1][d] expert outputs per (token, slot)
   float* S;                // [T][nh][s_stride] attention scores / exp weights
   long long s_stride;

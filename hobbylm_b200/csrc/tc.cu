@@ -23,6 +23,7 @@
 // Safety: every wait on an mbarrier is bounded (TC_SPIN_LIMIT polls); on expiry the CTA records
 // HG_ERR_TIMEOUT in the step's error word, skips the remaining work, and still frees its tensor
 // memory. No TMA and no multicast are used; all copies read this GPU's own memory.
+#include <algorithm>
 #include <cstdint>
 
 #include "hg_launch.h"
@@ -273,11 +274,291 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_mv_tc(Dims D, DecodeBufs B, Q
   }
 }
 
+// ------------------------------------------------------------------------------------------
+// Grouped tensor-core matvec for the FFN (model.rs:243-255, 295-324) of steps with many tokens.
+//
+// Groups: the shared expert or the dense FFN (group 0, every token) and the routed experts active
+// in the step (one group each, its token list from the router). A CTA covers 128 rows of the
+// group's matrix and strides over the group's 8-entry tiles. The MMAs and the f32 lane chains
+// are those of k_mv_tc; rows whose width is not a multiple of 128 bytes end in 1-3 tail blocks
+// (the packed layout keeps a tail block's 8 lanes of 4 bytes side by side), each one extra MMA with
+// one column per (entry, lane).
+//   GT_UP:   gate or up rows on the ffn-normed hidden state of each entry's token, stored per
+//            (token, slot) for k_swiglu_quant.
+//   GT_DOWN: down rows on each (token, slot)'s quantized SwiGLU activation, stored in y[t][slot].
+// ------------------------------------------------------------------------------------------
+enum { GT_UP = 0, GT_DOWN = 1 };
+
+struct GrpTc {
+  Q8M W;                   // routed-expert stack [ne][rows][cols]
+  Q8M W0;                  // group 0's matrix (shared expert / dense FFN); qs == null: no group 0
+  const int32_t* ecount;   // [ne + 2]: entries per expert, then the active-expert count
+  const int32_t* active;   // [ne]
+  const int32_t* elist;    // [ne][T]: t * 32 + slot
+  int T, ne, nrouted, slot0;
+  const int8_t* aq;        // inputs (lane-chunked rows of `cols` bytes)
+  const float* as;         // their scales (rows of ss floats)
+  int in_nslot;            // GT_UP: 0 (row = token); GT_DOWN: slots per token of the input rows
+  float* out;              // out[(t * out_nslot + slot) * ostride + row]
+  int out_nslot, ostride;
+  int nz;                  // CTAs striding over a group's entry tiles
+  int32_t* err;
+};
+
+constexpr int TC_TAIL_A = 3 * 4096;                 // tail A: up to 3 blocks x 128 rows x 32 B
+constexpr int TC_TAIL_B = 3 * TC_TOK * 256;         // tail B: up to 3 blocks x 8 entries x 8 lanes x 32 B
+constexpr size_t GT_SMEM = TC_SMEM + TC_TAIL_B;     // (tail A shares the weight ring's slot)
+
+template <int MODE>
+__global__ void __launch_bounds__(TC_THREADS, 2) k_grp_tc(GrpTc G) {
+  extern __shared__ __align__(16) unsigned char tc_raw[];
+  unsigned char* base = tc_raw + ((1024 - (smem_u32(tc_raw) & 1023)) & 1023);
+  unsigned char* wring = base;
+  unsigned char* bbuf = base + (size_t)TC_WSLOTS * TC_WCHUNK;
+  unsigned char* btail = bbuf + 2 * TC_BCHUNK;  // [3 tail blocks][8 entries][2 kc][8 lanes][16 B]
+  __shared__ uint64_t mma_bar;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int fail_s;
+  __shared__ int code_s[TC_TOK];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool has0 = G.W0.qs != nullptr;
+  const bool g0 = has0 && blockIdx.y == 0;
+  const int ri = (int)blockIdx.y - (has0 ? 1 : 0);  // routed slot in the active list
+  pdl_wait();  // the expert lists come from the router (or, for GT_DOWN, the activations from before)
+  pdl_trigger();
+  int expert = 0, count;
+  if (g0) {
+    count = G.T;
+  } else {
+    if (ri >= G.ecount[G.ne]) return;
+    expert = G.active[ri];
+    count = G.ecount[expert];
+  }
+  const Q8M& Wm = g0 ? G.W0 : G.W;
+  const int mi = g0 ? 0 : expert;
+  const int r0 = blockIdx.x * TC_M;
+  if (r0 >= Wm.rows) return;
+  const int ntiles = (count + TC_TOK - 1) / TC_TOK;
+  if ((int)blockIdx.z >= ntiles) return;
+  const int cols = Wm.cols, nb = cols >> 5, nch = nb >> 2, ntail = nb & 3, ss = Wm.ss;
+  const int nsteps = nch + (ntail ? 1 : 0);
+  const int8_t* wq = Wm.qs + (long long)mi * Wm.qs_mstride;
+  const float* wsc_m = Wm.sc + (long long)mi * Wm.sc_mstride;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                 "r"(TC_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    mbar_init(&mma_bar, 1);
+    fail_s = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  for (int i = tid; i < (2 * TC_BCHUNK + TC_TAIL_B) / 16; i += TC_THREADS)
+    reinterpret_cast<int4*>(bbuf)[i] = make_int4(0, 0, 0, 0);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base_s;
+
+  const int quad = warp & 3, half = warp >> 2;
+  const int row = r0 + quad * 32 + lane;
+  const bool row_ok = row < Wm.rows;
+  const float* wsc = wsc_m + (long long)(row_ok ? row : 0) * ss;
+  constexpr uint32_t IDESC = tc_idesc(TC_M, TC_N);
+  uint32_t phase = 0;
+  int fail = 0;
+
+  for (int tile = blockIdx.z; tile < ntiles; tile += G.nz) {
+    const int e0 = tile * TC_TOK, ntok = min(TC_TOK, count - e0);
+    __syncthreads();  // the previous tile is done with code_s
+    if (tid < TC_TOK)
+      code_s[tid] = tid < ntok ? (g0 ? (e0 + tid) * 32 + G.slot0 : G.elist[(size_t)expert * G.T + e0 + tid]) : -1;
+    __syncthreads();
+    // input row of entry tt (a valid row for padding entries)
+    auto in_row = [&](int tt) {
+      const int code = code_s[tt] < 0 ? code_s[0] : code_s[tt];
+      const int t = code >> 5, sl = code & 31;
+      return MODE == GT_UP ? t : t * G.in_nslot + sl;
+    };
+    auto issue_w = [&](int s) {
+      if (s < nch) {
+        unsigned char* dst = wring + (size_t)(s % TC_WSLOTS) * TC_WCHUNK;
+#pragma unroll
+        for (int k = 0; k < TC_WCHUNK / 16 / TC_THREADS; k++) {
+          const int i = tid + k * TC_THREADS, m = i >> 3, j = i & 7;
+          const int r = min(r0 + m, Wm.rows - 1);
+          cp_async16_tc(dst + m * 128 + ((j ^ (m & 7)) << 4), wq + (long long)r * cols + s * 128 + j * 16);
+        }
+      } else if (s == nch && ntail) {  // tail blocks, no swizzle: 8-row x 16-byte core matrices
+        unsigned char* dst = wring + (size_t)(s % TC_WSLOTS) * TC_WCHUNK;
+        for (int i = tid; i < TC_M * ntail * 2; i += TC_THREADS) {
+          const int m = i / (ntail * 2), rem = i - m * (ntail * 2), tb = rem >> 1, kc = rem & 1;
+          const int r = min(r0 + m, Wm.rows - 1);
+          cp_async16_tc(dst + tb * 4096 + (m >> 3) * 256 + kc * 128 + (m & 7) * 16,
+                        wq + (long long)r * cols + nch * 128 + tb * 32 + kc * 16);
+        }
+      }
+      cp_commit_tc();
+    };
+    auto stage_b = [&](int s) {
+      if (s < nch) {
+        const int q = tid & 3, li = (tid >> 2) & 1, tt = (tid >> 3) & (TC_TOK - 1), lp = tid >> 6;
+        int v = 0;
+        if (tt < ntok) v = *reinterpret_cast<const int*>(G.aq + (size_t)in_row(tt) * cols + s * 128 + lp * 32 + li * 16 + q * 4);
+        *reinterpret_cast<int*>(bbuf + (size_t)(s & 1) * TC_BCHUNK + lp * (TC_TOK * 256) + tt * 256 + li * 128 +
+                                (2 * q + li) * 16 + q * 4) = v;
+      } else if (tid < ntail * TC_TOK * 8) {  // tail block tb, entry tt, lane l: 4 bytes
+        const int l = tid & 7, tt = (tid >> 3) & (TC_TOK - 1), tb = tid >> 6;
+        int v = 0;
+        if (tt < ntok) v = *reinterpret_cast<const int*>(G.aq + (size_t)in_row(tt) * cols + nch * 128 + tb * 32 + l * 4);
+        *reinterpret_cast<int*>(btail + tb * (TC_TOK * 256) + tt * 256 + (l >> 2) * 128 + l * 16 + (l & 3) * 4) = v;
+      }
+    };
+    float acc[4][8];
+#pragma unroll
+    for (int tt = 0; tt < 4; tt++)
+#pragma unroll
+      for (int l = 0; l < 8; l++) acc[tt][l] = 0.0f;
+#pragma unroll
+    for (int s = 0; s < TC_WAHEAD; s++) issue_w(s);
+    stage_b(0);
+    for (int s = 0; s < nsteps; s++) {
+      issue_w(s + TC_WAHEAD);
+      cp_wait_tc<TC_WAHEAD>();
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      tc_fence_after();
+      const bool tail = s == nch;
+      if (tid == 0 && !fail) {
+        const uint32_t wa = smem_u32(wring + (size_t)(s % TC_WSLOTS) * TC_WCHUNK);
+        if (!tail) {
+          const uint32_t ba = smem_u32(bbuf + (size_t)(s & 1) * TC_BCHUNK);
+#pragma unroll
+          for (int lp = 0; lp < 4; lp++) {
+            const uint64_t ad = tc_desc(wa + lp * 32, 16, 1024, 2);
+            const uint64_t bd = tc_desc(ba + lp * (TC_TOK * 256), 128, 256, 0);
+            asm volatile(
+                "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(tbase + lp * TC_N),
+                "l"(ad), "l"(bd), "r"(IDESC), "r"(0));
+          }
+        } else {
+          const uint32_t ba = smem_u32(btail);
+          for (int tb = 0; tb < ntail; tb++) {
+            const uint64_t ad = tc_desc(wa + tb * 4096, 128, 256, 0);
+            const uint64_t bd = tc_desc(ba + tb * (TC_TOK * 256), 128, 256, 0);
+            asm volatile(
+                "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(tbase + tb * TC_N),
+                "l"(ad), "l"(bd), "r"(IDESC), "r"(0));
+          }
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(&mma_bar))
+                     : "memory");
+      }
+      if (s + 1 < nsteps) stage_b(s + 1);
+      // per-(entry, block) scales sw[row][b] * dx[entry][b] of this step's blocks
+      const int b0 = s * 4;
+      const float4 s4 = *reinterpret_cast<const float4*>(wsc + b0);
+      float sc[4][4];
+#pragma unroll
+      for (int tt = 0; tt < 4; tt++) {
+        const float4 d4 = *reinterpret_cast<const float4*>(G.as + (size_t)in_row(half * 4 + tt) * ss + b0);
+        sc[tt][0] = fmul(s4.x, d4.x);
+        sc[tt][1] = fmul(s4.y, d4.y);
+        sc[tt][2] = fmul(s4.z, d4.z);
+        sc[tt][3] = fmul(s4.w, d4.w);
+      }
+      if (!fail && !mbar_wait(&mma_bar, phase)) fail = 1;
+      fail = __any_sync(0xffffffffu, fail);
+      phase ^= 1;
+      tc_fence_after();
+      if (!fail) {
+        if (!tail) {
+#pragma unroll
+          for (int lp = 0; lp < 4; lp++) {
+            uint32_t v[32];
+            tmem_ld32(tbase + ((uint32_t)(quad * 32) << 16) + lp * TC_N + half * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int tt = 0; tt < 4; tt++)
+#pragma unroll
+              for (int q = 0; q < 4; q++)
+#pragma unroll
+                for (int li = 0; li < 2; li++) {
+                  const int l = 2 * lp + li;
+                  acc[tt][l] = __fmaf_rn(sc[tt][q], (float)(int)v[tt * 8 + 2 * q + li], acc[tt][l]);
+                }
+          }
+        } else {
+          for (int tb = 0; tb < ntail; tb++) {  // column tt * 8 + l: entry tt, lane l of block 4 nch + tb
+            uint32_t v[32];
+            tmem_ld32(tbase + ((uint32_t)(quad * 32) << 16) + tb * TC_N + half * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int tt = 0; tt < 4; tt++)
+#pragma unroll
+              for (int l = 0; l < 8; l++)
+                acc[tt][l] = __fmaf_rn(tb == 0 ? sc[tt][0] : tb == 1 ? sc[tt][1] : sc[tt][2], (float)(int)v[tt * 8 + l],
+                                       acc[tt][l]);
+          }
+        }
+      }
+    }
+    cp_wait_tc<0>();
+    // outputs of this tile: the lane tree (quant.rs:61-65)
+    if (!fail) {
+#pragma unroll
+      for (int tt = 0; tt < 4; tt++) {
+        const int e = half * 4 + tt;
+        if (e >= ntok || !row_ok) continue;
+        const float* a = acc[tt];
+        const float y = fadd(fadd(fadd(a[0], a[4]), fadd(a[2], a[6])), fadd(fadd(a[1], a[5]), fadd(a[3], a[7])));
+        const int code = code_s[e], t = code >> 5, sl = code & 31;
+        G.out[((size_t)t * G.out_nslot + sl) * G.ostride + row] = y;
+      }
+    }
+  }
+  if (fail) fail_s = 1;
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(TC_COLS));
+  if (fail_s && tid == 0 && G.err) atomicExch(G.err, HG_ERR_TIMEOUT);
+}
+
+// act = silu(g) * u (model.rs:247-248, 304, 317; silu ops.rs:80-82) of every (token, slot) row,
+// quantized per 32-block (quant.rs:112-123) into the lane-chunked layout the down projection reads.
+// One warp per 32-block.
+__global__ void __launch_bounds__(256) k_swiglu_quant(const float* __restrict__ g, const float* __restrict__ u,
+                                                      long long nrows, int fd, int8_t* q, float* sq) {
+  const int nb = fd >> 5, ssq = q8_ss(nb);
+  const long long blk = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  pdl_wait();
+  pdl_trigger();
+  if (blk >= nrows * nb) return;
+  const long long r = blk / nb;
+  const int b = (int)(blk - r * nb), lane = threadIdx.x & 31;
+  const size_t i = (size_t)r * fd + b * 32 + lane;
+  const float a = fmul(silu_ref(g[i]), u[i]);
+  float d;
+  const int8_t qv = quant_lane(a, &d);
+  q[(size_t)r * fd + q8_pos(b * 32 + lane, nb)] = qv;
+  if (lane == 0) sq[(size_t)r * ssq + b] = d;
+}
+
 static bool g_tc_ready[64];
 
 template <int EPI>
 static cudaError_t prepare_tc_t() {
   return cudaFuncSetAttribute((const void*)k_mv_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM);
+}
+template <int MODE>
+static cudaError_t prepare_grp_t() {
+  return cudaFuncSetAttribute((const void*)k_grp_tc<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GT_SMEM);
 }
 
 cudaError_t prepare_tc() {
@@ -287,6 +568,8 @@ cudaError_t prepare_tc() {
   if ((e = prepare_tc_t<TC_EPI_STORE>()) != cudaSuccess) return e;
   if ((e = prepare_tc_t<TC_EPI_RESID>()) != cudaSuccess) return e;
   if ((e = prepare_tc_t<TC_EPI_LMHEAD>()) != cudaSuccess) return e;
+  if ((e = prepare_grp_t<GT_UP>()) != cudaSuccess) return e;
+  if ((e = prepare_grp_t<GT_DOWN>()) != cudaSuccess) return e;
   if (dev >= 0 && dev < 64) g_tc_ready[dev] = true;
   return cudaSuccess;
 }
@@ -313,6 +596,74 @@ void launch_mv_tc(const Dims& D, const DecodeBufs& B, const Q8M& W, const int8_t
   if (epi == TC_EPI_STORE) cudaLaunchKernelEx(&cfg, k_mv_tc<TC_EPI_STORE>, D, B, W, aq, as, out, ostride);
   else if (epi == TC_EPI_RESID) cudaLaunchKernelEx(&cfg, k_mv_tc<TC_EPI_RESID>, D, B, W, aq, as, out, ostride);
   else cudaLaunchKernelEx(&cfg, k_mv_tc<TC_EPI_LMHEAD>, D, B, W, aq, as, out, ostride);
+}
+
+bool ffn_tc_usable(const Dims& D, const DecodeBufs& B, const LayerDev& L) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || !g_tc_ready[dev]) return false;
+  return B.T >= TC_MIN_T && B.ubuf && B.qact && B.sact && D.d % 128 == 0 && (L.moe ? D.f : D.df) % 32 == 0;
+}
+
+// The FFN of one layer for a step of many tokens: gate and up on the tensor cores, SwiGLU and the
+// quantization of the activations, down on the tensor cores. Same results as launch_ffn.
+void launch_ffn_tc(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaStream_t st) {
+  const bool moe = L.moe != 0;
+  const int fd = moe ? D.f : D.df, bslot = moe ? D.k + 1 : 1;
+  const int nrouted = moe ? std::min(D.ne, B.T * D.k) : 0;
+  const bool shared = moe ? D.nsh > 0 : true;
+  GrpTc G{};
+  G.T = B.T;
+  G.ne = D.ne;
+  G.nrouted = nrouted;
+  G.ecount = B.ecount;
+  G.active = B.active;
+  G.elist = B.elist;
+  G.err = B.err;
+  G.slot0 = moe ? D.k : 0;
+  G.nz = std::min((B.T + TC_TOK - 1) / TC_TOK, 16);
+  const int groups = (shared ? 1 : 0) + nrouted;
+  if (groups == 0) return;
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = GT_SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = B.T <= 64 ? 1 : 0;
+  auto up = [&](const Q8M& routed, const Q8M& grp0, float* out) {
+    G.W = moe ? routed : Q8M{};
+    G.W0 = shared ? grp0 : Q8M{};
+    G.aq = B.qh;
+    G.as = B.sh;
+    G.in_nslot = 0;
+    G.out = out;
+    G.out_nslot = bslot;
+    G.ostride = fd;
+    cfg.gridDim = dim3((fd + TC_M - 1) / TC_M, groups, G.nz);
+    cudaLaunchKernelEx(&cfg, k_grp_tc<GT_UP>, G);
+  };
+  up(L.gate, moe ? L.sgate : L.gate, B.act);
+  up(L.up, moe ? L.sup : L.up, B.ubuf);
+  const long long nrows = (long long)B.T * bslot, nblk = nrows * (fd >> 5);
+  {
+    cudaLaunchConfig_t c2 = cfg;
+    c2.gridDim = dim3((unsigned)((nblk + 7) / 8));
+    c2.blockDim = dim3(256);
+    c2.dynamicSmemBytes = 0;
+    cudaLaunchKernelEx(&c2, k_swiglu_quant, (const float*)B.act, (const float*)B.ubuf, nrows, fd, B.qact, B.sact);
+  }
+  G.W = moe ? L.down : Q8M{};
+  G.W0 = shared ? (moe ? L.sdown : L.down) : Q8M{};
+  G.aq = B.qact;
+  G.as = B.sact;
+  G.in_nslot = bslot;
+  G.out = B.y;
+  G.out_nslot = D.k + 1;
+  G.ostride = D.d;
+  cfg.gridDim = dim3((D.d + TC_M - 1) / TC_M, groups, G.nz);
+  cudaLaunchKernelEx(&cfg, k_grp_tc<GT_DOWN>, G);
 }
 
 }  // namespace hg
