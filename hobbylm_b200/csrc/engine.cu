@@ -196,7 +196,7 @@ void alloc_work(hg_engine* e) {
   // prefill sizing
   const int PF = e->pf_rows;
   const int rep = c.n_heads / c.n_kv_heads;
-  const size_t s_elems = (size_t)c.context_length * e->pf_tq * rep;
+  const size_t s_elems = (size_t)c.context_length * e->pf_tq * rep * c.n_kv_heads;  // every kv head's scores
   const size_t pf_act = std::max((size_t)PF * c.dense_ffn, (size_t)PF * (k + 1) * f);
   const size_t pf_act_s = std::max((size_t)PF * host_q8_ss(c.dense_ffn), (size_t)PF * (k + 1) * host_q8_ss(f));
   Arena& a = e->work;
@@ -257,7 +257,7 @@ void alloc_work(hg_engine* e) {
   P.y = a.take<float>((size_t)PF * (k + 1) * d);
   P.selw = a.take<float>((size_t)PF * k);
   P.S = a.take<float>(s_elems);
-  P.inv = a.take<float>((size_t)e->pf_tq * rep);
+  P.inv = a.take<float>((size_t)e->pf_tq * rep * c.n_kv_heads);
   P.qa = a.take<int8_t>((size_t)PF * std::max(d, qd));
   P.qact = a.take<int8_t>(pf_act);
   P.sa = a.take<float>((size_t)PF * std::max(ss_d, ss_q));

@@ -210,124 +210,203 @@ __global__ void __launch_bounds__(128) kp_qk_rope_append(const float* qkv, int r
 }
 
 // ------------------------------------------------------------------------------------------
-// Attention scores for a tile of query rows. R = (t_local, head-in-group) flattened for one kv
-// head g: R = t_local * rep + hr. S[j][R] = dot(q, k_j) * scale for j < base + t + 1 (causal), or
-// for j < nfix when nfix > 0: every row attends to the same nfix keys, the diffusion block's
-// prefix plus the whole block (model.rs:556-565). One thread per (R, j) with the ops::dot order
-// computed per SIMD lane.
+// Attention scores of query rows against positions, all kv heads in one launch (blockIdx.z =
+// kv head g, scores of head g at S + g * s_head). Rows R = (t_local, head-in-group) flattened:
+// R = t_local * rep + hr. S[j][R] = dot(q, k_j) * scale for j < base + t + 1 (causal), or for
+// j < nfix when nfix > 0: every row attends to the same nfix keys, the diffusion block's prefix
+// plus the whole block (model.rs:556-565).
+//
+// The ops::dot order (ops.rs:7-36): accumulator m (0..3) of SIMD lane l (0..7) is the chain
+// c = fma(a[32i + 8m + l], b[...], c) over i = 0..HD/32-1 from 0, lane l sums (c0 + c1) + (c2 + c3),
+// and the lanes meet in the tree ((t0+t4)+(t2+t6))+((t1+t5)+(t3+t7)). Shared memory keeps each
+// row with the HD/32 elements of one (l, m) chain side by side, so a chain's operands are one
+// vector load. CTA: 64 rows x a run of KP_KTILES tiles of 32 positions; a warp owns 4 positions
+// of a tile (broadcast loads), a lane 2 rows (lane, lane + 32: coalesced stores).
 // ------------------------------------------------------------------------------------------
+constexpr int KP_SR = 64;      // rows per CTA
+constexpr int KP_SJ = 32;      // positions per tile
+constexpr int KP_KTILES = 8;   // tiles per CTA
+// padded row length (floats): an odd number of vector widths, so lanes reading different rows
+// at the same offset hit different banks
 template <int HD>
-__global__ void __launch_bounds__(256) kp_scores(const float* q, int qd, int t0, int tq, int base, int rep, int kvh,
+constexpr int kp_row_stride() { return HD + (HD / 32 == 4 ? 4 : 2); }
+template <int HD>
+constexpr size_t kp_scores_smem() { return (size_t)(KP_SR + KP_SJ) * kp_row_stride<HD>() * sizeof(float); }
+
+template <int NI> struct KpVec;
+template <> struct KpVec<4> {
+  float v[4];
+  __device__ __forceinline__ void load(const float* p) {
+    const float4 t = *reinterpret_cast<const float4*>(p);
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+  }
+};
+template <> struct KpVec<2> {
+  float v[2];
+  __device__ __forceinline__ void load(const float* p) {
+    const float2 t = *reinterpret_cast<const float2*>(p);
+    v[0] = t.x; v[1] = t.y;
+  }
+};
+
+template <int HD>
+__global__ void __launch_bounds__(256) kp_scores(const float* q, int qd, int t0, int tq, int base, int rep,
                                                  const int32_t* bt, const float* k_pool, long long page_stride,
-                                                 float* S, int nR, int nfix) {
-  __shared__ float qs[32][HD + 1];
-  __shared__ float ks[32][HD + 1];
-  const int R0 = blockIdx.x * 32, j0 = blockIdx.y * 32;
-  const int nmax = nfix > 0 ? nfix : base + t0 + tq;  // longest row in the tile set
-  if (j0 >= nmax) return;
-  // rows of this R tile: token t_local = R / rep, head = kvh*rep + R%rep
-  for (int i = threadIdx.x; i < 32 * HD; i += 256) {
-    int rr = i / HD, dd = i - rr * HD;
-    int R = R0 + rr;
+                                                 float* S, long long s_head, int nR, int nfix) {
+  constexpr int NI = HD / 32, RS = kp_row_stride<HD>();
+  extern __shared__ __align__(16) float kp_sm[];
+  float* qs = kp_sm;              // [KP_SR][RS]
+  float* ks = kp_sm + KP_SR * RS; // [KP_SJ][RS]
+  const int g = blockIdx.z;
+  const int R0 = blockIdx.x * KP_SR, jt0 = blockIdx.y * KP_KTILES * KP_SJ;
+  const int Rl = min(R0 + KP_SR - 1, nR - 1);
+  const int lim_hi = nfix > 0 ? nfix : base + t0 + Rl / rep + 1;  // longest row of the tile
+  if (jt0 >= lim_hi) return;
+  float* Sg = S + (size_t)g * s_head;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // element e = 32 ii + 8 m + l of a row goes to (l * 4 + m) * NI + ii
+  auto perm = [](int e) { return (((e & 7) * 4 + ((e >> 3) & 3)) * NI) + (e >> 5); };
+  for (int i = tid; i < KP_SR * HD; i += 256) {
+    const int rr = i / HD, e = i - rr * HD, R = R0 + rr;
     float v = 0.0f;
     if (R < nR) {
-      int tl = R / rep, hr = R - tl * rep;
-      v = q[(size_t)(t0 + tl) * qd + (size_t)(kvh * rep + hr) * HD + dd];
+      const int tl = R / rep, hr = R - tl * rep;
+      v = q[(size_t)(t0 + tl) * qd + (size_t)(g * rep + hr) * HD + e];
     }
-    qs[rr][dd] = v;
-    int j = j0 + rr;
-    float kv = 0.0f;
-    if (j < nmax) kv = k_pool[(long long)bt[j / PAGE] * page_stride + ((long long)kvh * PAGE + (j % PAGE)) * HD + dd];
-    ks[rr][dd] = kv;
+    qs[rr * RS + perm(e)] = v;
   }
-  __syncthreads();
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
-  for (int o = threadIdx.x; o < 32 * 32; o += 256) {
-    int jj = o >> 5, rr = o & 31;  // consecutive threads -> consecutive R (coalesced store)
-    int R = R0 + rr, j = j0 + jj;
-    if (R >= nR) continue;
-    int tl = R / rep;
-    if (j >= (nfix > 0 ? nfix : base + t0 + tl + 1)) continue;
-    const float* a = qs[rr];
-    const float* b = ks[jj];
-    float t8[8];
+  int lim[2];
 #pragma unroll
-    for (int l = 0; l < 8; l++) {
-      float cm[4];
+  for (int k = 0; k < 2; k++) {
+    const int R = R0 + lane + 32 * k;
+    lim[k] = R < nR ? (nfix > 0 ? nfix : base + t0 + R / rep + 1) : 0;
+  }
+  const float* qa0 = qs + lane * RS;
+  const float* qa1 = qs + (lane + 32) * RS;
+  for (int kt = 0; kt < KP_KTILES; kt++) {
+    const int j0 = jt0 + kt * KP_SJ;
+    if (j0 >= lim_hi) break;  // CTA-uniform
+    __syncthreads();          // the previous tile's keys are no longer read
+    for (int i = tid; i < KP_SJ * HD; i += 256) {
+      const int jj = i / HD, e = i - jj * HD, j = j0 + jj;
+      float v = 0.0f;
+      if (j < lim_hi)
+        v = k_pool[(long long)bt[j / PAGE] * page_stride + ((long long)g * PAGE + (j % PAGE)) * HD + e];
+      ks[jj * RS + perm(e)] = v;
+    }
+    __syncthreads();
+    // pairs (row lane + 32 r, position j0 + 4 warp + p)
+    float A[2][4], Bt[2][4], Dt[2][4];
+    constexpr int LORD[8] = {0, 4, 2, 6, 1, 5, 3, 7};
+#pragma unroll
+    for (int li = 0; li < 8; li++) {
+      const int l = LORD[li];
+      float pc[2][4], qc[2][4];
 #pragma unroll
       for (int m = 0; m < 4; m++) {
-        float c = __fmaf_rn(a[8 * m + l], b[8 * m + l], 0.0f);
+        KpVec<NI> a[2], b[4];
+        a[0].load(qa0 + (l * 4 + m) * NI);
+        a[1].load(qa1 + (l * 4 + m) * NI);
 #pragma unroll
-        for (int i = 32; i < HD; i += 32) c = __fmaf_rn(a[i + 8 * m + l], b[i + 8 * m + l], c);
-        cm[m] = c;
+        for (int p = 0; p < 4; p++) b[p].load(ks + (warp * 4 + p) * RS + (l * 4 + m) * NI);
+#pragma unroll
+        for (int r = 0; r < 2; r++)
+#pragma unroll
+          for (int p = 0; p < 4; p++) {
+            float c = __fmaf_rn(a[r].v[0], b[p].v[0], 0.0f);
+#pragma unroll
+            for (int ii = 1; ii < NI; ii++) c = __fmaf_rn(a[r].v[ii], b[p].v[ii], c);
+            if (m == 0) pc[r][p] = c;
+            else if (m == 1) pc[r][p] = fadd(pc[r][p], c);
+            else if (m == 2) qc[r][p] = c;
+            else qc[r][p] = fadd(qc[r][p], c);
+          }
       }
-      t8[l] = fadd(fadd(cm[0], cm[1]), fadd(cm[2], cm[3]));
+#pragma unroll
+      for (int r = 0; r < 2; r++)
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+          const float t = fadd(pc[r][p], qc[r][p]);  // lane l: (c0 + c1) + (c2 + c3)
+          if (li == 0) A[r][p] = t;
+          else if (li == 1) A[r][p] = fadd(A[r][p], t);             // t0 + t4
+          else if (li == 2) Bt[r][p] = t;
+          else if (li == 3) A[r][p] = fadd(A[r][p], fadd(Bt[r][p], t));  // (t0+t4)+(t2+t6)
+          else if (li == 4) Bt[r][p] = t;
+          else if (li == 5) Bt[r][p] = fadd(Bt[r][p], t);           // t1 + t5
+          else if (li == 6) Dt[r][p] = t;
+          else A[r][p] = fadd(A[r][p], fadd(Bt[r][p], fadd(Dt[r][p], t)));  // + ((t1+t5)+(t3+t7))
+        }
     }
-    float s = fadd(fadd(fadd(t8[0], t8[4]), fadd(t8[2], t8[6])), fadd(fadd(t8[1], t8[5]), fadd(t8[3], t8[7])));
-    S[(size_t)j * nR + R] = fmul(s, scale);
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+      const int R = R0 + lane + 32 * r;
+#pragma unroll
+      for (int p = 0; p < 4; p++) {
+        const int j = j0 + warp * 4 + p;
+        if (j < lim[r]) Sg[(size_t)j * nR + R] = fmul(A[r][p], scale);
+      }
+    }
   }
 }
 
-// Softmax of 32 score rows (ops.rs:112-128) per CTA of 1024 threads: the row maxima in parallel
-// (order does not matter for a max), then in chunks of 256 positions e = exp(s - max) is written
-// back in place and staged in shared memory, where lane r of warp 0 adds row r's values in
-// position order (the reference's sequential sum). inv[R] = 1 / sum. Row lengths as kp_scores.
-__global__ void __launch_bounds__(1024) kp_softmax_rows(float* S, int nR, int rep, int base, int t0, int nfix,
-                                                        float* inv) {
-  __shared__ float ch[256][33];
-  __shared__ float mred[32][33];
-  __shared__ float m_s[32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int R = blockIdx.x * 32 + lane;
-  const bool valid = R < nR;
-  const int n = valid ? (nfix > 0 ? nfix : base + t0 + R / rep + 1) : 0;
-  const int Rl = min(blockIdx.x * 32 + 31, nR - 1);
-  const int nmax = nfix > 0 ? nfix : base + t0 + Rl / rep + 1;
+// Softmax of score rows (ops.rs:112-128), all kv heads (blockIdx.y = g). One thread per row:
+// the maximum, then e = exp(s - max) written back in place and summed in position order in a
+// register chain (the reference's sequential sum); inv[g * nR + R] = 1 / sum. Row lengths as
+// kp_scores. Lanes are consecutive rows, so every load and store is coalesced.
+__global__ void __launch_bounds__(32) kp_softmax_rows(float* S, long long s_head, int nR, int rep, int base, int t0,
+                                                      int nfix, float* inv) {
+  const int g = blockIdx.y, R = blockIdx.x * 32 + threadIdx.x;
+  if (R >= nR) return;
+  float* Sg = S + (size_t)g * s_head + R;
+  const int n = nfix > 0 ? nfix : base + t0 + R / rep + 1;
   float m = -INFINITY;
-  for (int j = warp; j < nmax; j += 32)
-    if (j < n) {
-      float v = S[(size_t)j * nR + R];
-      if (v > m) m = v;
-    }
-  mred[warp][lane] = m;
-  __syncthreads();
-  if (warp == 0) {
-    float mm = -INFINITY;
-    for (int w = 0; w < 32; w++) mm = fmaxf(mm, mred[w][lane]);
-    m_s[lane] = mm;
+  int j = 0;
+  for (; j + 4 <= n; j += 4) {
+    const float v0 = Sg[(size_t)j * nR], v1 = Sg[(size_t)(j + 1) * nR];
+    const float v2 = Sg[(size_t)(j + 2) * nR], v3 = Sg[(size_t)(j + 3) * nR];
+    if (v0 > m) m = v0;
+    if (v1 > m) m = v1;
+    if (v2 > m) m = v2;
+    if (v3 > m) m = v3;
   }
-  __syncthreads();
-  const float mrow = m_s[lane];
+  for (; j < n; j++) {
+    const float v = Sg[(size_t)j * nR];
+    if (v > m) m = v;
+  }
   float sum = 0.0f;
-  for (int j0 = 0; j0 < nmax; j0 += 256) {
-    for (int jj = warp; jj < 256; jj += 32) {
-      const int j = j0 + jj;
-      float e = 0.0f;
-      if (j < n) {
-        e = exp_cr(__fsub_rn(S[(size_t)j * nR + R], mrow));
-        S[(size_t)j * nR + R] = e;
-      }
-      ch[jj][lane] = e;
+  j = 0;
+  for (; j + 4 <= n; j += 4) {
+    float e[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) e[u] = exp_cr(__fsub_rn(Sg[(size_t)(j + u) * nR], m));
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      Sg[(size_t)(j + u) * nR] = e[u];
+      sum = fadd(sum, e[u]);
     }
-    __syncthreads();
-    if (warp == 0) {  // adding the zeros past a row's end leaves its sum unchanged (sum >= +0)
-#pragma unroll 8
-      for (int jj = 0; jj < 256; jj++) sum = fadd(sum, ch[jj][lane]);
-    }
-    __syncthreads();
   }
-  if (warp == 0 && valid) inv[R] = __fdiv_rn(1.0f, sum);
+  for (; j < n; j++) {
+    const float e = exp_cr(__fsub_rn(Sg[(size_t)j * nR], m));
+    Sg[(size_t)j * nR] = e;
+    sum = fadd(sum, e);
+  }
+  inv[(size_t)g * nR + R] = __fdiv_rn(1.0f, sum);
 }
 
 // O[t][h][dd] = sum_j (e_j * inv) * v_j[dd], sequential in j (model.rs:426-432; 573-584 for a
-// diffusion block, whose prefix-then-block order is position order). Tile: 32 R x HD.
+// diffusion block, whose prefix-then-block order is position order). Tile: 32 R x HD of kv head
+// g = blockIdx.y.
 template <int HD>
-__global__ void __launch_bounds__(256) kp_pv(const float* S, const float* inv, int nR, int rep, int base, int t0,
-                                             int nfix, int kvh, const int32_t* bt, const float* v_pool,
+__global__ void __launch_bounds__(256) kp_pv(const float* S, long long s_head, const float* inv, int nR, int rep,
+                                             int base, int t0, int nfix, const int32_t* bt, const float* v_pool,
                                              long long page_stride, float* o, int qd) {
   constexpr int PD = HD / 32;  // dims per thread (threads: 8 R-groups x 32 dims)
   __shared__ float ps[32][33];
   __shared__ float vs[32][HD];
+  const int kvh = blockIdx.y;
+  const float* Sg = S + (size_t)kvh * s_head;
+  const float* ig = inv + (size_t)kvh * nR;
   const int R0 = blockIdx.x * 32;
   const int rg = threadIdx.x >> 5, dl = threadIdx.x & 31;  // rows rg*4..rg*4+3, dims dl + 32*k
   float acc[4][PD];
@@ -341,7 +420,7 @@ __global__ void __launch_bounds__(256) kp_pv(const float* S, const float* inv, i
   for (int i = 0; i < 4; i++) {
     int R = R0 + rg * 4 + i;
     lim[i] = R < nR ? (nfix > 0 ? nfix : base + t0 + R / rep + 1) : 0;
-    iv[i] = R < nR ? inv[R] : 0.0f;
+    iv[i] = R < nR ? ig[R] : 0.0f;
   }
   int Rlast = min(R0 + 31, nR - 1);
   const int nmax = nfix > 0 ? nfix : base + t0 + Rlast / rep + 1;
@@ -350,7 +429,7 @@ __global__ void __launch_bounds__(256) kp_pv(const float* S, const float* inv, i
     for (int i = threadIdx.x; i < 32 * 32; i += 256) {
       int jj = i >> 5, rr = i & 31;
       int R = R0 + rr, j = j0 + jj;
-      ps[rr][jj] = (R < nR && j < nmax) ? S[(size_t)j * nR + R] : 0.0f;
+      ps[rr][jj] = (R < nR && j < nmax) ? Sg[(size_t)j * nR + R] : 0.0f;
     }
     for (int i = threadIdx.x; i < 32 * HD; i += 256) {
       int jj = i / HD, dd = i - jj * HD;
@@ -563,20 +642,33 @@ void launch_kp_qk_rope_append(const float* qkv, int rows, int base, int nh, int 
 void launch_kp_attention(const float* q, int qd, int t0, int tq, int base, int nfix, int nh, int nkv, int hd,
                          const int32_t* bt, const float* k_pool, const float* v_pool, long long page_stride, float* S,
                          float* inv, float* o, cudaStream_t st) {
+  static bool smem_set[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !smem_set[dev]) {
+    cudaFuncSetAttribute((const void*)kp_scores<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kp_scores_smem<128>());
+    cudaFuncSetAttribute((const void*)kp_scores<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kp_scores_smem<64>());
+    smem_set[dev] = true;
+  }
   const int rep = nh / nkv;
   const int nR = tq * rep;
   const int nmax = nfix > 0 ? nfix : base + t0 + tq;
-  for (int g = 0; g < nkv; g++) {
-    dim3 gs((nR + 31) / 32, (nmax + 31) / 32);
-    if (hd == 128)
-      kp_scores<128><<<gs, 256, 0, st>>>(q, qd, t0, tq, base, rep, g, bt, k_pool, page_stride, S, nR, nfix);
-    else kp_scores<64><<<gs, 256, 0, st>>>(q, qd, t0, tq, base, rep, g, bt, k_pool, page_stride, S, nR, nfix);
-    kp_softmax_rows<<<(nR + 31) / 32, 1024, 0, st>>>(S, nR, rep, base, t0, nfix, inv);
-    dim3 gp((nR + 31) / 32);
-    if (hd == 128)
-      kp_pv<128><<<gp, 256, 0, st>>>(S, inv, nR, rep, base, t0, nfix, g, bt, v_pool, page_stride, o, qd);
-    else kp_pv<64><<<gp, 256, 0, st>>>(S, inv, nR, rep, base, t0, nfix, g, bt, v_pool, page_stride, o, qd);
-  }
+  const long long s_head = (long long)nmax * nR;  // scores of one kv head
+  const dim3 gs((nR + KP_SR - 1) / KP_SR, (nmax + KP_KTILES * KP_SJ - 1) / (KP_KTILES * KP_SJ), nkv);
+  if (hd == 128)
+    kp_scores<128><<<gs, 256, kp_scores_smem<128>(), st>>>(q, qd, t0, tq, base, rep, bt, k_pool, page_stride, S,
+                                                           s_head, nR, nfix);
+  else
+    kp_scores<64><<<gs, 256, kp_scores_smem<64>(), st>>>(q, qd, t0, tq, base, rep, bt, k_pool, page_stride, S,
+                                                         s_head, nR, nfix);
+  kp_softmax_rows<<<dim3((nR + 31) / 32, nkv), 32, 0, st>>>(S, s_head, nR, rep, base, t0, nfix, inv);
+  const dim3 gp((nR + 31) / 32, nkv);
+  if (hd == 128)
+    kp_pv<128><<<gp, 256, 0, st>>>(S, s_head, inv, nR, rep, base, t0, nfix, bt, v_pool, page_stride, o, qd);
+  else
+    kp_pv<64><<<gp, 256, 0, st>>>(S, s_head, inv, nR, rep, base, t0, nfix, bt, v_pool, page_stride, o, qd);
 }
 void launch_kp_route(const float* h, int tn, int d, const float* router, const float* bias, int ne, int k, int gsig,
                      int wnorm, float wscale, int32_t* sel, float* selw, int32_t* ecount, int32_t* elist, int list_cap,
