@@ -356,109 +356,154 @@ __global__ void __launch_bounds__(256) kp_scores(const float* q, int qd, int t0,
 // kp_scores. Lanes are consecutive rows, so every load and store is coalesced.
 __global__ void __launch_bounds__(32) kp_softmax_rows(float* S, long long s_head, int nR, int rep, int base, int t0,
                                                       int nfix, float* inv) {
+  constexpr int U = 8;  // positions in flight per thread (few rows per launch: parallelism per thread)
   const int g = blockIdx.y, R = blockIdx.x * 32 + threadIdx.x;
   if (R >= nR) return;
   float* Sg = S + (size_t)g * s_head + R;
+  const size_t st = (size_t)nR;
   const int n = nfix > 0 ? nfix : base + t0 + R / rep + 1;
   float m = -INFINITY;
   int j = 0;
-  for (; j + 4 <= n; j += 4) {
-    const float v0 = Sg[(size_t)j * nR], v1 = Sg[(size_t)(j + 1) * nR];
-    const float v2 = Sg[(size_t)(j + 2) * nR], v3 = Sg[(size_t)(j + 3) * nR];
-    if (v0 > m) m = v0;
-    if (v1 > m) m = v1;
-    if (v2 > m) m = v2;
-    if (v3 > m) m = v3;
+  for (; j + U <= n; j += U) {
+    float v[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) v[u] = Sg[(j + u) * st];
+#pragma unroll
+    for (int u = 0; u < U; u++)
+      if (v[u] > m) m = v[u];
   }
   for (; j < n; j++) {
-    const float v = Sg[(size_t)j * nR];
+    const float v = Sg[j * st];
     if (v > m) m = v;
   }
   float sum = 0.0f;
   j = 0;
-  for (; j + 4 <= n; j += 4) {
-    float e[4];
+  if (j + U <= n) {
+    float v[U];
 #pragma unroll
-    for (int u = 0; u < 4; u++) e[u] = exp_cr(__fsub_rn(Sg[(size_t)(j + u) * nR], m));
+    for (int u = 0; u < U; u++) v[u] = Sg[(j + u) * st];
+    for (; j + U <= n; j += U) {
+      float e[U];
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
-      Sg[(size_t)(j + u) * nR] = e[u];
-      sum = fadd(sum, e[u]);
+      for (int u = 0; u < U; u++) e[u] = exp_cr(__fsub_rn(v[u], m));
+      if (j + 2 * U <= n) {  // the next group's scores, loaded while this group's sum runs
+#pragma unroll
+        for (int u = 0; u < U; u++) v[u] = Sg[(j + U + u) * st];
+      }
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        Sg[(j + u) * st] = e[u];
+        sum = fadd(sum, e[u]);
+      }
     }
   }
   for (; j < n; j++) {
-    const float e = exp_cr(__fsub_rn(Sg[(size_t)j * nR], m));
-    Sg[(size_t)j * nR] = e;
+    const float e = exp_cr(__fsub_rn(Sg[j * st], m));
+    Sg[j * st] = e;
     sum = fadd(sum, e);
   }
   inv[(size_t)g * nR + R] = __fdiv_rn(1.0f, sum);
 }
 
 // O[t][h][dd] = sum_j (e_j * inv) * v_j[dd], sequential in j (model.rs:426-432; 573-584 for a
-// diffusion block, whose prefix-then-block order is position order). Tile: 32 R x HD of kv head
-// g = blockIdx.y.
+// diffusion block, whose prefix-then-block order is position order), kv head g = blockIdx.y.
+// CTA: 64 rows x HD dims; warp w owns rows 8w..8w+7, lane owns dims HD/32 * lane + 0..HD/32-1, so a
+// thread runs 8 x HD/32 chains. Tiles of 32 positions are staged in shared memory, double
+// buffered and loaded into registers a tile ahead: p = e * inv (ops.rs:124-126) formed once per
+// (row, position), and 0 past the row's length -- adding fmul(0, v) = +-0 leaves a chain exactly
+// unchanged (a chain that starts at +0 never holds -0), so the chains need no per-position test.
+constexpr int KP_PR = 64;   // rows per CTA
+constexpr int KP_PJ = 32;   // positions per tile
+template <int HD>
+constexpr size_t kp_pv_smem() { return (size_t)2 * KP_PJ * (KP_PR + HD) * sizeof(float); }
+
 template <int HD>
 __global__ void __launch_bounds__(256) kp_pv(const float* S, long long s_head, const float* inv, int nR, int rep,
                                              int base, int t0, int nfix, const int32_t* bt, const float* v_pool,
                                              long long page_stride, float* o, int qd) {
-  constexpr int PD = HD / 32;  // dims per thread (threads: 8 R-groups x 32 dims)
-  __shared__ float ps[32][33];
-  __shared__ float vs[32][HD];
-  const int kvh = blockIdx.y;
-  const float* Sg = S + (size_t)kvh * s_head;
-  const float* ig = inv + (size_t)kvh * nR;
-  const int R0 = blockIdx.x * 32;
-  const int rg = threadIdx.x >> 5, dl = threadIdx.x & 31;  // rows rg*4..rg*4+3, dims dl + 32*k
-  float acc[4][PD];
-#pragma unroll
-  for (int i = 0; i < 4; i++)
-#pragma unroll
-    for (int k = 0; k < PD; k++) acc[i][k] = 0.0f;
-  int lim[4];
-  float iv[4];
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    int R = R0 + rg * 4 + i;
-    lim[i] = R < nR ? (nfix > 0 ? nfix : base + t0 + R / rep + 1) : 0;
-    iv[i] = R < nR ? ig[R] : 0.0f;
-  }
-  int Rlast = min(R0 + 31, nR - 1);
+  constexpr int DPT = HD / 32;                 // dims per thread
+  constexpr int VQ = KP_PJ * HD / 4 / 256;     // float4 pieces of a V tile per thread
+  constexpr int SQ = KP_PJ * KP_PR / 256;      // probabilities of a tile per thread
+  extern __shared__ __align__(16) float kp_pv_sm[];
+  float* ps = kp_pv_sm;                        // [2][KP_PJ][KP_PR]
+  float* vs = kp_pv_sm + 2 * KP_PJ * KP_PR;    // [2][KP_PJ][HD]
+  const int g = blockIdx.y;
+  const float* Sg = S + (size_t)g * s_head;
+  const float* ig = inv + (size_t)g * nR;
+  const int R0 = blockIdx.x * KP_PR;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int Rlast = min(R0 + KP_PR - 1, nR - 1);
   const int nmax = nfix > 0 ? nfix : base + t0 + Rlast / rep + 1;
-  for (int j0 = 0; j0 < nmax; j0 += 32) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < 32 * 32; i += 256) {
-      int jj = i >> 5, rr = i & 31;
-      int R = R0 + rr, j = j0 + jj;
-      ps[rr][jj] = (R < nR && j < nmax) ? Sg[(size_t)j * nR + R] : 0.0f;
-    }
-    for (int i = threadIdx.x; i < 32 * HD; i += 256) {
-      int jj = i / HD, dd = i - jj * HD;
-      int j = j0 + jj;
-      vs[jj][dd] = j < nmax ? v_pool[(long long)bt[j / PAGE] * page_stride + ((long long)kvh * PAGE + (j % PAGE)) * HD + dd]
-                            : 0.0f;
-    }
-    __syncthreads();
-    const int jn = min(32, nmax - j0);
-    for (int jj = 0; jj < jn; jj++) {
-      const int j = j0 + jj;
+  // staging role: one row (tid % 64) of the probabilities
+  const int sr = tid & (KP_PR - 1), sR = R0 + sr;
+  const int slim = sR < nR ? (nfix > 0 ? nfix : base + t0 + sR / rep + 1) : 0;
+  const float siv = sR < nR ? ig[sR] : 0.0f;
+  float pr[SQ];
+  float4 vr[VQ];
+  auto load_tile = [&](int j0) {
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        if (j < lim[i]) {
-          float p = fmul(ps[rg * 4 + i][jj], iv[i]);
+    for (int q = 0; q < SQ; q++) {
+      const int j = j0 + ((tid + 256 * q) >> 6);
+      pr[q] = j < slim ? fmul(Sg[(size_t)j * nR + sR], siv) : 0.0f;
+    }
 #pragma unroll
-          for (int k = 0; k < PD; k++) acc[i][k] = fadd(acc[i][k], fmul(p, vs[jj][dl + 32 * k]));
-        }
+    for (int q = 0; q < VQ; q++) {
+      const int idx = tid + 256 * q, jj = idx / (HD / 4), c4 = idx - jj * (HD / 4), j = j0 + jj;
+      vr[q] = j < nmax ? *reinterpret_cast<const float4*>(
+                             v_pool + (long long)bt[j / PAGE] * page_stride + ((long long)g * PAGE + (j % PAGE)) * HD +
+                             c4 * 4)
+                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+  };
+  auto store_tile = [&](int b) {
+    float* pb = ps + b * KP_PJ * KP_PR;
+    float* vb = vs + b * KP_PJ * HD;
+#pragma unroll
+    for (int q = 0; q < SQ; q++) pb[((tid + 256 * q) >> 6) * KP_PR + sr] = pr[q];
+#pragma unroll
+    for (int q = 0; q < VQ; q++) reinterpret_cast<float4*>(vb)[tid + 256 * q] = vr[q];
+  };
+  float acc[8][DPT];
+#pragma unroll
+  for (int i = 0; i < 8; i++)
+#pragma unroll
+    for (int k = 0; k < DPT; k++) acc[i][k] = 0.0f;
+  const int ntile = (nmax + KP_PJ - 1) / KP_PJ;
+  load_tile(0);
+  for (int t = 0; t < ntile; t++) {
+    const int b = t & 1;
+    store_tile(b);  // buffer b was last read two tiles ago, before the previous barrier
+    if (t + 1 < ntile) load_tile((t + 1) * KP_PJ);
+    __syncthreads();
+    const float* pb = ps + b * KP_PJ * KP_PR + warp * 8;
+    const float* vb = vs + b * KP_PJ * HD + lane * DPT;
+#pragma unroll 4
+    for (int jj = 0; jj < KP_PJ; jj++) {
+      const float4 p0 = *reinterpret_cast<const float4*>(pb + jj * KP_PR);
+      const float4 p1 = *reinterpret_cast<const float4*>(pb + jj * KP_PR + 4);
+      const float p[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+      float v[DPT];
+      if (DPT == 4) {
+        const float4 t4 = *reinterpret_cast<const float4*>(vb + jj * HD);
+        v[0] = t4.x; v[1] = t4.y; v[2 % DPT] = t4.z; v[3 % DPT] = t4.w;
+      } else {
+        const float2 t2 = *reinterpret_cast<const float2*>(vb + jj * HD);
+        v[0] = t2.x; v[1 % DPT] = t2.y;
       }
+#pragma unroll
+      for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int k = 0; k < DPT; k++) acc[i][k] = fadd(acc[i][k], fmul(p[i], v[k]));
     }
   }
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
-    int R = R0 + rg * 4 + i;
+  for (int i = 0; i < 8; i++) {
+    const int R = R0 + warp * 8 + i;
     if (R >= nR) continue;
-    int tl = R / rep, hr = R - tl * rep;
-    float* dst = o + (size_t)(t0 + tl) * qd + (size_t)(kvh * rep + hr) * HD;
+    const int tl = R / rep, hr = R - tl * rep;
+    float* dst = o + (size_t)(t0 + tl) * qd + (size_t)(g * rep + hr) * HD + lane * DPT;
 #pragma unroll
-    for (int k = 0; k < PD; k++) dst[dl + 32 * k] = acc[i][k];
+    for (int k = 0; k < DPT; k++) dst[k] = acc[i][k];
   }
 }
 
@@ -650,6 +695,8 @@ void launch_kp_attention(const float* q, int qd, int t0, int tq, int base, int n
                          (int)kp_scores_smem<128>());
     cudaFuncSetAttribute((const void*)kp_scores<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)kp_scores_smem<64>());
+    cudaFuncSetAttribute((const void*)kp_pv<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kp_pv_smem<128>());
+    cudaFuncSetAttribute((const void*)kp_pv<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kp_pv_smem<64>());
     smem_set[dev] = true;
   }
   const int rep = nh / nkv;
@@ -664,11 +711,13 @@ void launch_kp_attention(const float* q, int qd, int t0, int tq, int base, int n
     kp_scores<64><<<gs, 256, kp_scores_smem<64>(), st>>>(q, qd, t0, tq, base, rep, bt, k_pool, page_stride, S,
                                                          s_head, nR, nfix);
   kp_softmax_rows<<<dim3((nR + 31) / 32, nkv), 32, 0, st>>>(S, s_head, nR, rep, base, t0, nfix, inv);
-  const dim3 gp((nR + 31) / 32, nkv);
+  const dim3 gp((nR + KP_PR - 1) / KP_PR, nkv);
   if (hd == 128)
-    kp_pv<128><<<gp, 256, 0, st>>>(S, s_head, inv, nR, rep, base, t0, nfix, bt, v_pool, page_stride, o, qd);
+    kp_pv<128><<<gp, 256, kp_pv_smem<128>(), st>>>(S, s_head, inv, nR, rep, base, t0, nfix, bt, v_pool, page_stride,
+                                                   o, qd);
   else
-    kp_pv<64><<<gp, 256, 0, st>>>(S, s_head, inv, nR, rep, base, t0, nfix, bt, v_pool, page_stride, o, qd);
+    kp_pv<64><<<gp, 256, kp_pv_smem<64>(), st>>>(S, s_head, inv, nR, rep, base, t0, nfix, bt, v_pool, page_stride, o,
+                                                 qd);
 }
 void launch_kp_route(const float* h, int tn, int d, const float* router, const float* bias, int ne, int k, int gsig,
                      int wnorm, float wscale, int32_t* sel, float* selw, int32_t* ecount, int32_t* elist, int list_cap,
