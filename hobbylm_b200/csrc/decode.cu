@@ -681,6 +681,8 @@ __device__ __forceinline__ bool attn_pos_ok(const AttnArgs& A, int pos) {
 // the token's k heads, appended with its v heads to their page slot (model.rs:199-210). One CTA
 // per token, one warp per head (q heads first, then kv heads). Also resets the token's score
 // maxima (read by k_attn_softmax two kernels later).
+constexpr int ATT_MAX_T = 256;  // tokens of one attention call (engine batches and hg_op_kv_attn)
+
 template <int HD>
 __global__ void k_qk_prep(AttnArgs A) {
   extern __shared__ __align__(16) float prep_s[];  // one HD-float scratch per warp
@@ -689,6 +691,22 @@ __global__ void k_qk_prep(AttnArgs A) {
   // kernels ago), the position, the gains, the RoPE rows and the page slot are handled before the
   // wait
   for (int h = threadIdx.x; h < A.nh; h += blockDim.x) A.mkey[(size_t)t * A.nh + h] = 0u;
+  if (A.order && blockIdx.x == 0) {
+    // the tokens by decreasing position (ties by index), a permutation: the value sums and the
+    // softmax hand their longest chains out first, so no SM ends up holding several of them
+    __shared__ int pos_sh[ATT_MAX_T];
+    for (int u = threadIdx.x; u < A.T; u += blockDim.x) pos_sh[u] = A.pos[u];
+    __syncthreads();
+    for (int u = threadIdx.x; u < A.T; u += blockDim.x) {
+      const int pu = pos_sh[u];
+      int r = 0;
+      for (int v = 0; v < A.T; v++) {
+        const int pv = pos_sh[v];
+        r += (pv > pu) || (pv == pu && v < u);
+      }
+      A.order[r] = u;
+    }
+  }
   const int pos = A.pos[t];
   const bool ok = attn_pos_ok(A, pos);
   const bool is_q = warp < A.nh, is_k = !is_q && warp < A.nh + A.nkv;
@@ -977,7 +995,8 @@ __global__ void __launch_bounds__(SMX_THREADS) k_attn_softmax(AttnArgs A) {
   constexpr int PER = (SMX_ECH + SMX_THREADS - 33) / (SMX_THREADS - 32);  // exps per thread (warps 1..)
   __shared__ __align__(16) float ebuf[2][SMX_ECH];
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int t = blockIdx.x / A.nh, h = blockIdx.x - t * A.nh;
+  const int rk = blockIdx.x / A.nh, h = blockIdx.x - rk * A.nh;
+  const int t = A.order ? A.order[rk] : rk;  // written two kernels ago
   pdl_wait();
   pdl_trigger();
   const int pos = A.pos[t];
@@ -1080,7 +1099,8 @@ __global__ void __launch_bounds__(HD) k_attn_pv(AttnArgs A) {
   extern __shared__ __align__(16) float pv_smem[];
   __shared__ __align__(16) float p_s[2][PV_STAGE][4];
   const int tid = threadIdx.x;
-  const int t = blockIdx.x / A.nkv, kvh = blockIdx.x - t * A.nkv, h0 = kvh * REP;
+  const int rk = blockIdx.x / A.nkv, kvh = blockIdx.x - rk * A.nkv, h0 = kvh * REP;
+  const int t = A.order ? A.order[rk] : rk;  // longest first; written three kernels ago
   const int pos = A.pos[t];  // positions and page ids are older than the previous kernel
   if (!attn_pos_ok(A, pos)) {  // flagged by k_qk_prep
     pdl_wait();
@@ -1204,7 +1224,8 @@ __global__ void __launch_bounds__(32 * REP) k_attn_pv_small(AttnArgs A) {
   __shared__ __align__(16) float p_s[REP][2][PVS_STAGE];  // per warp (head), double-buffered
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int slice = blockIdx.x % DS, tk = blockIdx.x / DS;
-  const int t = tk / A.nkv, kvh = tk - t * A.nkv, h = kvh * REP + w, d = slice * 32 + lane;
+  const int rk = tk / A.nkv, kvh = tk - rk * A.nkv, h = kvh * REP + w, d = slice * 32 + lane;
+  const int t = A.order ? A.order[rk] : rk;  // longest first; written three kernels ago
   const int pos = A.pos[t];
   if (!attn_pos_ok(A, pos)) {  // flagged by k_qk_prep
     pdl_wait();
@@ -1356,10 +1377,8 @@ template <int EPI>
 static void launch_mv_tokens_t(const Dims& D, const DecodeBufs& B, const Q8M& W, const int8_t* aq, const float* as,
                                float* out, int ostride, cudaStream_t st) {
   int nb = W.cols >> 5;
-  if (tc_usable(W, B.T)) {  // many tokens: the partials come from the tensor cores (tc.cu)
-    launch_mv_tc(D, B, W, aq, as, out, ostride, EPI, st);
-    return;
-  }
+  // many tokens: the partials come from the tensor cores (tc.cu)
+  if (tc_usable(W, B.T) && launch_mv_tc(D, B, W, aq, as, out, ostride, EPI, st)) return;
   if (B.T == 1) {
     constexpr int ROWS = 8, TT = 1;
     dim3 grid((W.rows + ROWS - 1) / ROWS);
@@ -1420,10 +1439,7 @@ void launch_moe_combine(const Dims& D, const DecodeBufs& B, float* y_out, cudaSt
 }
 
 void launch_ffn(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaStream_t st) {
-  if (ffn_tc_usable(D, B, L)) {  // many tokens: the tensor-core FFN (tc.cu)
-    launch_ffn_tc(D, B, L, st);
-    return;
-  }
+  if (ffn_tc_usable(D, B, L) && launch_ffn_tc(D, B, L, st)) return;  // many tokens: the tensor-core FFN (tc.cu)
   const int nrouted = L.moe ? (D.ne < B.T * D.k ? D.ne : B.T * D.k) : 0;
   launch_ffn_ex(D, B, L, true, nrouted, st);
 }

@@ -19,6 +19,9 @@
 
 namespace hg {
 
+// rows of one bidirectional pass (hg_run_block; the uncached diffusion canvas)
+constexpr int PF_BLOCK_MAX = 1024;
+
 static thread_local std::string g_last_error;
 void set_last_error(const std::string& m) { g_last_error = m; }
 
@@ -103,11 +106,12 @@ struct hg_engine {
   int pf_rows = 0;
   struct Pf {
     float *x, *h, *qkv, *q, *o, *g, *u, *act, *y, *selw, *S, *inv;
+    uint32_t* mkey;  // row maxima of the scores (order-preserving keys)
     int8_t *qa, *qact;
     float *sa, *sact;
     int32_t *ids, *sel, *ecount, *elist, *a_idx, *o_idx, *gm, *go, *gc;
   } pf{};
-  int pf_tq = 1024;
+  int pf_tq = 4096;
   float* blk_logits = nullptr;  // [blk_logits_rows][vocab] logits of diffusion block rows
   int blk_logits_rows = 0;
   std::vector<int32_t> last_sel;  // [n_layers][max_batch][k] from the last decode step
@@ -239,6 +243,7 @@ void alloc_work(hg_engine* e) {
   B.s_stride = ((long long)c.context_length + 15) & ~15LL;
   B.S = a.take<float>((size_t)T * c.n_heads * B.s_stride);
   B.mkey = a.take<uint32_t>((size_t)T * c.n_heads);
+  B.order = a.take<int32_t>((size_t)T);
   B.rinv = a.take<float>((size_t)T * c.n_heads);
   B.qn = a.take<float>((size_t)T * D.qd);
   B.logits = a.take<float>((size_t)T * c.vocab_size);
@@ -258,6 +263,7 @@ void alloc_work(hg_engine* e) {
   P.selw = a.take<float>((size_t)PF * k);
   P.S = a.take<float>(s_elems);
   P.inv = a.take<float>((size_t)e->pf_tq * rep * c.n_kv_heads);
+  P.mkey = a.take<uint32_t>((size_t)e->pf_tq * rep * c.n_kv_heads);
   P.qa = a.take<int8_t>((size_t)PF * std::max(d, qd));
   P.qact = a.take<int8_t>(pf_act);
   P.sa = a.take<float>((size_t)PF * std::max(ss_d, ss_q));
@@ -389,7 +395,7 @@ void load_engine(hg_engine* e, const char* path, const hg_engine_opts& o) {
   HG_CUDA(cudaMalloc((void**)&e->d_bt, (size_t)e->max_rows * e->bt_stride * 4));
   HG_CUDA(cudaMemset(e->d_bt, 0, (size_t)e->max_rows * e->bt_stride * 4));
   for (int r = e->max_rows - 1; r >= 0; r--) e->free_rows.push_back(r);
-  e->pf_rows = 1024;
+  e->pf_rows = 4096;  // prefill rows per chunk: a chunk's attention launches hold rows x heads chains
   alloc_work(e);
   HG_CUDA(cudaMallocHost((void**)&e->h_meta, 3 * e->max_batch * 4));
   HG_CUDA(cudaMallocHost((void**)&e->h_amax, e->max_batch * 8));
@@ -463,6 +469,7 @@ AttnArgs make_attn_args(hg_engine* e, const DecodeBufs& B, int l) {
   A.S = B.S;
   A.s_stride = B.s_stride;
   A.mkey = B.mkey;
+  A.order = B.order;
   A.rinv = B.rinv;
   A.qn = B.qn;
   A.out = nullptr;
@@ -694,7 +701,7 @@ void prefill_chunk(hg_engine* e, hg_seq* s, const uint32_t* ids, const float* em
       int tq = std::min(e->pf_tq, tn - t0);
       launch_kp_attention(P.q, D.qd, t0, tq, base, bidir ? base + tn : 0, c.n_heads, c.n_kv_heads, c.head_dim, bt, kb,
                           vb, e->page_stride,
-                          P.S, P.inv, P.o, st);
+                          P.S, P.inv, P.mkey, P.o, st);
     }
     launch_kp_quant_rows(P.o, tn, D.qd, P.qa, P.sa, st);
     launch_kp_matmul(mm_args(Ld.wo, P.qa, P.sa, tn, P.x, d, 1), tn, 1, st);
@@ -798,7 +805,7 @@ void prefill(hg_engine* e, hg_seq* s, const uint32_t* ids, const float* embeds, 
 // [n_logits][vocab] of the last n_logits rows through output.matmul (model.rs:505-508).
 void run_block(hg_engine* e, hg_seq* s, const uint32_t* ids, int n, int n_logits, bool commit, float* logits) {
   const hg_config& c = e->cfg;
-  if (n <= 0 || n > e->pf_rows) throw Error(HG_ERR_INVALID, "block rows out of range (1..1024 per bidirectional pass)");
+  if (n <= 0 || n > PF_BLOCK_MAX) throw Error(HG_ERR_INVALID, "block rows out of range (1..1024 per bidirectional pass)");
   if (n_logits < 0 || n_logits > n) throw Error(HG_ERR_INVALID, "n_logits out of range");
   for (int i = 0; i < n; i++)
     if ((int64_t)ids[i] >= c.vocab_size) throw Error(HG_ERR_TOKEN, "token id out of range");
@@ -1146,7 +1153,8 @@ size_t kv_s_stride(const hg_kv_attn_args* a) { return ((size_t)a->max_pos + 15) 
 size_t kv_scratch_bytes(const hg_kv_attn_args* a) {
   return align256((size_t)a->n_seqs * a->n_heads * kv_s_stride(a) * 4) +
          align256((size_t)a->n_seqs * a->n_heads * 4) +
-         align256((size_t)a->n_seqs * a->n_heads * 4) + align256((size_t)a->n_seqs * a->n_heads * a->head_dim * 4) + 256;
+         align256((size_t)a->n_seqs * a->n_heads * 4) + align256((size_t)a->n_seqs * a->n_heads * a->head_dim * 4) +
+         align256((size_t)a->n_seqs * 4) + 256;
 }
 
 }  // namespace
@@ -1585,6 +1593,8 @@ int hg_op_kv_attn(const hg_kv_attn_args* a, void* scratch, void* stream) {
     A.mkey = reinterpret_cast<uint32_t*>(base + s_bytes);
     A.rinv = reinterpret_cast<float*>(base + s_bytes + align256((size_t)a->n_seqs * a->n_heads * 4));
     A.qn = reinterpret_cast<float*>(reinterpret_cast<char*>(A.rinv) + align256((size_t)a->n_seqs * a->n_heads * 4));
+    A.order = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(A.qn) +
+                                         align256((size_t)a->n_seqs * a->n_heads * a->head_dim * 4));
     A.err = nullptr;
     A.out = a->out;
     A.qo = nullptr;

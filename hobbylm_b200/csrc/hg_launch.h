@@ -33,12 +33,17 @@ void launch_feedback(const DecodeBufs& B, int32_t* tok, int32_t* pos, int32_t* g
 constexpr int TC_MIN_T = 32;
 cudaError_t prepare_tc();
 bool tc_usable(const Q8M& W, int T);
-void launch_mv_tc(const Dims& D, const DecodeBufs& B, const Q8M& W, const int8_t* aq, const float* as, float* out,
+// false (nothing launched) when the weights cannot be described by a tensor map
+bool launch_mv_tc(const Dims& D, const DecodeBufs& B, const Q8M& W, const int8_t* aq, const float* as, float* out,
                   int ostride, int epi, cudaStream_t st);
 // the FFN of a layer on the tensor cores (gate, up, SwiGLU + quantization, down); needs B.ubuf,
 // B.qact and B.sact
 bool ffn_tc_usable(const Dims& D, const DecodeBufs& B, const LayerDev& L);
-void launch_ffn_tc(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaStream_t st);
+bool launch_ffn_tc(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaStream_t st);
+// the prefill-order matmul (MmArgs) on the tensor cores, for at least TC_MIN_T activation rows
+bool kp_tc_usable(const MmArgs& a, int nrows_max, int groups);
+// count: matrices of the stack a.W the launch may index (tensor-map extent)
+bool launch_kp_tc(const MmArgs& a, int nrows_max, int groups, int count, cudaStream_t st);
 
 // prefill.cu
 void launch_kp_norm(float* in, const float* add, int rows, int d, const float* w, float eps, float* h_out, int8_t* q,
@@ -51,7 +56,7 @@ void launch_kp_qk_rope_append(const float* qkv, int rows, int base, int nh, int 
 // nfix = 0: causal rows (query t sees keys 0..base+t); nfix > 0: every row sees keys 0..nfix-1.
 void launch_kp_attention(const float* q, int qd, int t0, int tq, int base, int nfix, int nh, int nkv, int hd,
                          const int32_t* bt, const float* k_pool, const float* v_pool, long long page_stride, float* S,
-                         float* inv, float* o, cudaStream_t st);
+                         float* inv, uint32_t* mkey, float* o, cudaStream_t st);
 void launch_kp_route(const float* h, int tn, int d, const float* router, const float* bias, int ne, int k, int gsig,
                      int wnorm, float wscale, int32_t* sel, float* selw, int32_t* ecount, int32_t* elist, int list_cap,
                      cudaStream_t st);

@@ -79,6 +79,7 @@ struct DecodeBufs {
   float* rinv;             // [T][nh] 1 / softmax denominator
   float* qn;               // [T][nh][hd] QK-normed, roped q
   uint32_t* mkey;          // [T][nh] running maximum of the attention scores (order-preserving key)
+  int32_t* order;          // [T] tokens by decreasing position (attention work order)
   float* logits;           // [T][vocab] or null
   unsigned long long* amax;// [T]
   int32_t* dbg_sel;        // [L][T][k] routing capture
@@ -106,6 +107,8 @@ struct AttnArgs {
   float* rinv;     // [T][nh] 1 / softmax denominator
   float* qn;       // [T][nh][hd] QK-normed, roped q (k_qk_prep)
   uint32_t* mkey;  // [T][nh] maximum score per (token, head) as an order-preserving key (f2key)
+  int32_t* order;  // [T] the tokens by decreasing position (k_qk_prep), or null: value sums and
+                   // softmax take the longest sequences first
   float* out;      // [T][nh*hd] or null
   int8_t* qo;      // [T][nh*hd] or null
   float* so;       // [T][ss(nh*hd/32)]
@@ -129,6 +132,7 @@ struct MmArgs {
   const int32_t* grp_mat;    // [groups] stacked matrix index, -1 = skip
   const int32_t* grp_off;    // [groups] first entry
   const int32_t* grp_cnt;    // [groups] entry count
+  int32_t* err;              // device error word (tensor-core path: HG_ERR_TIMEOUT), or null
 };
 
 }  // namespace hg

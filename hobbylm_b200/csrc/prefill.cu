@@ -10,7 +10,7 @@
 //     (model.rs:705-746).
 // The prompt may be processed in chunks: every per-row step is row-local and attention reads the
 // cache, so chunking does not change any result.
-#include "hg_model.cuh"
+#include "hg_launch.h"
 
 namespace hg {
 
@@ -252,8 +252,9 @@ template <> struct KpVec<2> {
 template <int HD>
 __global__ void __launch_bounds__(256) kp_scores(const float* q, int qd, int t0, int tq, int base, int rep,
                                                  const int32_t* bt, const float* k_pool, long long page_stride,
-                                                 float* S, long long s_head, int nR, int nfix) {
+                                                 float* S, long long s_head, int nR, int nfix, uint32_t* mkey) {
   constexpr int NI = HD / 32, RS = kp_row_stride<HD>();
+  __shared__ uint32_t mred[KP_SR];  // this CTA's maxima of its rows (order-preserving keys)
   extern __shared__ __align__(16) float kp_sm[];
   float* qs = kp_sm;              // [KP_SR][RS]
   float* ks = kp_sm + KP_SR * RS; // [KP_SJ][RS]
@@ -284,6 +285,8 @@ __global__ void __launch_bounds__(256) kp_scores(const float* q, int qd, int t0,
   }
   const float* qa0 = qs + lane * RS;
   const float* qa1 = qs + (lane + 32) * RS;
+  if (tid < KP_SR) mred[tid] = 0u;  // ordered before use by the first tile's barrier
+  float mx[2] = {-INFINITY, -INFINITY};
   for (int kt = 0; kt < KP_KTILES; kt++) {
     const int j0 = jt0 + kt * KP_SJ;
     if (j0 >= lim_hi) break;  // CTA-uniform
@@ -344,40 +347,38 @@ __global__ void __launch_bounds__(256) kp_scores(const float* q, int qd, int t0,
 #pragma unroll
       for (int p = 0; p < 4; p++) {
         const int j = j0 + warp * 4 + p;
-        if (j < lim[r]) Sg[(size_t)j * nR + R] = fmul(A[r][p], scale);
+        if (j < lim[r]) {
+          const float sv = fmul(A[r][p], scale);
+          Sg[(size_t)j * nR + R] = sv;
+          mx[r] = fmaxf(mx[r], sv);
+        }
       }
     }
   }
+  // row maxima for the softmax (any order gives the same maximum): the CTA's, then global
+#pragma unroll
+  for (int r = 0; r < 2; r++)
+    if (mx[r] > -INFINITY) atomicMax(&mred[lane + 32 * r], f2key(mx[r]));
+  __syncthreads();
+  if (tid < KP_SR && R0 + tid < nR && mred[tid]) atomicMax(&mkey[(size_t)g * nR + R0 + tid], mred[tid]);
 }
 
-// Softmax of score rows (ops.rs:112-128), all kv heads (blockIdx.y = g). One thread per row:
-// the maximum, then e = exp(s - max) written back in place and summed in position order in a
-// register chain (the reference's sequential sum); inv[g * nR + R] = 1 / sum. Row lengths as
-// kp_scores. Lanes are consecutive rows, so every load and store is coalesced.
+// Softmax of score rows (ops.rs:112-128), all kv heads (blockIdx.y = g). One thread per row: with
+// the row maximum that kp_scores left in mkey, e = exp(s - max) is written back in place and
+// summed in position order in a register chain (the reference's sequential sum);
+// inv[g * nR + R] = 1 / sum. Row lengths as kp_scores. Lanes are consecutive rows, so every load
+// and store is coalesced.
 __global__ void __launch_bounds__(32) kp_softmax_rows(float* S, long long s_head, int nR, int rep, int base, int t0,
-                                                      int nfix, float* inv) {
-  constexpr int U = 8;  // positions in flight per thread (few rows per launch: parallelism per thread)
+                                                      int nfix, const uint32_t* mkey, float* inv) {
+  constexpr int U = 8;  // positions in flight per thread
   const int g = blockIdx.y, R = blockIdx.x * 32 + threadIdx.x;
   if (R >= nR) return;
   float* Sg = S + (size_t)g * s_head + R;
   const size_t st = (size_t)nR;
   const int n = nfix > 0 ? nfix : base + t0 + R / rep + 1;
-  float m = -INFINITY;
-  int j = 0;
-  for (; j + U <= n; j += U) {
-    float v[U];
-#pragma unroll
-    for (int u = 0; u < U; u++) v[u] = Sg[(j + u) * st];
-#pragma unroll
-    for (int u = 0; u < U; u++)
-      if (v[u] > m) m = v[u];
-  }
-  for (; j < n; j++) {
-    const float v = Sg[j * st];
-    if (v > m) m = v;
-  }
+  const float m = key2f(mkey[(size_t)g * nR + R]);  // the row's maximum score, from kp_scores
   float sum = 0.0f;
-  j = 0;
+  int j = 0;
   if (j + U <= n) {
     float v[U];
 #pragma unroll
@@ -673,6 +674,10 @@ void launch_kp_norm(float* in, const float* add, int rows, int d, const float* w
   kp_norm_exact<<<(rows + 3) / 4, 128, 4 * d * sizeof(float), st>>>(in, add, rows, d, w, eps, h_out, q, s);
 }
 void launch_kp_matmul(const MmArgs& a, int nrows_max, int groups, cudaStream_t st) {
+  // block sums from the tensor cores (tc.cu); a grouped launch indexes matrices 0..groups-1
+  if (kp_tc_usable(a, nrows_max, groups) &&
+      launch_kp_tc(a, nrows_max, groups, a.grp_mat ? groups : a.mat + 1, st))
+    return;
   dim3 grid((a.W.rows + 63) / 64, (nrows_max + 63) / 64, groups);
   kp_matmul<<<grid, 256, 0, st>>>(a);
 }
@@ -686,7 +691,7 @@ void launch_kp_qk_rope_append(const float* qkv, int rows, int base, int nh, int 
 }
 void launch_kp_attention(const float* q, int qd, int t0, int tq, int base, int nfix, int nh, int nkv, int hd,
                          const int32_t* bt, const float* k_pool, const float* v_pool, long long page_stride, float* S,
-                         float* inv, float* o, cudaStream_t st) {
+                         float* inv, uint32_t* mkey, float* o, cudaStream_t st) {
   static bool smem_set[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -704,13 +709,14 @@ void launch_kp_attention(const float* q, int qd, int t0, int tq, int base, int n
   const int nmax = nfix > 0 ? nfix : base + t0 + tq;
   const long long s_head = (long long)nmax * nR;  // scores of one kv head
   const dim3 gs((nR + KP_SR - 1) / KP_SR, (nmax + KP_KTILES * KP_SJ - 1) / (KP_KTILES * KP_SJ), nkv);
+  cudaMemsetAsync(mkey, 0, (size_t)nkv * nR * sizeof(uint32_t), st);  // key 0 sorts below every score
   if (hd == 128)
     kp_scores<128><<<gs, 256, kp_scores_smem<128>(), st>>>(q, qd, t0, tq, base, rep, bt, k_pool, page_stride, S,
-                                                           s_head, nR, nfix);
+                                                           s_head, nR, nfix, mkey);
   else
     kp_scores<64><<<gs, 256, kp_scores_smem<64>(), st>>>(q, qd, t0, tq, base, rep, bt, k_pool, page_stride, S,
-                                                         s_head, nR, nfix);
-  kp_softmax_rows<<<dim3((nR + 31) / 32, nkv), 32, 0, st>>>(S, s_head, nR, rep, base, t0, nfix, inv);
+                                                         s_head, nR, nfix, mkey);
+  kp_softmax_rows<<<dim3((nR + 31) / 32, nkv), 32, 0, st>>>(S, s_head, nR, rep, base, t0, nfix, mkey, inv);
   const dim3 gp((nR + KP_PR - 1) / KP_PR, nkv);
   if (hd == 128)
     kp_pv<128><<<gp, 256, kp_pv_smem<128>(), st>>>(S, s_head, inv, nR, rep, base, t0, nfix, bt, v_pool, page_stride,

@@ -30,6 +30,8 @@
 // HG_ERR_TIMEOUT in the step's error word, stops issuing, waits (bounded) for its last MMAs and
 // copies, and still frees its tensor memory. No TMA and no multicast are used; all copies read
 // this GPU's own memory.
+#include <cuda.h>  // CUtensorMap (the encoder is fetched through the runtime; no driver library link)
+
 #include <algorithm>
 #include <cstdint>
 
@@ -42,16 +44,21 @@ constexpr int TC_N = TC_TOK * 8;      // MMA N
 constexpr int TC_M = 128;             // rows per CTA (MMA M)
 constexpr int TC_BUFCOLS = 4 * TC_N;  // tensor-memory columns of one step: 4 lane-pair MMAs
 constexpr int TC_COLS = 2 * TC_BUFCOLS;  // two step buffers: all 512 columns of the SM
-constexpr int TC_THREADS = 512;       // 16 warps: TMEM lane quadrant w % 4, entry pair w / 4
-constexpr int TC_WSLOTS = 6;          // weight-chunk ring (16 KB each)
-constexpr int TC_WAHEAD = 4;          // weight chunks in flight ahead of the step being reduced
-constexpr int TC_WCHUNK = TC_M * 128; // bytes per weight chunk
-constexpr int TC_BCHUNK = 4 * TC_TOK * 256;  // bytes per expanded activation chunk (4 lane pairs)
-constexpr int TC_TAIL_B = 3 * TC_TOK * 256;  // expanded tail blocks: up to 3 x 8 entries x 8 lanes x 32 B
+// roles: 16 chain warps (TMEM lane quadrant w % 4, entry pair w / 4), 2 copy warps, 1 MMA warp
+constexpr int TC_EPI_WARPS = 16;
+constexpr int TC_PROD_WARPS = 2;
+constexpr int TC_MMA_WARP = TC_EPI_WARPS + TC_PROD_WARPS;
+constexpr int TC_THREADS = 32 * (TC_MMA_WARP + 1);
+constexpr int TC_PROD0 = 32 * TC_EPI_WARPS;   // first copy thread
+constexpr int TC_NPROD = 32 * TC_PROD_WARPS;  // copy threads
+constexpr int TC_SLOTS = 6;                   // ring slots, each one step's operands
+constexpr int TC_WCHUNK = TC_M * 128;         // bytes of a step's weights
+constexpr int TC_BCHUNK = 4 * TC_TOK * 256;   // bytes of an expanded activation chunk (4 lane pairs)
+constexpr int TC_TAIL_B = 3 * TC_TOK * 256;   // expanded tail blocks: up to 3 x 8 entries x 8 lanes x 32 B
+constexpr int TC_SLOT_BYTES = TC_WCHUNK + TC_BCHUNK + TC_TAIL_B;  // a multiple of 1024
 constexpr long long TC_SPIN_LIMIT = 1ll << 26;
-// + alignment slack, the weight ring (a tail step's A tiles use a ring slot), two expanded
-// activation chunks and two expanded tail chunks
-constexpr size_t TC_SMEM = 1024 + (size_t)TC_WSLOTS * TC_WCHUNK + 2 * TC_BCHUNK + 2 * TC_TAIL_B;
+constexpr size_t TC_SMEM = 1024 + (size_t)TC_SLOTS * TC_SLOT_BYTES;  // + alignment slack
+static_assert(TC_SLOT_BYTES % 1024 == 0, "slots keep the 1024-byte alignment of the swizzled tiles");
 static_assert(TC_COLS == 512, "tensor memory holds 512 columns per SM");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -96,6 +103,44 @@ __device__ __forceinline__ void cp_async16_tc(void* dst, const void* src) {
 __device__ __forceinline__ void cp_commit_tc() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_wait_tc() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void cp_async4_tc(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// D (tensor memory) += A * B, kind::i8, one thread
+__device__ __forceinline__ void tc_mma(uint32_t dt, uint64_t ad, uint64_t bd, uint32_t idesc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(dt),
+      "l"(ad), "l"(bd), "r"(idesc), "r"(1));
+}
+// D (tensor memory) = A * B (+ D when acc), kind::i8, one thread
+__device__ __forceinline__ void tc_mma_acc(uint32_t dt, uint64_t ad, uint64_t bd, uint32_t idesc, bool acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(dt),
+      "l"(ad), "l"(bd), "r"(idesc), "r"(acc ? 1 : 0));
+}
+// the mbarrier completes a phase once every MMA this thread issued before has completed
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+// the barrier's current phase also waits for `bytes` more bytes of bulk copies (no arrival)
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// One box of a 3-D tensor map (this GPU's own memory; no multicast) into shared memory; the bytes
+// complete on the mbarrier. x (bytes of an 8-bit tensor) is a multiple of 16.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
 
 // 16 consecutive tensor-memory columns of this warp's 32 lanes (one 32-bit value per column).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* v) {
@@ -122,6 +167,9 @@ __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.
 constexpr uint32_t TC_BIAS = 0x4B400000u;
 constexpr float TC_BIAS_F = 12582912.0f;
 __device__ __forceinline__ float tc_partial(uint32_t v) { return __fsub_rn(__uint_as_float(v), TC_BIAS_F); }
+// float(v) of an int32 |v| < 2^22 (a block sum): the bias added in integer arithmetic, then removed
+// as a float, exactly
+__device__ __forceinline__ float tc_isum(uint32_t v) { return __fsub_rn(__uint_as_float(v + TC_BIAS), TC_BIAS_F); }
 
 // Output of a finished row tile x entry tile.
 //   TC_OUT_STORE:  out[(t * out_nslot + slot) * ostride + row] = y
@@ -135,7 +183,15 @@ enum { TC_OUT_STORE = 0, TC_OUT_RESID = 1, TC_OUT_LMHEAD = 2 };
 // of a group, ordered group by group, row tile by row tile, entry tile fastest. Every unit has the
 // same number of steps, so CTA c of the 1-D grid takes the contiguous run of units
 // [c * U / grid, (c + 1) * U / grid) and the CTAs finish together.
+// Tensor maps of a Q8 matrix stack (x = byte of the row, y = row, z = matrix): `main` boxes a
+// chunk of 128 rows x 128 bytes with the 128-byte swizzle (the MMA's A tile as is); `tail` boxes
+// 128 rows x 16 bytes (half of a tail block, 8-row x 16-byte core matrices).
+struct TcMaps {
+  CUtensorMap main, tail;
+};
+
 struct TcArgs {
+  TcMaps m0, m1;           // maps of W0 and W (64-byte aligned members first)
   Q8M W;                   // routed-expert stack [ne][rows][cols]
   Q8M W0;                  // group 0's matrix (same shape); qs == null: no group 0
   const int32_t* ecount;   // [ne + 2]: entries per expert, then the active-expert count
@@ -157,16 +213,14 @@ constexpr int TC_MAX_GROUPS = 72;   // group 0 + up to 71 routed experts
 constexpr int TC_MAX_UNITS = 128;   // units per CTA (the host sizes the grid so that runs fit)
 
 template <int OUT>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_tc(TcArgs G) {
+__global__ void __launch_bounds__(TC_THREADS, 1) k_tc(const __grid_constant__ TcArgs G) {
   extern __shared__ __align__(16) unsigned char tc_raw[];
-  // 1024-byte aligned tiles (the 128-byte swizzle pattern repeats every 1024 bytes)
-  unsigned char* base = tc_raw + ((1024 - (smem_u32(tc_raw) & 1023)) & 1023);
-  unsigned char* wring = base;                                 // [TC_WSLOTS][128 rows][128 B], swizzled
-  unsigned char* bbuf = base + (size_t)TC_WSLOTS * TC_WCHUNK;  // [2][4 lp][TC_TOK][2 kc][8 rows][16 B]
-  unsigned char* btail = bbuf + 2 * TC_BCHUNK;                 // [2][3 tail blocks][TC_TOK][2 kc][8][16 B]
-  __shared__ uint64_t mma_bar[2];
+  // slots of 1024-byte aligned tiles (the 128-byte swizzle pattern repeats every 1024 bytes):
+  // [weights 128 rows x 128 B, swizzled][expanded chunk: 4 lp x TC_TOK x 256 B][expanded tail]
+  unsigned char* ring = tc_raw + ((1024 - (smem_u32(tc_raw) & 1023)) & 1023);
+  __shared__ uint64_t full_bar[TC_SLOTS], empty_bar[TC_SLOTS], tfull_bar[2], tempty_bar[2];
   __shared__ uint32_t tmem_base_s;
-  __shared__ int fail_s, run_s[2];
+  __shared__ int fail_s, run_s[2], mma_last_s;
   __shared__ int g_start[TC_MAX_GROUPS + 1], g_tiles[TC_MAX_GROUPS], g_count[TC_MAX_GROUPS], g_exp[TC_MAX_GROUPS];
   __shared__ int u_gi[TC_MAX_UNITS], u_r0[TC_MAX_UNITS];
   __shared__ int u_code[TC_MAX_UNITS][TC_TOK];
@@ -177,7 +231,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc(TcArgs G) {
   const int nst = nch + (ntail ? 1 : 0);
   const int rt = (rows + TC_M - 1) / TC_M;
   const int ng = (has0 ? 1 : 0) + G.nrouted;
-  if (G.nrouted > 0) pdl_wait();  // the expert lists come from the router
+  pdl_wait();  // activations (and, for the FFN, the expert lists) come from the previous kernels
 
   // ---- the groups, this CTA's run of units, and the units' entry codes ----
   if (warp == 0) {
@@ -211,6 +265,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc(TcArgs G) {
   __syncthreads();
   const int ub = run_s[0], nun = run_s[1];
   if (nun <= 0) return;
+  pdl_trigger();
   for (int i = tid; i < nun * TC_TOK; i += TC_THREADS) {
     const int ui = i / TC_TOK, e = i - ui * TC_TOK, u = ub + ui;
     int lo = 0, hi = ng - 1;  // the group gi with g_start[gi] <= u < g_start[gi + 1]
@@ -231,334 +286,659 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc(TcArgs G) {
   }
   const int S = nun * nst;
 
-  // ---- set-up: tensor memory, the MMA barriers, zeroed activation expansions ----
-  if (warp == 0) {
+  // ---- set-up: tensor memory, barriers, zeroed activation expansions, biased accumulators ----
+  if (warp == TC_MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
                  "r"(TC_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    mbar_init(&mma_bar[0], 1);
-    mbar_init(&mma_bar[1], 1);
+    for (int k = 0; k < TC_SLOTS; k++) {
+      mbar_init(&full_bar[k], TC_NPROD);  // every copy thread, after its copies of the slot landed
+      mbar_init(&empty_bar[k], 1);        // the MMAs that read the slot (commit)
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull_bar[b], 1);              // the MMAs that wrote the buffer (commit)
+      mbar_init(&tempty_bar[b], TC_EPI_WARPS);  // every chain warp, after reading the buffer
+    }
     fail_s = 0;
+    mma_last_s = -1;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  for (int i = tid; i < (2 * TC_BCHUNK + 2 * TC_TAIL_B) / 16; i += TC_THREADS)
-    reinterpret_cast<int4*>(bbuf)[i] = make_int4(0, 0, 0, 0);
+  for (int i = tid; i < TC_SLOTS * (TC_BCHUNK + TC_TAIL_B) / 16; i += TC_THREADS) {
+    const int k = i / ((TC_BCHUNK + TC_TAIL_B) / 16), r = i - k * ((TC_BCHUNK + TC_TAIL_B) / 16);
+    reinterpret_cast<int4*>(ring + (size_t)k * TC_SLOT_BYTES + TC_WCHUNK)[r] = make_int4(0, 0, 0, 0);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = tmem_base_s;
-
-  // matrix of unit ui: its quantized rows and scales
-  auto unit_q = [&](int ui) -> const int8_t* {
-    const int gi = u_gi[ui];
-    return (has0 && gi == 0) ? G.W0.qs : G.W.qs + (long long)g_exp[gi] * G.W.qs_mstride;
-  };
-  auto unit_s = [&](int ui) -> const float* {
-    const int gi = u_gi[ui];
-    return (has0 && gi == 0) ? G.W0.sc : G.W.sc + (long long)g_exp[gi] * G.W.sc_mstride;
-  };
-  auto in_row = [&](int code) -> int {
-    return G.in_nslot ? (code >> 5) * G.in_nslot + (code & 31) : (code >> 5);
-  };
-
-  // Steps g = 0..S-1: step g is chunk s = g % nst of unit g / nst, ring slot g % TC_WSLOTS,
-  // buffers g % 2. Four running positions: the weight copies (g + TC_WAHEAD), the activation
-  // words (g + 2), the scales (g + 1) and the chains (g), each with the pointers of its unit.
-  // ---- weight copies: 16-byte pieces (rows wm0 and wm0 + 64, piece wj) of each chunk ----
-  const int wj = tid & 7, wm0 = tid >> 3;
-  const int wdst = wm0 * 128 + ((wj ^ (wm0 & 7)) << 4);  // same swizzle phase for row wm0 + 64
-  int uw = 0, sw = 0, rw = 0;                            // unit, chunk and ring slot of step g + TC_WAHEAD
-  const int8_t* wsrc0 = nullptr;
-  const int8_t* wsrc1 = nullptr;
-  auto w_unit = [&](int ui) {
-    const int8_t* q = unit_q(ui) + wj * 16;
-    const int r0 = u_r0[ui];
-    wsrc0 = q + (long long)min(r0 + wm0, rows - 1) * cols;
-    wsrc1 = q + (long long)min(r0 + wm0 + 64, rows - 1) * cols;
-  };
-  auto issue_w = [&](bool live) {  // one commit group per call
-    if (live) {
-      unsigned char* dst = wring + (size_t)rw * TC_WCHUNK;
-      if (sw < nch) {
-        cp_async16_tc(dst + wdst, wsrc0 + sw * 128);
-        cp_async16_tc(dst + wdst + 64 * 128, wsrc1 + sw * 128);
-      } else {  // tail blocks, no swizzle: 8-row x 16-byte core matrices
-        const int8_t* q = unit_q(uw);
-        const int r0 = u_r0[uw];
-        for (int i = tid; i < TC_M * ntail * 2; i += TC_THREADS) {
-          const int m = i / (ntail * 2), rem = i - m * (ntail * 2), tb = rem >> 1, kc = rem & 1;
-          cp_async16_tc(dst + tb * 4096 + (m >> 3) * 256 + kc * 128 + (m & 7) * 16,
-                        q + (long long)min(r0 + m, rows - 1) * cols + nch * 128 + tb * 32 + kc * 16);
-        }
-      }
-    }
-    cp_commit_tc();
-  };
-  auto w_next = [&]() {
-    if (++rw == TC_WSLOTS) rw = 0;
-    if (++sw == nst) {
-      sw = 0;
-      if (++uw < nun) w_unit(uw);
-    }
-  };
-
-  // ---- activation words: thread tid < 256 = (lane pair lp, entry eb, lane li, block q) holds
-  // the entry's bytes lp*32 + li*16 + q*4 .. + 3; tail: tid < ntail * 64 = (tail block, entry, lane)
-  const int eb = (tid >> 3) & (TC_TOK - 1);
-  const int sq = tid & 3, sli = (tid >> 2) & 1, slp = tid >> 6, stl = tid & 7, stb = tid >> 6;
-  const bool smain = tid < 4 * TC_TOK * 8, stail = tid < ntail * TC_TOK * 8;
-  const int aoff = slp * 32 + sli * 16 + sq * 4, atoff = nch * 128 + stb * 32 + stl * 4;
-  const int boff = slp * (TC_TOK * 256) + eb * 256 + sli * 128 + (2 * sq + sli) * 16 + sq * 4;
-  const int btoff = stb * (TC_TOK * 256) + eb * 256 + (stl >> 2) * 128 + stl * 16 + (stl & 3) * 4;
-  int ua = 0, sa = 0;  // unit and chunk of the next word to load
-  const int8_t* arow = nullptr;
-  auto a_unit = [&](int ui) {
-    const int code = u_code[ui][eb];
-    arow = code >= 0 ? G.aq + (size_t)in_row(code) * cols : nullptr;
-  };
-  auto load_word = [&]() -> int {
-    if (!arow) return 0;
-    if (sa < nch) return smain ? *reinterpret_cast<const int*>(arow + sa * 128 + aoff) : 0;
-    return stail ? *reinterpret_cast<const int*>(arow + atoff) : 0;
-  };
-  auto a_next = [&]() {
-    if (++sa == nst) {
-      sa = 0;
-      if (++ua < nun) a_unit(ua);
-    }
-  };
-  auto store_word = [&](int b, int s, int v) {
-    if (s < nch) {
-      if (smain) *reinterpret_cast<int*>(bbuf + (size_t)b * TC_BCHUNK + boff) = v;
-    } else if (stail) {
-      *reinterpret_cast<int*>(btail + (size_t)b * TC_TAIL_B + btoff) = v;
-    }
-  };
-
-  // ---- chains: row r0 + 32 (warp % 4) + lane of the unit, entries 2 (warp / 4) + 0..1 ----
-  const int quad = warp & 3, pr = warp >> 2;
-  int u1 = 0, s1 = 0;  // unit and chunk of the next scales to load
-  const float* wsc = nullptr;
-  const float* dsc0 = nullptr;
-  const float* dsc1 = nullptr;
-  auto c_unit = [&](int ui) {
-    wsc = unit_s(ui) + (long long)min(u_r0[ui] + quad * 32 + lane, rows - 1) * ss;
-    const int c0 = u_code[ui][2 * pr], c1 = u_code[ui][2 * pr + 1];
-    dsc0 = G.as + (size_t)(c0 >= 0 ? in_row(c0) : 0) * ss;  // padding entries read row 0, unused
-    dsc1 = G.as + (size_t)(c1 >= 0 ? in_row(c1) : 0) * ss;
-  };
-  auto load_scales = [&](float4& s4, float4& d0, float4& d1) {
-    s4 = __ldg(reinterpret_cast<const float4*>(wsc + 4 * s1));
-    d0 = *reinterpret_cast<const float4*>(dsc0 + 4 * s1);
-    d1 = *reinterpret_cast<const float4*>(dsc1 + 4 * s1);
-  };
-  auto c_next = [&]() {
-    if (++s1 == nst) {
-      s1 = 0;
-      if (++u1 < nun) c_unit(u1);
-    }
-  };
-
-  constexpr uint32_t IDESC = tc_idesc(TC_M, TC_N);
-  // the MMAs of a step (chunk s, ring slot) into tensor-memory buffer b, committed to mma_bar[b]
-  auto issue_mma = [&](int b, int s, int slot) {
-    const uint32_t wa = smem_u32(wring + (size_t)slot * TC_WCHUNK);
-    const uint32_t dt = tbase + b * TC_BUFCOLS;
-    if (s < nch) {
-      const uint32_t ba = smem_u32(bbuf + (size_t)b * TC_BCHUNK);
+  const int quad = warp & 3, pr = (warp >> 2) & 3;
+  const uint32_t tw = tbase + ((uint32_t)(quad * 32) << 16) + pr * 16;  // chain warps' columns
+  if (warp < TC_EPI_WARPS) {
 #pragma unroll
-      for (int lp = 0; lp < 4; lp++) {
-        const uint64_t ad = tc_desc(wa + lp * 32, 16, 1024, 2);              // 128-byte swizzled, K-major
-        const uint64_t bd = tc_desc(ba + lp * (TC_TOK * 256), 128, 256, 0);  // no swizzle, K-major
-        asm volatile(
-            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-            " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(dt + lp * TC_N),
-            "l"(ad), "l"(bd), "r"(IDESC), "r"(1));  // D += A * B onto the bias
-      }
-    } else {
-      const uint32_t ba = smem_u32(btail + (size_t)b * TC_TAIL_B);
-      for (int tb = 0; tb < ntail; tb++) {
-        const uint64_t ad = tc_desc(wa + tb * 4096, 128, 256, 0);
-        const uint64_t bd = tc_desc(ba + tb * (TC_TOK * 256), 128, 256, 0);
-        asm volatile(
-            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-            " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(dt + tb * TC_N),
-            "l"(ad), "l"(bd), "r"(IDESC), "r"(1));
-      }
-    }
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_u32(&mma_bar[b]))
-                 : "memory");
-  };
-
-  // ---- prologue: weights of steps 0..TC_WAHEAD-1 (constant data: before the dependency wait for
-  // a launch without routed groups), step 0 staged and issued, step 1's word and step 0's scales
-  // in registers ----
-  w_unit(0);
+    for (int b = 0; b < 2; b++)
 #pragma unroll
-  for (int g = 0; g < TC_WAHEAD; g++) {
-    issue_w(g < S);
-    w_next();
+      for (int lp = 0; lp < 4; lp++) tmem_st16_same(tw + b * TC_BUFCOLS + lp * TC_N, TC_BIAS);
+    tmem_st_wait();
   }
-  if (G.nrouted == 0) pdl_wait();
-  pdl_trigger();
-  a_unit(0);
-  c_unit(0);
-  store_word(0, 0, load_word());
-  a_next();
-  int wnext = 0;
-  if (S > 1) {
-    wnext = load_word();
-    a_next();
-  }
-  float4 s4, d0, d1;
-  load_scales(s4, d0, d1);
-  c_next();
-  cp_wait_tc<TC_WAHEAD - 1>();  // this thread's pieces of step 0's weights
-  fence_async_smem();           // generic-proxy writes (cp.async, the expansion) -> tensor-core reads
-  // this warp's accumulator columns of both buffers start at the bias
-  const uint32_t tw = tbase + ((uint32_t)(quad * 32) << 16) + pr * 16;
-#pragma unroll
-  for (int b = 0; b < 2; b++)
-#pragma unroll
-    for (int lp = 0; lp < 4; lp++) tmem_st16_same(tw + b * TC_BUFCOLS + lp * TC_N, TC_BIAS);
-  tmem_st_wait();
+  fence_async_smem();  // the zeroed expansions -> tensor-core reads
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  int issued = 0;  // steps whose MMAs were issued (thread 0)
-  if (tid == 0) {
-    issue_mma(0, 0, 0);
-    issued = 1;
-  }
 
-  float acc[2][8];
+  auto in_row = [&](int code) -> int {
+    return G.in_nslot ? (code >> 5) * G.in_nslot + (code & 31) : (code >> 5);
+  };
+  auto failed = [&]() -> bool { return *reinterpret_cast<volatile int*>(&fail_s) != 0; };
+  auto give_up = [&]() { *reinterpret_cast<volatile int*>(&fail_s) = 1; };
+
+  if (warp >= TC_EPI_WARPS && warp < TC_MMA_WARP) {
+    // =================== copy warps: weights and activation words of every step ===================
+    const int p = tid - TC_PROD0;  // 0..TC_NPROD-1
+    constexpr int APT = 4 * TC_TOK * 8 / TC_NPROD;  // activation words per thread
+    // weights: one bulk tensor copy per step by thread 0 (rows past the matrix read as zeros);
+    // activation words: w = p + TC_NPROD i (i < APT) = (lane pair lp, entry e, lane li, block q)
+    const TcMaps* wmap = nullptr;
+    int r0 = 0, wz = 0;
+    const int8_t* arow[APT];
+    int aoff[APT], boff[APT];
 #pragma unroll
-  for (int e = 0; e < 2; e++)
+    for (int i = 0; i < APT; i++) {
+      const int w = p + TC_NPROD * i, q = w & 3, li = (w >> 2) & 1, e = (w >> 3) & (TC_TOK - 1), lp = w >> 6;
+      aoff[i] = lp * 32 + li * 16 + q * 4;
+      boff[i] = lp * (TC_TOK * 256) + e * 256 + li * 128 + (2 * q + li) * 16 + q * 4;
+      arow[i] = nullptr;
+    }
+    int ui = -1;
+    auto set_unit = [&](int u) {
+      ui = u;
+      const int gi = u_gi[u];
+      wmap = (has0 && gi == 0) ? &G.m0 : &G.m1;
+      wz = (has0 && gi == 0) ? 0 : g_exp[gi];
+      r0 = u_r0[u];
 #pragma unroll
-    for (int l = 0; l < 8; l++) acc[e][l] = 0.0f;
-  int u0 = 0, s0 = 0, r1 = 1;  // unit and chunk of step g; ring slot of step g + 1
-  int fail = 0;
-  for (int g = 0; g < S; g++) {
-    issue_w(g + TC_WAHEAD < S);  // ring slot of step g - 2, whose MMAs this thread saw complete
-    w_next();
-    int s_next = s0 + 1 == nst ? 0 : s0 + 1;  // chunk of step g + 1
-    if (g + 1 < S) {
-      store_word((g + 1) & 1, s_next, wnext);  // buffer (g + 1) % 2: last read by step g - 1's MMAs
-      if (g + 2 < S) {
-        wnext = load_word();
-        a_next();
+      for (int i = 0; i < APT; i++) {
+        const int e = ((p + TC_NPROD * i) >> 3) & (TC_TOK - 1), code = u_code[u][e];
+        arow[i] = code >= 0 ? G.aq + (size_t)in_row(code) * cols : nullptr;
+      }
+    };
+    constexpr int PD = 3;  // copy groups in flight per thread before a slot is signalled
+    int s = 0, u = 0;
+    set_unit(0);
+    int sig = 0;  // next step to signal
+    for (int g = 0; g < S; g++) {
+      const int k = g % TC_SLOTS, n = g / TC_SLOTS;
+      if (n >= 1 && !failed() && !mbar_wait(&empty_bar[k], (n - 1) & 1)) give_up();
+      if (!failed()) {
+        unsigned char* slot = ring + (size_t)k * TC_SLOT_BYTES;
+        if (s < nch) {
+          if (p == 0) {  // the A tile: 128 rows x 128 bytes, swizzled by the copy engine
+            mbar_expect_tx(&full_bar[k], TC_WCHUNK);
+            tma_load_3d(slot, &wmap->main, s * 128, r0, wz, &full_bar[k]);
+          }
+#pragma unroll
+          for (int i = 0; i < APT; i++)
+            if (arow[i]) cp_async4_tc(slot + TC_WCHUNK + boff[i], arow[i] + s * 128 + aoff[i]);
+        } else {
+          if (p == 0) {  // tail block tb, half kc: 128 rows x 16 bytes at tb * 4096 + kc * 2048
+            mbar_expect_tx(&full_bar[k], ntail * 4096);
+            for (int tb = 0; tb < ntail; tb++)
+              for (int kc = 0; kc < 2; kc++)
+                tma_load_3d(slot + tb * 4096 + kc * 2048, &wmap->tail, nch * 128 + tb * 32 + kc * 16, r0, wz,
+                            &full_bar[k]);
+          }
+          for (int w = p; w < ntail * TC_TOK * 8; w += TC_NPROD) {  // (tail block tb, entry e, lane l)
+            const int l = w & 7, e = (w >> 3) & (TC_TOK - 1), tb = w >> 6, code = u_code[ui][e];
+            if (code >= 0)
+              cp_async4_tc(slot + TC_WCHUNK + TC_BCHUNK + tb * (TC_TOK * 256) + e * 256 + (l >> 2) * 128 + l * 16 +
+                               (l & 3) * 4,
+                           G.aq + (size_t)in_row(code) * cols + nch * 128 + tb * 32 + l * 4);
+          }
+        }
+      }
+      cp_commit_tc();
+      if (++s == nst) {
+        s = 0;
+        if (++u < nun) set_unit(u);
+      }
+      if (g - sig == PD - 1) {  // step sig's copies landed: publish them to the tensor cores
+        cp_wait_tc<PD - 1>();
+        fence_async_smem();
+        mbar_arrive(&full_bar[sig % TC_SLOTS]);
+        sig++;
       }
     }
-    cp_wait_tc<TC_WAHEAD - 1>();  // this thread's pieces of step g + 1's weights have landed
+    cp_wait_tc<0>();
     fence_async_smem();
-    if (fail && lane == 0) fail_s = 1;
-    tc_fence_before();
-    __syncthreads();  // step g + 1 staged; everyone done reading step g - 1's partials
-    tc_fence_after();
-    fail = fail_s;
-    if (tid == 0 && !fail && g + 1 < S) {
-      issue_mma((g + 1) & 1, s_next, r1);
-      issued = g + 2;
-    }
-    if (++r1 == TC_WSLOTS) r1 = 0;
-    float sc0[4], sc1[4];
-    sc0[0] = fmul(s4.x, d0.x); sc0[1] = fmul(s4.y, d0.y); sc0[2] = fmul(s4.z, d0.z); sc0[3] = fmul(s4.w, d0.w);
-    sc1[0] = fmul(s4.x, d1.x); sc1[1] = fmul(s4.y, d1.y); sc1[2] = fmul(s4.z, d1.z); sc1[3] = fmul(s4.w, d1.w);
-    if (g + 1 < S) {
-      load_scales(s4, d0, d1);
-      c_next();
-    }
-    if (!fail && !mbar_wait(&mma_bar[g & 1], (g >> 1) & 1)) fail = 1;
-    fail = __any_sync(0xffffffffu, fail);  // warp-uniform: tcgen05.ld below is a .sync.aligned warp op
-    tc_fence_after();
-    if (!fail) {
-      const uint32_t ta = tw + (g & 1) * TC_BUFCOLS;
-      uint32_t v[16];
-      if (s0 < nch) {
-        // column e*8 + 2q + li of lane pair lp: entry 2pr + e, block 4c + q, lane 2lp + li
+    for (; sig < S; sig++) mbar_arrive(&full_bar[sig % TC_SLOTS]);
+  } else if (warp == TC_MMA_WARP) {
+    // =================== MMA warp: one thread issues every step's MMAs ===================
+    if (lane == 0) {
+      constexpr uint32_t IDESC = tc_idesc(TC_M, TC_N);
+      int s = 0;
+      for (int g = 0; g < S && !failed(); g++) {
+        const int k = g % TC_SLOTS, b = g & 1;
+        if (!mbar_wait(&full_bar[k], (g / TC_SLOTS) & 1)) { give_up(); break; }
+        if (g >= 2 && !mbar_wait(&tempty_bar[b], ((g >> 1) - 1) & 1)) { give_up(); break; }
+        tc_fence_after();
+        unsigned char* slot = ring + (size_t)k * TC_SLOT_BYTES;
+        const uint32_t wa = smem_u32(slot), dt = tbase + b * TC_BUFCOLS;
+        if (s < nch) {
+          const uint32_t ba = smem_u32(slot + TC_WCHUNK);
 #pragma unroll
-        for (int lp = 0; lp < 4; lp++) {  // one lane pair per tensor-memory round trip
-          tmem_ld16(ta + lp * TC_N, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int q = 0; q < 4; q++)
-#pragma unroll
-            for (int li = 0; li < 2; li++) {
-              const int l = 2 * lp + li;
-              acc[0][l] = __fmaf_rn(sc0[q], tc_partial(v[2 * q + li]), acc[0][l]);
-              acc[1][l] = __fmaf_rn(sc1[q], tc_partial(v[8 + 2 * q + li]), acc[1][l]);
-            }
+          for (int lp = 0; lp < 4; lp++) {
+            const uint64_t ad = tc_desc(wa + lp * 32, 16, 1024, 2);              // 128-byte swizzled, K-major
+            const uint64_t bd = tc_desc(ba + lp * (TC_TOK * 256), 128, 256, 0);  // no swizzle, K-major
+            tc_mma(dt + lp * TC_N, ad, bd, IDESC);
+          }
+        } else {
+          const uint32_t ba = smem_u32(slot + TC_WCHUNK + TC_BCHUNK);
+          for (int tb = 0; tb < ntail; tb++)
+            tc_mma(dt + tb * TC_N, tc_desc(wa + tb * 4096, 2048, 128, 0), tc_desc(ba + tb * (TC_TOK * 256), 128, 256, 0),
+                   IDESC);
         }
-      } else {
-        // column e*8 + l of tail block tb: entry 2pr + e, lane l of block 4 nch + tb
+        tc_commit(&tfull_bar[b]);   // the chain warps may read buffer b
+        tc_commit(&empty_bar[k]);   // the copy warps may refill slot k
+        mma_last_s = g;
+        if (++s == nst) s = 0;
+      }
+    }
+    __syncwarp();
+  } else {
+    // =================== chain warps: row r0 + 32 (warp % 4) + lane, entries 2 (warp / 4) + 0..1 =====
+    int u1 = 0, s1 = 0;  // unit and chunk of the next scales to load
+    const float* wsc = nullptr;
+    const float* dsc0 = nullptr;
+    const float* dsc1 = nullptr;
+    auto c_unit = [&](int ui) {
+      const int gi = u_gi[ui];
+      const float* sc = (has0 && gi == 0) ? G.W0.sc : G.W.sc + (long long)g_exp[gi] * G.W.sc_mstride;
+      wsc = sc + (long long)min(u_r0[ui] + quad * 32 + lane, rows - 1) * ss;
+      const int c0 = u_code[ui][2 * pr], c1 = u_code[ui][2 * pr + 1];
+      dsc0 = G.as + (size_t)(c0 >= 0 ? in_row(c0) : 0) * ss;  // padding entries read row 0, unused
+      dsc1 = G.as + (size_t)(c1 >= 0 ? in_row(c1) : 0) * ss;
+    };
+    float4 s4, d0, d1;
+    auto load_scales = [&]() {
+      s4 = __ldg(reinterpret_cast<const float4*>(wsc + 4 * s1));
+      d0 = *reinterpret_cast<const float4*>(dsc0 + 4 * s1);
+      d1 = *reinterpret_cast<const float4*>(dsc1 + 4 * s1);
+      if (++s1 == nst) {
+        s1 = 0;
+        if (++u1 < nun) c_unit(u1);
+      }
+    };
+    c_unit(0);
+    load_scales();
+    float acc[2][8];
 #pragma unroll
-        for (int tb = 0; tb < 3; tb++)
-          if (tb < ntail) {
-            tmem_ld16(ta + tb * TC_N, v);
+    for (int e = 0; e < 2; e++)
+#pragma unroll
+      for (int l = 0; l < 8; l++) acc[e][l] = 0.0f;
+    int u0 = 0, s0 = 0, fail = 0;
+    for (int g = 0; g < S; g++) {
+      const int b = g & 1;
+      float sc0[4], sc1[4];
+      sc0[0] = fmul(s4.x, d0.x); sc0[1] = fmul(s4.y, d0.y); sc0[2] = fmul(s4.z, d0.z); sc0[3] = fmul(s4.w, d0.w);
+      sc1[0] = fmul(s4.x, d1.x); sc1[1] = fmul(s4.y, d1.y); sc1[2] = fmul(s4.z, d1.z); sc1[3] = fmul(s4.w, d1.w);
+      if (g + 1 < S) load_scales();
+      if (!fail) {
+        if (failed() || !mbar_wait(&tfull_bar[b], (g >> 1) & 1)) fail = 1;
+        fail = __any_sync(0xffffffffu, fail);  // warp-uniform: tcgen05.ld below is a .sync.aligned warp op
+        if (fail) give_up();
+      }
+      tc_fence_after();
+      if (!fail) {
+        const uint32_t ta = tw + b * TC_BUFCOLS;
+        uint32_t v[16];
+        if (s0 < nch) {
+          // column e*8 + 2q + li of lane pair lp: entry 2pr + e, block 4c + q, lane 2lp + li
+#pragma unroll
+          for (int lp = 0; lp < 4; lp++) {
+            tmem_ld16(ta + lp * TC_N, v);
             tmem_ld_wait();
 #pragma unroll
-            for (int l = 0; l < 8; l++) {
-              acc[0][l] = __fmaf_rn(sc0[tb], tc_partial(v[l]), acc[0][l]);
-              acc[1][l] = __fmaf_rn(sc1[tb], tc_partial(v[8 + l]), acc[1][l]);
-            }
+            for (int q = 0; q < 4; q++)
+#pragma unroll
+              for (int li = 0; li < 2; li++) {
+                const int l = 2 * lp + li;
+                acc[0][l] = __fmaf_rn(sc0[q], tc_partial(v[2 * q + li]), acc[0][l]);
+                acc[1][l] = __fmaf_rn(sc1[q], tc_partial(v[8 + 2 * q + li]), acc[1][l]);
+              }
           }
-      }
-      // back to the bias for step g + 2's MMAs (issued after the next barrier)
+        } else {
+          // column e*8 + l of tail block tb: entry 2pr + e, lane l of block 4 nch + tb
 #pragma unroll
-      for (int lp = 0; lp < 4; lp++) tmem_st16_same(ta + lp * TC_N, TC_BIAS);
-      tmem_st_wait();
-    }
-    if (++s0 == nst) {
-      // ---- unit u0 done: the lane tree ((l0+l4)+(l2+l6))+((l1+l5)+(l3+l7)) (quant.rs:61-65) ----
-      s0 = 0;
-      if (!fail) {
-        const int row = u_r0[u0] + quad * 32 + lane;
-        const bool row_ok = row < rows;
+          for (int tb = 0; tb < 3; tb++)
+            if (tb < ntail) {
+              tmem_ld16(ta + tb * TC_N, v);
+              tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 2; e++) {
-          const int code = u_code[u0][2 * pr + e];  // warp-uniform
-          const float* a = acc[e];
-          const float yv = fadd(fadd(fadd(a[0], a[4]), fadd(a[2], a[6])), fadd(fadd(a[1], a[5]), fadd(a[3], a[7])));
-          const bool ok = row_ok && code >= 0;
-          const int t = code >> 5, sl = code & 31;
-          if (OUT == TC_OUT_STORE) {
-            if (ok) G.out[((size_t)t * G.out_nslot + sl) * G.ostride + row] = yv;
-          } else if (OUT == TC_OUT_RESID) {
-            if (ok) {
-              float* xp = G.x + (size_t)t * G.d + row;
-              *xp = fadd(*xp, yv);
+              for (int l = 0; l < 8; l++) {
+                acc[0][l] = __fmaf_rn(sc0[tb], tc_partial(v[l]), acc[0][l]);
+                acc[1][l] = __fmaf_rn(sc1[tb], tc_partial(v[8 + l]), acc[1][l]);
+              }
             }
-          } else {
-            if (ok && G.out) G.out[(size_t)t * G.ostride + row] = yv;
-            unsigned long long key = (ok && row < G.valid) ? argmax_key(yv, (uint32_t)row) : 0ull;
+        }
+        // back to the bias for the MMAs of step g + 2, then hand the buffer back
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
-            if (lane == 0 && code >= 0 && key) atomicMax(&G.amax[t], key);
+        for (int lp = 0; lp < 4; lp++) tmem_st16_same(ta + lp * TC_N, TC_BIAS);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[b]);
+      }
+      if (++s0 == nst) {
+        // ---- unit u0 done: the lane tree ((l0+l4)+(l2+l6))+((l1+l5)+(l3+l7)) (quant.rs:61-65) ----
+        s0 = 0;
+        if (!fail) {
+          const int row = u_r0[u0] + quad * 32 + lane;
+          const bool row_ok = row < rows;
+#pragma unroll
+          for (int e = 0; e < 2; e++) {
+            const int code = u_code[u0][2 * pr + e];  // warp-uniform
+            const float* a = acc[e];
+            const float yv =
+                fadd(fadd(fadd(a[0], a[4]), fadd(a[2], a[6])), fadd(fadd(a[1], a[5]), fadd(a[3], a[7])));
+            const bool ok = row_ok && code >= 0;
+            const int t = code >> 5, sl = code & 31;
+            if (OUT == TC_OUT_STORE) {
+              if (ok) G.out[((size_t)t * G.out_nslot + sl) * G.ostride + row] = yv;
+            } else if (OUT == TC_OUT_RESID) {
+              if (ok) {
+                float* xp = G.x + (size_t)t * G.d + row;
+                *xp = fadd(*xp, yv);
+              }
+            } else {
+              if (ok && G.out) G.out[(size_t)t * G.ostride + row] = yv;
+              unsigned long long key = (ok && row < G.valid) ? argmax_key(yv, (uint32_t)row) : 0ull;
+#pragma unroll
+              for (int o = 16; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+              if (lane == 0 && code >= 0 && key) atomicMax(&G.amax[t], key);
+            }
           }
         }
+#pragma unroll
+        for (int e = 0; e < 2; e++)
+#pragma unroll
+          for (int l = 0; l < 8; l++) acc[e][l] = 0.0f;
+        u0++;
       }
-#pragma unroll
-      for (int e = 0; e < 2; e++)
-#pragma unroll
-        for (int l = 0; l < 8; l++) acc[e][l] = 0.0f;
-      u0++;
     }
   }
-  cp_wait_tc<0>();
-  if (fail && lane == 0) fail_s = 1;
+  // ---- wind-down: every MMA complete before the columns are freed ----
   __syncthreads();
-  if (fail_s && tid == 0 && issued > 0) {
-    // stopped early: let the last issued MMAs finish (bounded) before the columns are freed
-    const int last = issued - 1;
-    mbar_wait(&mma_bar[last & 1], (last >> 1) & 1);
+  if (tid == TC_MMA_WARP * 32 && failed() && mma_last_s >= 0) {
+    // stopped early: the last commit covers every MMA issued before it (bounded wait)
+    const int last = mma_last_s;
+    mbar_wait(&tfull_bar[last & 1], (last >> 1) & 1);
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(TC_COLS));
-  if (fail_s && tid == 0 && G.err) atomicExch(G.err, HG_ERR_TIMEOUT);
+  if (warp == TC_MMA_WARP)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(TC_COLS));
+  if (failed() && tid == 0 && G.err) atomicExch(G.err, HG_ERR_TIMEOUT);
+}
+
+// ------------------------------------------------------------------------------------------
+// Prefill-order Q8 matmul on the tensor cores (quant.rs:144-193): per output (row o, activation
+// row t) acc = fadd(acc, fmul(fmul(sw[o][b], sx[t][b]), float(isum[o][t][b]))) over the blocks b
+// in order, isum the exact int32 dot of one 32-element block. An MMA of kind::i8 gives the block
+// sums: for lane pair lp of a 128-byte chunk, B row n = 4 t + q holds activation row t's bytes of
+// block q (its 8 bytes in the lane pair, zeros elsewhere), so the four lane-pair MMAs accumulate
+// D[o][4 t + q] = isum of block 4c + q. Tail blocks (rows whose width is not a multiple of 128
+// bytes) are contiguous 32 bytes: one MMA per tail block with B row t = activation row t.
+// A unit is 128 weight rows x 64 activation rows of one group (a matrix of the stack and its
+// entry range, MmArgs grp tables); CTAs take balanced runs of units; the roles and the pipeline
+// are those of k_tc (copy warps, one MMA thread, chain warps) with a 3-slot ring.
+// ------------------------------------------------------------------------------------------
+constexpr int KT_TOK = 64;                              // activation rows per unit
+constexpr int KT_N = 4 * KT_TOK;                        // MMA N of a chunk step
+constexpr int KT_BMAIN = 4 * KT_N * 32;                 // expanded chunk: 4 lp x 256 rows x 32 B
+constexpr int KT_BTAIL = 3 * KT_TOK * 32;               // tail blocks: 3 x 64 rows x 32 B
+constexpr int KT_SX = KT_TOK * 16;                      // the rows' 4 block scales of the step
+constexpr int KT_SLOT_BYTES = ((TC_WCHUNK + KT_BMAIN + KT_BTAIL + KT_SX + 1023) / 1024) * 1024;
+constexpr int KT_SLOTS = 3;
+constexpr int KT_PROD_WARPS = 2;
+constexpr int KT_NPROD = 32 * KT_PROD_WARPS;            // == KT_TOK: copy thread p serves activation row p
+constexpr int KT_MMA_WARP = TC_EPI_WARPS + KT_PROD_WARPS;
+constexpr int KT_THREADS = 32 * (KT_MMA_WARP + 1);
+constexpr size_t KT_SMEM = 1024 + (size_t)KT_SLOTS * KT_SLOT_BYTES;
+static_assert(KT_NPROD == KT_TOK, "one copy thread per activation row");
+
+struct KtArgs {
+  TcMaps m;     // maps of the stack W
+  MmArgs a;
+  int ngroups;
+};
+
+__global__ void __launch_bounds__(KT_THREADS, 1) kp_tc(const __grid_constant__ KtArgs K) {
+  const MmArgs& a = K.a;
+  const int ngroups = K.ngroups;
+  extern __shared__ __align__(16) unsigned char kt_raw[];
+  unsigned char* ring = kt_raw + ((1024 - (smem_u32(kt_raw) & 1023)) & 1023);
+  __shared__ uint64_t full_bar[KT_SLOTS], empty_bar[KT_SLOTS], sxfree_bar[KT_SLOTS], tfull_bar[2], tempty_bar[2];
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int fail_s, run_s[2], mma_last_s;
+  __shared__ int g_start[TC_MAX_GROUPS + 1], g_tiles[TC_MAX_GROUPS], g_count[TC_MAX_GROUPS], g_mat[TC_MAX_GROUPS],
+      g_off[TC_MAX_GROUPS];
+  __shared__ int u_gi[TC_MAX_UNITS], u_r0[TC_MAX_UNITS], u_a0[TC_MAX_UNITS];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const Q8M& W = a.W;
+  const int rows = W.rows, cols = W.cols, nb = cols >> 5, nch = nb >> 2, ntail = nb & 3, ss = W.ss;
+  const int nst = nch + (ntail ? 1 : 0);
+  const int rt = (rows + TC_M - 1) / TC_M;
+
+  // ---- groups (one, or the grp tables of an expert launch), this CTA's run of units ----
+  if (warp == 0) {
+    for (int gi = lane; gi < ngroups; gi += 32) {
+      int mat = a.mat, off = 0, cnt = a.nrows;
+      if (a.grp_mat) {
+        mat = a.grp_mat[gi];
+        off = a.grp_off[gi];
+        cnt = mat < 0 ? 0 : a.grp_cnt[gi];
+      }
+      g_mat[gi] = mat;
+      g_off[gi] = off;
+      g_count[gi] = cnt;
+      g_tiles[gi] = (cnt + KT_TOK - 1) / KT_TOK;
+    }
+    __syncwarp();
+    if (lane == 0) {
+      int acc = 0;
+      for (int gi = 0; gi < ngroups; gi++) {
+        g_start[gi] = acc;
+        acc += rt * g_tiles[gi];
+      }
+      g_start[ngroups] = acc;
+      const long long U = acc, nc = gridDim.x;
+      const int ub = (int)(U * blockIdx.x / nc), ue = (int)(U * (blockIdx.x + 1) / nc);
+      run_s[0] = ub;
+      run_s[1] = min(ue - ub, TC_MAX_UNITS);
+      if (ue - ub > TC_MAX_UNITS && a.err) atomicExch(a.err, HG_ERR_INVALID);  // host sizing bug: loud
+    }
+  }
+  __syncthreads();
+  const int ub = run_s[0], nun = run_s[1];
+  if (nun <= 0) return;
+  for (int ui = tid; ui < nun; ui += KT_THREADS) {
+    const int u = ub + ui;
+    int lo = 0, hi = ngroups - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (g_start[mid] <= u) lo = mid;
+      else hi = mid - 1;
+    }
+    const int tl = g_tiles[lo], ul = u - g_start[lo], rtile = ul / tl;
+    u_gi[ui] = lo;
+    u_r0[ui] = rtile * TC_M;
+    u_a0[ui] = (ul - rtile * tl) * KT_TOK;
+  }
+  const int S = nun * nst;
+
+  if (warp == KT_MMA_WARP) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                 "r"(TC_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    for (int k = 0; k < KT_SLOTS; k++) {
+      mbar_init(&full_bar[k], KT_NPROD);
+      mbar_init(&empty_bar[k], 1);
+      mbar_init(&sxfree_bar[k], TC_EPI_WARPS);  // every chain warp, after reading the slot's scales
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], TC_EPI_WARPS);
+    }
+    fail_s = 0;
+    mma_last_s = -1;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  for (int i = tid; i < KT_SLOTS * (KT_BMAIN / 16); i += KT_THREADS) {  // the expansions' zeros, once
+    const int k = i / (KT_BMAIN / 16), r = i - k * (KT_BMAIN / 16);
+    reinterpret_cast<int4*>(ring + (size_t)k * KT_SLOT_BYTES + TC_WCHUNK)[r] = make_int4(0, 0, 0, 0);
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base_s;
+  auto failed = [&]() -> bool { return *reinterpret_cast<volatile int*>(&fail_s) != 0; };
+  auto give_up = [&]() { *reinterpret_cast<volatile int*>(&fail_s) = 1; };
+  auto arow_of = [&](int ui, int i) -> long long {  // activation row of entry i of unit ui, or -1
+    const int gi = u_gi[ui], e = u_a0[ui] + i;
+    if (e >= g_count[gi]) return -1;
+    const int idx = g_off[gi] + e;
+    return a.a_idx ? (long long)a.a_idx[idx] : (long long)idx;
+  };
+
+  if (warp >= TC_EPI_WARPS && warp < KT_MMA_WARP) {
+    // =================== copy warps: thread p = activation row p of the unit ===================
+    const int p = tid - TC_EPI_WARPS * 32;
+    int r0 = 0, wz = 0;
+    const int8_t* xrow = nullptr;  // activation row p of the unit (null past the group's rows)
+    const float* xsc = nullptr;
+    int ui = 0;
+    auto set_unit = [&](int u) {
+      ui = u;
+      const int mat = g_mat[u_gi[u]];
+      wz = mat < 0 ? 0 : mat;
+      r0 = u_r0[u];
+      const long long ar = arow_of(u, p);
+      xrow = ar >= 0 ? a.aq + ar * cols : nullptr;
+      xsc = ar >= 0 ? a.as + ar * ss : nullptr;
+    };
+    constexpr int PD = 2;
+    int s = 0, u = 0, sig = 0;
+    set_unit(0);
+    for (int g = 0; g < S; g++) {
+      const int k = g % KT_SLOTS, n = g / KT_SLOTS;
+      if (n >= 1 && !failed() &&
+          (!mbar_wait(&empty_bar[k], (n - 1) & 1) || !mbar_wait(&sxfree_bar[k], (n - 1) & 1)))
+        give_up();
+      if (!failed()) {
+        unsigned char* slot = ring + (size_t)k * KT_SLOT_BYTES;
+        float* sxd = reinterpret_cast<float*>(slot + TC_WCHUNK + KT_BMAIN + KT_BTAIL) + p * 4;
+        if (s < nch) {
+          if (p == 0) {  // the A tile: 128 rows x 128 bytes, swizzled by the copy engine
+            mbar_expect_tx(&full_bar[k], TC_WCHUNK);
+            tma_load_3d(slot, &K.m.main, s * 128, r0, wz, &full_bar[k]);
+          }
+          if (xrow) {
+            // byte lp*32 + li*16 + q*4 .. + 3 of the chunk -> B row n = 4 p + q of lane pair lp, K
+            // bytes li*16 + q*4 .. + 3 (8-row x 16-byte core matrices, rows 16 B apart)
+            unsigned char* bb = slot + TC_WCHUNK;
+            const int8_t* src = xrow + s * 128;
+#pragma unroll
+            for (int lp = 0; lp < 4; lp++)
+#pragma unroll
+              for (int li = 0; li < 2; li++)
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                  const int nrow = 4 * p + q;
+                  cp_async4_tc(bb + lp * (KT_N * 32) + (nrow >> 3) * 256 + li * 128 + (nrow & 7) * 16 + q * 4,
+                               src + lp * 32 + li * 16 + q * 4);
+                }
+            cp_async16_tc(sxd, xsc + 4 * s);
+          }
+        } else {
+          if (p == 0) {  // tail block tb, half kc: 128 rows x 16 bytes at tb * 4096 + kc * 2048
+            mbar_expect_tx(&full_bar[k], ntail * 4096);
+            for (int tb = 0; tb < ntail; tb++)
+              for (int kc = 0; kc < 2; kc++)
+                tma_load_3d(slot + tb * 4096 + kc * 2048, &K.m.tail, nch * 128 + tb * 32 + kc * 16, r0, wz,
+                            &full_bar[k]);
+          }
+          if (xrow) {
+            unsigned char* bt = slot + TC_WCHUNK + KT_BMAIN;
+            for (int tb = 0; tb < ntail; tb++)
+#pragma unroll
+              for (int kc = 0; kc < 2; kc++)
+                cp_async16_tc(bt + tb * (KT_TOK * 32) + (p >> 3) * 256 + kc * 128 + (p & 7) * 16,
+                              xrow + nch * 128 + tb * 32 + kc * 16);
+            cp_async16_tc(sxd, xsc + 4 * s);
+          }
+        }
+      }
+      cp_commit_tc();
+      if (++s == nst) {
+        s = 0;
+        if (++u < nun) set_unit(u);
+      }
+      if (g - sig == PD - 1) {
+        cp_wait_tc<PD - 1>();
+        fence_async_smem();
+        mbar_arrive(&full_bar[sig % KT_SLOTS]);
+        sig++;
+      }
+    }
+    cp_wait_tc<0>();
+    fence_async_smem();
+    for (; sig < S; sig++) mbar_arrive(&full_bar[sig % KT_SLOTS]);
+  } else if (warp == KT_MMA_WARP) {
+    // =================== MMA thread ===================
+    if (lane == 0) {
+      constexpr uint32_t IDESC = tc_idesc(TC_M, KT_N), IDESC_T = tc_idesc(TC_M, KT_TOK);
+      int s = 0;
+      for (int g = 0; g < S && !failed(); g++) {
+        const int k = g % KT_SLOTS, b = g & 1;
+        if (!mbar_wait(&full_bar[k], (g / KT_SLOTS) & 1)) { give_up(); break; }
+        if (g >= 2 && !mbar_wait(&tempty_bar[b], ((g >> 1) - 1) & 1)) { give_up(); break; }
+        tc_fence_after();
+        unsigned char* slot = ring + (size_t)k * KT_SLOT_BYTES;
+        const uint32_t wa = smem_u32(slot), dt = tbase + b * (TC_COLS / 2);
+        if (s < nch) {
+          const uint32_t ba = smem_u32(slot + TC_WCHUNK);
+#pragma unroll
+          for (int lp = 0; lp < 4; lp++)  // the four lane pairs accumulate into the same block sums
+            tc_mma_acc(dt, tc_desc(wa + lp * 32, 16, 1024, 2), tc_desc(ba + lp * (KT_N * 32), 128, 256, 0), IDESC,
+                       lp > 0);
+        } else {
+          const uint32_t ba = smem_u32(slot + TC_WCHUNK + KT_BMAIN);
+          for (int tb = 0; tb < ntail; tb++)
+            tc_mma_acc(dt + tb * KT_TOK, tc_desc(wa + tb * 4096, 2048, 128, 0),
+                       tc_desc(ba + tb * (KT_TOK * 32), 128, 256, 0), IDESC_T, false);
+        }
+        tc_commit(&tfull_bar[b]);
+        tc_commit(&empty_bar[k]);
+        mma_last_s = g;
+        if (++s == nst) s = 0;
+      }
+    }
+    __syncwarp();
+  } else {
+    // =================== chain warps: row 32 (warp % 4) + lane, activation rows 16 (warp / 4) + 0..15
+    const int quad = warp & 3, grp = warp >> 2;
+    const uint32_t tw = tbase + ((uint32_t)(quad * 32) << 16);
+    int u1 = 0, s1 = 0;
+    const float* wsc = nullptr;
+    auto c_unit = [&](int ui) {
+      const int mat = g_mat[u_gi[ui]];
+      wsc = W.sc + (long long)(mat < 0 ? 0 : mat) * W.sc_mstride +
+            (long long)min(u_r0[ui] + quad * 32 + lane, rows - 1) * ss;
+    };
+    float4 sw4;
+    auto load_scales = [&]() {
+      sw4 = __ldg(reinterpret_cast<const float4*>(wsc + 4 * s1));
+      if (++s1 == nst) {
+        s1 = 0;
+        if (++u1 < nun) c_unit(u1);
+      }
+    };
+    c_unit(0);
+    load_scales();
+    float acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) acc[i] = 0.0f;
+    int u0 = 0, s0 = 0, fail = 0;
+    for (int g = 0; g < S; g++) {
+      const int b = g & 1, k = g % KT_SLOTS;
+      const float sw[4] = {sw4.x, sw4.y, sw4.z, sw4.w};
+      if (g + 1 < S) load_scales();
+      if (!fail) {
+        if (failed() || !mbar_wait(&tfull_bar[b], (g >> 1) & 1)) fail = 1;
+        fail = __any_sync(0xffffffffu, fail);
+        if (fail) give_up();
+      }
+      tc_fence_after();
+      if (!fail) {
+        // the rows' block scales, staged with the step's operands (the slot is refilled only after
+        // every chain warp released it on sxfree_bar)
+        const float4* sx = reinterpret_cast<const float4*>(ring + (size_t)k * KT_SLOT_BYTES + TC_WCHUNK + KT_BMAIN +
+                                                           KT_BTAIL) + grp * 16;
+        const uint32_t ta = tw + b * (TC_COLS / 2);
+        uint32_t v[16];
+        if (s0 < nch) {
+#pragma unroll
+          for (int j = 0; j < 4; j++) {  // rows 16 grp + 4 j .. + 3: columns (4 rows x 4 blocks)
+            tmem_ld16(ta + grp * 64 + j * 16, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+              const float4 x4 = sx[4 * j + r];
+              const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+              for (int q = 0; q < 4; q++)
+                acc[4 * j + r] = fadd(acc[4 * j + r], fmul(fmul(sw[q], xs[q]), tc_isum(v[4 * r + q])));
+            }
+          }
+        } else {
+#pragma unroll
+          for (int tb = 0; tb < 3; tb++)
+            if (tb < ntail) {
+              tmem_ld16(ta + tb * KT_TOK + grp * 16, v);
+              tmem_ld_wait();
+#pragma unroll
+              for (int r = 0; r < 16; r++) {
+                const float4 x4 = sx[r];
+                const float xq = tb == 0 ? x4.x : tb == 1 ? x4.y : x4.z;
+                acc[r] = fadd(acc[r], fmul(fmul(sw[tb], xq), tc_isum(v[r])));
+              }
+            }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&tempty_bar[b]);
+          mbar_arrive(&sxfree_bar[k]);
+        }
+      }
+      if (++s0 == nst) {
+        s0 = 0;
+        if (!fail) {
+          const int row = u_r0[u0] + quad * 32 + lane;
+          if (row < rows) {
+            const int gi = u_gi[u0];
+#pragma unroll
+            for (int r = 0; r < 16; r++) {
+              const int e = u_a0[u0] + grp * 16 + r;
+              if (e < g_count[gi]) {
+                const int idx = g_off[gi] + e;
+                const long long orow = a.o_idx ? (long long)a.o_idx[idx] : (long long)idx;
+                float* po = a.out + orow * a.ostride + row;
+                *po = a.mode == 1 ? fadd(*po, acc[r]) : acc[r];
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i++) acc[i] = 0.0f;
+        u0++;
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == KT_MMA_WARP * 32 && failed() && mma_last_s >= 0) {
+    const int last = mma_last_s;
+    mbar_wait(&tfull_bar[last & 1], (last >> 1) & 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == KT_MMA_WARP)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(TC_COLS));
+  if (failed() && tid == 0 && a.err) atomicExch(a.err, HG_ERR_TIMEOUT);
 }
 
 // act = silu(g) * u (model.rs:247-248, 304, 317; silu ops.rs:80-82) of every (token, slot) row,
@@ -584,6 +964,49 @@ __global__ void __launch_bounds__(256) k_swiglu_quant(const float* __restrict__ 
 static bool g_tc_ready[64];
 static int g_tc_sms[64];
 
+// cuTensorMapEncodeTiled, fetched through the runtime once (no link against the driver library)
+typedef CUresult (*TmapEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static TmapEncodeFn g_tmap_encode = nullptr;
+
+static bool tmap_init() {
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_tmap_encode = reinterpret_cast<TmapEncodeFn>(fn);
+  }
+  return g_tmap_encode != nullptr;
+}
+
+// the layout a tensor map can describe: 16-byte aligned base, rows and matrices 16-byte strided
+static bool tc_mappable(const Q8M& W, int count) {
+  const unsigned long long ms = count > 1 ? (unsigned long long)W.qs_mstride : (unsigned long long)W.rows * W.cols;
+  return W.qs && reinterpret_cast<uintptr_t>(W.qs) % 16 == 0 && W.cols % 16 == 0 && ms % 16 == 0;
+}
+
+// maps of a stack of `count` matrices (count 1: one matrix)
+static bool tc_maps(const Q8M& W, int count, TcMaps* m) {
+  if (!g_tmap_encode || !tc_mappable(W, count)) return false;
+  const cuuint64_t ms = count > 1 ? (cuuint64_t)W.qs_mstride : (cuuint64_t)W.rows * W.cols;
+  const cuuint64_t dims[3] = {(cuuint64_t)W.cols, (cuuint64_t)W.rows, (cuuint64_t)count};
+  const cuuint64_t strides[2] = {(cuuint64_t)W.cols, ms};
+  const cuuint32_t box_main[3] = {128, TC_M, 1}, box_tail[3] = {16, TC_M, 1}, es[3] = {1, 1, 1};
+  *m = TcMaps{};
+  if (W.cols >= 128 &&
+      g_tmap_encode(&m->main, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(W.qs), dims, strides, box_main,
+                    es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  return g_tmap_encode(&m->tail, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(W.qs), dims, strides, box_tail,
+                       es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int OUT>
 static cudaError_t prepare_tc_t() {
   return cudaFuncSetAttribute((const void*)k_tc<OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM);
@@ -596,7 +1019,11 @@ cudaError_t prepare_tc() {
   if ((e = prepare_tc_t<TC_OUT_STORE>()) != cudaSuccess) return e;
   if ((e = prepare_tc_t<TC_OUT_RESID>()) != cudaSuccess) return e;
   if ((e = prepare_tc_t<TC_OUT_LMHEAD>()) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute((const void*)kp_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)KT_SMEM)) !=
+      cudaSuccess)
+    return e;
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+  if (!tmap_init()) return cudaSuccess;  // no tensor-map encoder: the dp4a kernels serve every step
   if (dev >= 0 && dev < 64) {
     g_tc_sms[dev] = sms;
     g_tc_ready[dev] = true;
@@ -612,7 +1039,8 @@ static bool tc_ready_here(int* sms) {
 }
 
 bool tc_usable(const Q8M& W, int T) {
-  return tc_ready_here(nullptr) && T >= TC_MIN_T && W.cols % 128 == 0 && W.cols >= 128 && W.ss % 4 == 0;
+  return tc_ready_here(nullptr) && T >= TC_MIN_T && W.cols % 128 == 0 && W.cols >= 128 && W.ss % 4 == 0 &&
+         tc_mappable(W, 1);
 }
 
 // CTAs of a launch of at most `units` units: one per SM (the runs balance the work), more when a
@@ -642,11 +1070,12 @@ static void tc_launch(int out, const TcArgs& G, int nc, int T, cudaStream_t st) 
 
 // epi: 0 store (out[t * ostride + row]), 1 residual add into B.x, 2 lm_head (logits to out when
 // set, argmax keys into B.amax) -- the EPI codes of the dp4a kernels in decode.cu.
-void launch_mv_tc(const Dims& D, const DecodeBufs& B, const Q8M& W, const int8_t* aq, const float* as, float* out,
+bool launch_mv_tc(const Dims& D, const DecodeBufs& B, const Q8M& W, const int8_t* aq, const float* as, float* out,
                   int ostride, int epi, cudaStream_t st) {
   int sms = 148;
   tc_ready_here(&sms);
   TcArgs G{};
+  if (!tc_maps(W, 1, &G.m0)) return false;
   G.W0 = W;
   G.T = B.T;
   G.ne = 0;
@@ -666,23 +1095,32 @@ void launch_mv_tc(const Dims& D, const DecodeBufs& B, const Q8M& W, const int8_t
   const long long units = (long long)((W.rows + TC_M - 1) / TC_M) * ((B.T + TC_TOK - 1) / TC_TOK);
   const int out_mode = epi == 1 ? TC_OUT_RESID : epi == 2 ? TC_OUT_LMHEAD : TC_OUT_STORE;
   tc_launch(out_mode, G, tc_ctas(units, sms), B.T, st);
+  return true;
 }
 
 bool ffn_tc_usable(const Dims& D, const DecodeBufs& B, const LayerDev& L) {
-  return tc_ready_here(nullptr) && B.T >= TC_MIN_T && B.ubuf && B.qact && B.sact && D.d % 128 == 0 &&
-         (L.moe ? D.f : D.df) % 32 == 0 && (!L.moe || D.ne + 1 <= TC_MAX_GROUPS);
+  if (!(tc_ready_here(nullptr) && B.T >= TC_MIN_T && B.ubuf && B.qact && B.sact && D.d % 128 == 0 &&
+        (L.moe ? D.f : D.df) % 32 == 0 && (!L.moe || D.ne + 1 <= TC_MAX_GROUPS)))
+    return false;
+  const bool moe = L.moe != 0;
+  if (moe) {
+    if (!tc_mappable(L.gate, D.ne) || !tc_mappable(L.up, D.ne) || !tc_mappable(L.down, D.ne)) return false;
+    if (D.nsh > 0 && (!tc_mappable(L.sgate, 1) || !tc_mappable(L.sup, 1) || !tc_mappable(L.sdown, 1))) return false;
+    return true;
+  }
+  return tc_mappable(L.gate, 1) && tc_mappable(L.up, 1) && tc_mappable(L.down, 1);
 }
 
 // The FFN of one layer for a step of many tokens: gate and up on the tensor cores, SwiGLU and the
 // quantization of the activations, down on the tensor cores. Same results as launch_ffn.
-void launch_ffn_tc(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaStream_t st) {
+bool launch_ffn_tc(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaStream_t st) {
   int sms = 148;
   tc_ready_here(&sms);
   const bool moe = L.moe != 0;
   const int fd = moe ? D.f : D.df, bslot = moe ? D.k + 1 : 1;
   const int nrouted = moe ? std::min(D.ne, B.T * D.k) : 0;
   const bool shared = moe ? D.nsh > 0 : true;
-  if (!shared && nrouted == 0) return;
+  if (!shared && nrouted == 0) return true;
   // units per row tile: group 0's tiles and at most T * k / 8 + nrouted routed tiles (each active
   // expert's last tile may be partial)
   const long long tiles = (shared ? (B.T + TC_TOK - 1) / TC_TOK : 0) +
@@ -696,7 +1134,16 @@ void launch_ffn_tc(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaSt
   G.err = B.err;
   G.nrouted = nrouted;
   G.slot0 = moe ? D.k : 0;
-  auto up = [&](const Q8M& routed, const Q8M& grp0, float* out) {
+  // the maps of all three projections first: a failure leaves the step to the dp4a kernels
+  TcMaps mg0{}, mg1{}, mu0{}, mu1{}, md0{}, md1{};
+  if (shared && (!tc_maps(moe ? L.sgate : L.gate, 1, &mg0) || !tc_maps(moe ? L.sup : L.up, 1, &mu0) ||
+                 !tc_maps(moe ? L.sdown : L.down, 1, &md0)))
+    return false;
+  if (moe && (!tc_maps(L.gate, D.ne, &mg1) || !tc_maps(L.up, D.ne, &mu1) || !tc_maps(L.down, D.ne, &md1)))
+    return false;
+  auto up = [&](const Q8M& routed, const Q8M& grp0, const TcMaps& m0, const TcMaps& m1, float* out) {
+    G.m0 = m0;
+    G.m1 = m1;
     G.W = moe ? routed : Q8M{};
     G.W0 = shared ? grp0 : Q8M{};
     G.aq = B.qh;
@@ -707,8 +1154,8 @@ void launch_ffn_tc(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaSt
     G.ostride = fd;
     tc_launch(TC_OUT_STORE, G, tc_ctas(tiles * ((fd + TC_M - 1) / TC_M), sms), B.T, st);
   };
-  up(L.gate, moe ? L.sgate : L.gate, B.act);
-  up(L.up, moe ? L.sup : L.up, B.ubuf);
+  up(L.gate, moe ? L.sgate : L.gate, mg0, mg1, B.act);
+  up(L.up, moe ? L.sup : L.up, mu0, mu1, B.ubuf);
   const long long nrows = (long long)B.T * bslot, nblk = nrows * (fd >> 5);
   {
     cudaLaunchConfig_t c2{};
@@ -722,6 +1169,8 @@ void launch_ffn_tc(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaSt
     c2.numAttrs = B.T <= 64 ? 1 : 0;
     cudaLaunchKernelEx(&c2, k_swiglu_quant, (const float*)B.act, (const float*)B.ubuf, nrows, fd, B.qact, B.sact);
   }
+  G.m0 = md0;
+  G.m1 = md1;
   G.W = moe ? L.down : Q8M{};
   G.W0 = shared ? (moe ? L.sdown : L.down) : Q8M{};
   G.aq = B.qact;
@@ -731,6 +1180,25 @@ void launch_ffn_tc(const Dims& D, const DecodeBufs& B, const LayerDev& L, cudaSt
   G.out_nslot = D.k + 1;
   G.ostride = D.d;
   tc_launch(TC_OUT_STORE, G, tc_ctas(tiles * ((D.d + TC_M - 1) / TC_M), sms), B.T, st);
+  return true;
+}
+
+bool kp_tc_usable(const MmArgs& a, int nrows_max, int groups) {
+  return tc_ready_here(nullptr) && nrows_max >= TC_MIN_T && groups >= 1 && groups <= TC_MAX_GROUPS &&
+         a.W.cols % 32 == 0 && a.W.cols >= 32 && a.W.ss % 4 == 0;
+}
+
+// the stacked matrices a launch may index: the grp tables' (up to `groups`) or a.mat
+bool launch_kp_tc(const MmArgs& a, int nrows_max, int groups, int count, cudaStream_t st) {
+  int sms = 148;
+  tc_ready_here(&sms);
+  KtArgs K{};
+  if (!tc_maps(a.W, count, &K.m)) return false;
+  K.a = a;
+  K.ngroups = groups;
+  const long long units = (long long)((a.W.rows + TC_M - 1) / TC_M) * groups * ((nrows_max + KT_TOK - 1) / KT_TOK);
+  kp_tc<<<tc_ctas(units, sms), KT_THREADS, KT_SMEM, st>>>(K);
+  return true;
 }
 
 }  // namespace hg

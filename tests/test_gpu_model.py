@@ -30,7 +30,7 @@ def test_prefill_bitexact_config1(engine130, oracle130):
 
 
 def test_prefill_chunked_equals_whole(engine130):
-    ids = synth.prompt_ids(1300, 7)  # spans two 1024-row prefill chunks
+    ids = synth.prompt_ids(4400, 7)  # spans two 4096-row prefill chunks
     with engine130.new_cache() as a, engine130.new_cache() as b:
         whole = engine130.prefill(a, ids)
         engine130.prefill(b, ids[:300])
