@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--ep", action="store_true",
                     help="expert parallelism under torchrun: the routed experts split across the ranks, "
                          "(token, expert) rows exchanged with NCCL inside each step (config 5's variant)")
+    ap.add_argument("--prefill-case", action="store_true",
+                    help="time the prefill alone: --seqs prompts of --lo ids each (500M, one GPU)")
     ap.add_argument("--attn-case", action="store_true",
                     help="time the decode-attention op alone on a config-3-shaped case (one GPU); "
                          "--seqs/--lo/--hi/--pages/--layers shape it")
@@ -602,6 +604,32 @@ def run_attn_case(args):
                       "ms_per_call": round(best, 4), "kv_gb_per_s": round(kv_bytes / (best / 1e3) / 1e9, 1)}))
 
 
+def run_prefill_case(args):
+    """Model::prefill alone (the exact-order prefill kernels) on the 500M model: --seqs prompts of
+    --lo random ids each (seed 100 + i), one at a time, wall clock per prompt after a first prompt
+    that loads the kernels."""
+    import numpy as np
+
+    from hobbylm_b200 import Engine, synth
+
+    n, length = max(1, args.seqs), max(1, args.lo)
+    eng = Engine.load(synth.cached_model("500M", 0, context_length=CTX), device=0, max_batch=1,
+                      kv_pool_tokens=(n + 1) * (length + 64))
+    times = []
+    for i in range(n + 1):
+        c = eng.new_cache()
+        t0 = time.time()
+        lg = eng.prefill(c, synth.prompt_ids(length, 100 + i))
+        dt = time.time() - t0
+        if i > 0:
+            times.append(round(dt, 4))
+        assert np.isfinite(lg).all()
+        c.close()
+    eng.close()
+    print(json.dumps({"prefill_case": True, "prompts": n, "tokens": length, "s_per_prompt": times,
+                      "tok_s": round(length * n / sum(times), 1)}), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -610,6 +638,8 @@ def main():
         run_diffusion(args)
     elif args.attn_case:
         run_attn_case(args)
+    elif args.prefill_case:
+        run_prefill_case(args)
     elif args.bs1_only:
         from hobbylm_b200 import synth
 

@@ -19,17 +19,17 @@
 // a tail block's 8 lanes of 4 bytes side by side): one MMA per tail block with one column per
 // (entry, lane).
 //
-// Pipeline: one CTA per SM (512 threads) owns all 512 tensor-memory columns as two 256-column
-// buffers. A CTA walks a stream of steps (its entry tiles x the chunks of a row); in step g one
-// thread issues the MMAs of step g + 1 into the other buffer while all 16 warps run the f32
-// chains of step g out of tensor memory. Weight chunks stream through a 6-slot cp.async ring four
-// steps ahead; the activation words and the scales of the next steps are loaded into registers a
-// step ahead, so no global-memory latency sits between two steps.
+// Pipeline: one CTA per SM owns all 512 tensor-memory columns as two 256-column buffers and walks
+// a balanced run of units (a 128-row tile x 8 entries of one matrix; the steps of a unit are its
+// 128-byte chunks). Roles: two copy warps fill a 6-slot ring (the weight tile by one TMA copy with
+// the 128-byte swizzle, the activation words by 4-byte cp.async), one thread issues each step's
+// MMAs into the free buffer, and 16 chain warps read the partials back and run the f32 chains;
+// they hand off through mbarriers (slot full / empty, buffer full / empty), not CTA barriers.
 //
 // Safety: every wait on an mbarrier is bounded (TC_SPIN_LIMIT polls); on expiry the CTA records
-// HG_ERR_TIMEOUT in the step's error word, stops issuing, waits (bounded) for its last MMAs and
-// copies, and still frees its tensor memory. No TMA and no multicast are used; all copies read
-// this GPU's own memory.
+// HG_ERR_TIMEOUT in the step's error word, its roles stop waiting, it waits (bounded) for its last
+// MMAs and copies, and still frees its tensor memory. TMA loads carry no multicast and read only
+// this GPU's own memory; their x coordinates are multiples of 16 bytes.
 #include <cuda.h>  // CUtensorMap (the encoder is fetched through the runtime; no driver library link)
 
 #include <algorithm>
@@ -109,13 +109,6 @@ __device__ __forceinline__ void cp_async4_tc(void* dst, const void* src) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-// D (tensor memory) += A * B, kind::i8, one thread
-__device__ __forceinline__ void tc_mma(uint32_t dt, uint64_t ad, uint64_t bd, uint32_t idesc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(dt),
-      "l"(ad), "l"(bd), "r"(idesc), "r"(1));
-}
 // D (tensor memory) = A * B (+ D when acc), kind::i8, one thread
 __device__ __forceinline__ void tc_mma_acc(uint32_t dt, uint64_t ad, uint64_t bd, uint32_t idesc, bool acc) {
   asm volatile(
@@ -151,24 +144,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* v) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-// The same 32-bit value into 16 consecutive columns of this warp's 32 lanes.
-__device__ __forceinline__ void tmem_st16_same(uint32_t taddr, uint32_t x) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
-      "r"(x)
-      : "memory");
-}
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-// The accumulators start at TC_BIAS, the bit pattern of 1.5 * 2^23: the MMAs add the exact partial
-// p (|p| <= 4 * 128 * 128 < 2^22) in int32, so the result read back is the float 1.5 * 2^23 + p
-// (every integer in [2^23, 2^24) is representable), and subtracting 1.5 * 2^23 gives float(p)
-// exactly -- one full-rate add instead of an int-to-float conversion.
+// float(v) of an int32 |v| < 2^22 (a lane partial or a block sum), exactly: 1.5 * 2^23 added in
+// integer arithmetic makes the bit pattern of the float 1.5 * 2^23 + v (every integer in
+// [2^23, 2^24) is representable), and subtracting 1.5 * 2^23 as a float leaves v -- an integer add
+// and a full-rate float add instead of an int-to-float conversion.
 constexpr uint32_t TC_BIAS = 0x4B400000u;
 constexpr float TC_BIAS_F = 12582912.0f;
-__device__ __forceinline__ float tc_partial(uint32_t v) { return __fsub_rn(__uint_as_float(v), TC_BIAS_F); }
-// float(v) of an int32 |v| < 2^22 (a block sum): the bias added in integer arithmetic, then removed
-// as a float, exactly
 __device__ __forceinline__ float tc_isum(uint32_t v) { return __fsub_rn(__uint_as_float(v + TC_BIAS), TC_BIAS_F); }
 
 // Output of a finished row tile x entry tile.
@@ -315,13 +296,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc(const __grid_constant__ Tc
   const uint32_t tbase = tmem_base_s;
   const int quad = warp & 3, pr = (warp >> 2) & 3;
   const uint32_t tw = tbase + ((uint32_t)(quad * 32) << 16) + pr * 16;  // chain warps' columns
-  if (warp < TC_EPI_WARPS) {
-#pragma unroll
-    for (int b = 0; b < 2; b++)
-#pragma unroll
-      for (int lp = 0; lp < 4; lp++) tmem_st16_same(tw + b * TC_BUFCOLS + lp * TC_N, TC_BIAS);
-    tmem_st_wait();
-  }
   fence_async_smem();  // the zeroed expansions -> tensor-core reads
   tc_fence_before();
   __syncthreads();
@@ -430,13 +404,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc(const __grid_constant__ Tc
           for (int lp = 0; lp < 4; lp++) {
             const uint64_t ad = tc_desc(wa + lp * 32, 16, 1024, 2);              // 128-byte swizzled, K-major
             const uint64_t bd = tc_desc(ba + lp * (TC_TOK * 256), 128, 256, 0);  // no swizzle, K-major
-            tc_mma(dt + lp * TC_N, ad, bd, IDESC);
+            tc_mma_acc(dt + lp * TC_N, ad, bd, IDESC, false);  // every lane pair has its own columns
           }
         } else {
           const uint32_t ba = smem_u32(slot + TC_WCHUNK + TC_BCHUNK);
           for (int tb = 0; tb < ntail; tb++)
-            tc_mma(dt + tb * TC_N, tc_desc(wa + tb * 4096, 2048, 128, 0), tc_desc(ba + tb * (TC_TOK * 256), 128, 256, 0),
-                   IDESC);
+            tc_mma_acc(dt + tb * TC_N, tc_desc(wa + tb * 4096, 2048, 128, 0),
+                       tc_desc(ba + tb * (TC_TOK * 256), 128, 256, 0), IDESC, false);
         }
         tc_commit(&tfull_bar[b]);   // the chain warps may read buffer b
         tc_commit(&empty_bar[k]);   // the copy warps may refill slot k
@@ -503,8 +477,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc(const __grid_constant__ Tc
 #pragma unroll
               for (int li = 0; li < 2; li++) {
                 const int l = 2 * lp + li;
-                acc[0][l] = __fmaf_rn(sc0[q], tc_partial(v[2 * q + li]), acc[0][l]);
-                acc[1][l] = __fmaf_rn(sc1[q], tc_partial(v[8 + 2 * q + li]), acc[1][l]);
+                acc[0][l] = __fmaf_rn(sc0[q], tc_isum(v[2 * q + li]), acc[0][l]);
+                acc[1][l] = __fmaf_rn(sc1[q], tc_isum(v[8 + 2 * q + li]), acc[1][l]);
               }
           }
         } else {
@@ -516,15 +490,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc(const __grid_constant__ Tc
               tmem_ld_wait();
 #pragma unroll
               for (int l = 0; l < 8; l++) {
-                acc[0][l] = __fmaf_rn(sc0[tb], tc_partial(v[l]), acc[0][l]);
-                acc[1][l] = __fmaf_rn(sc1[tb], tc_partial(v[8 + l]), acc[1][l]);
+                acc[0][l] = __fmaf_rn(sc0[tb], tc_isum(v[l]), acc[0][l]);
+                acc[1][l] = __fmaf_rn(sc1[tb], tc_isum(v[8 + l]), acc[1][l]);
               }
             }
         }
-        // back to the bias for the MMAs of step g + 2, then hand the buffer back
-#pragma unroll
-        for (int lp = 0; lp < 4; lp++) tmem_st16_same(ta + lp * TC_N, TC_BIAS);
-        tmem_st_wait();
+        // hand the buffer back to the MMAs of step g + 2
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty_bar[b]);
