@@ -231,7 +231,7 @@ constexpr int KP_KTILES = 8;   // tiles per CTA
 template <int HD>
 constexpr int kp_row_stride() { return HD + (HD / 32 == 4 ? 4 : 2); }
 template <int HD>
-constexpr size_t kp_scores_smem() { return (size_t)(KP_SR + KP_SJ) * kp_row_stride<HD>() * sizeof(float); }
+constexpr size_t kp_scores_smem() { return (size_t)(KP_SR + 2 * KP_SJ) * kp_row_stride<HD>() * sizeof(float); }
 
 template <int NI> struct KpVec;
 template <> struct KpVec<4> {
@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(256) kp_scores(const float* q, int qd, int t0,
   __shared__ uint32_t mred[KP_SR];  // this CTA's maxima of its rows (order-preserving keys)
   extern __shared__ __align__(16) float kp_sm[];
   float* qs = kp_sm;              // [KP_SR][RS]
-  float* ks = kp_sm + KP_SR * RS; // [KP_SJ][RS]
+  float* kbuf = kp_sm + KP_SR * RS;  // [2][KP_SJ][RS]: the tile being scored and the next one
   const int g = blockIdx.z;
   const int R0 = blockIdx.x * KP_SR, jt0 = blockIdx.y * KP_KTILES * KP_SJ;
   const int Rl = min(R0 + KP_SR - 1, nR - 1);
@@ -287,17 +287,38 @@ __global__ void __launch_bounds__(256) kp_scores(const float* q, int qd, int t0,
   const float* qa1 = qs + (lane + 32) * RS;
   if (tid < KP_SR) mred[tid] = 0u;  // ordered before use by the first tile's barrier
   float mx[2] = {-INFINITY, -INFINITY};
-  for (int kt = 0; kt < KP_KTILES; kt++) {
-    const int j0 = jt0 + kt * KP_SJ;
-    if (j0 >= lim_hi) break;  // CTA-uniform
-    __syncthreads();          // the previous tile's keys are no longer read
-    for (int i = tid; i < KP_SJ * HD; i += 256) {
-      const int jj = i / HD, e = i - jj * HD, j = j0 + jj;
-      float v = 0.0f;
-      if (j < lim_hi)
-        v = k_pool[(long long)bt[j / PAGE] * page_stride + ((long long)g * PAGE + (j % PAGE)) * HD + e];
-      ks[jj * RS + perm(e)] = v;
+  // K tiles: thread tid holds 16-byte pieces c = tid + 256 i of the next tile in registers while
+  // the current one is scored (piece c: position c / (HD / 4), elements 4 (c % (HD / 4)) .. + 3)
+  constexpr int KQ = KP_SJ * HD / 4 / 256;
+  float4 kr[KQ];
+  auto load_k = [&](int j0) {
+#pragma unroll
+    for (int i = 0; i < KQ; i++) {
+      const int c = tid + 256 * i, jj = c / (HD / 4), e4 = (c - jj * (HD / 4)) * 4, j = j0 + jj;
+      kr[i] = j < lim_hi ? *reinterpret_cast<const float4*>(k_pool + (long long)bt[j / PAGE] * page_stride +
+                                                            ((long long)g * PAGE + (j % PAGE)) * HD + e4)
+                         : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
+  };
+  auto store_k = [&](float* kb) {
+#pragma unroll
+    for (int i = 0; i < KQ; i++) {
+      const int c = tid + 256 * i, jj = c / (HD / 4), e4 = (c - jj * (HD / 4)) * 4;
+      float* row = kb + jj * RS;
+      row[perm(e4)] = kr[i].x;
+      row[perm(e4 + 1)] = kr[i].y;
+      row[perm(e4 + 2)] = kr[i].z;
+      row[perm(e4 + 3)] = kr[i].w;
+    }
+  };
+  int ntile = 0;
+  while (ntile < KP_KTILES && jt0 + ntile * KP_SJ < lim_hi) ntile++;
+  load_k(jt0);
+  for (int kt = 0; kt < ntile; kt++) {
+    const int j0 = jt0 + kt * KP_SJ;
+    float* ks = kbuf + (kt & 1) * KP_SJ * RS;
+    store_k(ks);  // buffer kt % 2 was last read by tile kt - 2, before the previous barrier
+    if (kt + 1 < ntile) load_k(j0 + KP_SJ);
     __syncthreads();
     // pairs (row lane + 32 r, position j0 + 4 warp + p)
     float A[2][4], Bt[2][4], Dt[2][4];
