@@ -469,16 +469,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc(const __grid_constant__ Tc
         if (s0 < nch) {
           // column e*8 + 2q + li of lane pair lp: entry 2pr + e, block 4c + q, lane 2lp + li
 #pragma unroll
-          for (int lp = 0; lp < 4; lp++) {
-            tmem_ld16(ta + lp * TC_N, v);
+          for (int h = 0; h < 2; h++) {  // two lane pairs per tensor-memory round trip
+            uint32_t w[16];
+            tmem_ld16(ta + (2 * h) * TC_N, v);
+            tmem_ld16(ta + (2 * h + 1) * TC_N, w);
             tmem_ld_wait();
 #pragma unroll
             for (int q = 0; q < 4; q++)
 #pragma unroll
               for (int li = 0; li < 2; li++) {
-                const int l = 2 * lp + li;
+                const int l = 4 * h + li, l2 = 4 * h + 2 + li;  // lanes of pairs 2h and 2h + 1
                 acc[0][l] = __fmaf_rn(sc0[q], tc_isum(v[2 * q + li]), acc[0][l]);
                 acc[1][l] = __fmaf_rn(sc1[q], tc_isum(v[8 + 2 * q + li]), acc[1][l]);
+                acc[0][l2] = __fmaf_rn(sc0[q], tc_isum(w[2 * q + li]), acc[0][l2]);
+                acc[1][l2] = __fmaf_rn(sc1[q], tc_isum(w[8 + 2 * q + li]), acc[1][l2]);
               }
           }
         } else {
