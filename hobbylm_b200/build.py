@@ -19,7 +19,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libhobbygpu.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["engine.cu", "decode.cu", "tc.cu", "ep.cu", "prefill.cu", "noalloc.cu", "gguf.cpp", "sampler.cpp"]
+SOURCES = ["engine.cu", "decode.cu", "tc.cu", "ep.cu", "prefill.cu", "sample.cu", "noalloc.cu", "gguf.cpp", "sampler.cpp"]
 HEADERS = ["hg_device.cuh", "hg_model.cuh", "hg_launch.h", "hg_host.h", "hg_ep.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

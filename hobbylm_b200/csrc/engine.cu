@@ -98,6 +98,8 @@ struct hg_engine {
   int32_t* h_meta = nullptr;   // pinned
   unsigned long long* h_amax = nullptr;  // pinned [max_batch]
   int32_t* h_err = nullptr;    // pinned
+  void* smp = nullptr;          // device sampling scratch (sample.cu), allocated by the first sampled generate
+  uint32_t* h_smp = nullptr;    // pinned: the sampled id
   std::map<int, cudaGraphExec_t> graphs;
   std::map<int, int> graph_kernels;  // kernel nodes per step graph
   int32_t* d_gen = nullptr;          // [GEN_CAP][max_batch] generated ids ring
@@ -420,6 +422,8 @@ void free_engine(hg_engine* e) {
   if (e->h_meta) cudaFreeHost(e->h_meta);
   if (e->h_amax) cudaFreeHost(e->h_amax);
   if (e->h_err) cudaFreeHost(e->h_err);
+  if (e->h_smp) cudaFreeHost(e->h_smp);
+  if (e->smp) cudaFree(e->smp);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
 }
@@ -867,9 +871,20 @@ int generate(hg_engine* e, const float* rows, int n_rows, const uint32_t* ids, i
   if (n + n_rows == 0) return 0;  // lib.rs:122-124
   std::unique_ptr<hg_seq, void (*)(hg_seq*)> s(seq_create(e, e->cfg.context_length), seq_free);
   const int V = e->cfg.vocab_size, valid = std::min(50257, V);
-  const bool host_path = o.temp > 0.0f || o.rep_penalty != 1.0f;
+  // sampled tokens (temperature, top-p, repetition penalty) are drawn on the GPU (sample.cu) from
+  // the step's logits in place; only vocabularies wider than the device sort use the host sampler
+  const bool sampled = o.temp > 0.0f || o.rep_penalty != 1.0f;
+  const bool dev_sample = sampled && sample_usable(V);
+  const bool host_path = sampled && !dev_sample;
   std::vector<float> logits(host_path ? V : 0);
   Rng rng(o.seed);
+  if (dev_sample) {
+    if (!e->smp) HG_CUDA(cudaMalloc(&e->smp, sample_scratch_bytes(V)));
+    if (!e->h_smp) HG_CUDA(cudaMallocHost((void**)&e->h_smp, 16));
+    unsigned long long state = 0;
+    sample_reset(e->smp, V, o.seed, e->stream, &state);
+    HG_CUDA(cudaStreamSynchronize(e->stream));
+  }
   uint32_t gpu_next = 0;
   if (n_rows > 0)
     prefill(e, s.get(), nullptr, rows, n_rows, n == 0 && host_path ? logits.data() : nullptr, &gpu_next);
@@ -878,7 +893,13 @@ int generate(hg_engine* e, const float* rows, int n_rows, const uint32_t* ids, i
   std::vector<uint32_t> out;
   for (int it = 0; it < o.max_new; it++) {
     uint32_t next;
-    if (host_path) {
+    if (dev_sample) {  // the last step's logits (row 0 of the step buffer) are still on the GPU
+      launch_sample(e->buf.logits, V, valid, o.temp, o.top_p, o.rep_penalty, e->smp, e->stream);
+      HG_CUDA(cudaGetLastError());
+      HG_CUDA(cudaMemcpyAsync(e->h_smp, sample_next_ptr(e->smp), 4, cudaMemcpyDeviceToHost, e->stream));
+      HG_CUDA(cudaStreamSynchronize(e->stream));
+      next = e->h_smp[0];
+    } else if (host_path) {
       for (int i = valid; i < V; i++) logits[i] = -INFINITY;
       if (o.rep_penalty != 1.0f)
         for (uint32_t t : out) {

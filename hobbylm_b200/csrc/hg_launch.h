@@ -45,6 +45,16 @@ bool kp_tc_usable(const MmArgs& a, int nrows_max, int groups);
 // count: matrices of the stack a.W the launch may index (tensor-map extent)
 bool launch_kp_tc(const MmArgs& a, int nrows_max, int groups, int count, cudaStream_t st);
 
+// sample.cu: Engine::generate's sampled tokens on the GPU (temperature, top-p, repetition penalty,
+// xorshift64*), bit-identical to the host sampler; the scratch keeps the history counts and the
+// RNG state between calls of one generate
+bool sample_usable(int V);
+size_t sample_scratch_bytes(int V);
+void sample_reset(void* scratch, int V, unsigned long long seed, cudaStream_t st, unsigned long long* h_state);
+void launch_sample(const float* logits, int V, int valid, float temp, float top_p, float rep_penalty, void* scratch,
+                   cudaStream_t st);
+uint32_t* sample_next_ptr(void* scratch);
+
 // prefill.cu
 void launch_kp_norm(float* in, const float* add, int rows, int d, const float* w, float eps, float* h_out, int8_t* q,
                     float* s, cudaStream_t st);

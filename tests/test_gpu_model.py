@@ -102,12 +102,15 @@ def test_generate_api_matches_oracle(engine130, oracle130):
     assert len(stop) == 1
 
 
-def test_sampling_matches_oracle(engine130, oracle130):
-    """temp/top-p sampling and the repetition penalty run on the host (sample.rs) over GPU logits."""
+@pytest.mark.parametrize("temp,top_p,rep", [(0.8, 0.9, 1.3), (1.0, 1.0, 1.0), (0.0, 0.9, 1.5), (0.7, 0.5, 1.0)])
+def test_sampling_matches_oracle(engine130, oracle130, temp, top_p, rep):
+    """Temperature / top-p sampling and the repetition penalty (sample.rs, lib.rs:125-142) drawn on
+    the GPU from the step's logits, with the RNG state on the device: the same ids as the oracle,
+    through the nucleus, the plain draw and the penalised argmax."""
     ids = synth.prompt_ids(32, 5)
-    o = GenOpts(max_new=24, temp=0.8, top_p=0.9, seed=77, rep_penalty=1.3)
+    o = GenOpts(max_new=24, temp=temp, top_p=top_p, seed=77, rep_penalty=rep)
     got = engine130.generate(ids, o)
-    ref, _, _, _ = oracle130.generate(ids, 24, temp=0.8, top_p=0.9, seed=77, rep_penalty=1.3)
+    ref, _, _, _ = oracle130.generate(ids, 24, temp=temp, top_p=top_p, seed=77, rep_penalty=rep)
     assert got == list(ref)
 
 
