@@ -177,7 +177,10 @@ int hg_debug_time_attention(hg_engine* e, hg_seq** seqs, int n, int iters, float
 
 /* Engine::generate (lib.rs:107-162) on token ids: prefill, then per step mask ids >= 50257,
  * sample (greedy when temp <= 0), stop on EOS, stream the id, stop at context_length.
- * out_ids (may be NULL) receives up to opts->max_new ids. Returns the count (>= 0) or an error. */
+ * The sample is drawn on the GPU from the step's logits (temperature, top-p, repetition penalty,
+ * the xorshift64* state of opts->seed kept on the device) with the same ids as sample.rs; only
+ * the id is read back per step. out_ids (may be NULL) receives up to opts->max_new ids. Returns
+ * the count (>= 0) or an error. */
 int hg_generate(hg_engine* e, const uint32_t* ids, int n, const hg_gen_opts* opts, hg_token_cb cb, void* user,
                 uint32_t* out_ids);
 /* Engine::generate (lib.rs:107-162) with `embeds`: n_embeds caller rows of d_model floats (host
