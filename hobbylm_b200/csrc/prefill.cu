@@ -391,7 +391,7 @@ __global__ void __launch_bounds__(256) kp_scores(const float* q, int qd, int t0,
 // and store is coalesced.
 __global__ void __launch_bounds__(32) kp_softmax_rows(float* S, long long s_head, int nR, int rep, int base, int t0,
                                                       int nfix, const uint32_t* mkey, float* inv) {
-  constexpr int U = 8;  // positions in flight per thread
+  constexpr int U = 16;  // positions in flight per thread
   const int g = blockIdx.y, R = blockIdx.x * 32 + threadIdx.x;
   if (R >= nR) return;
   float* Sg = S + (size_t)g * s_head + R;
